@@ -1,0 +1,328 @@
+"""Benchmark of the HFFN sparse FFN hot path on B200: one JSON line on rank 0.
+
+Default workload (``--workload fwd``): the Pythia-410M-shape synthetic HFFN layer of the benchmark plan, d_model 1024,
+d_ff 4096, 512-of-1024 supports per neuron (50 %), N = 4096 tokens per step, float32. A step is one forward of the
+layer over one batch: the up kernel (+ bias + GELU) then the down kernel, launched through the C ABI on inputs
+resident in HBM. ``--workload fwd_bf16`` runs the same in bfloat16 storage; ``--workload train`` the training step
+(d_model 2048, d_ff 8192, 80 %, N = 8192, MSE loss, fused backward + AdamW).
+
+Timing: W warm-up steps, then exactly K timed steps bracketed by a barrier and a device synchronisation; every step
+is timed with CUDA events on the launching stream and the L2 is flushed (a 512 MiB write) between steps, outside the
+events. Multi-GPU (torchrun, one process per GPU): each rank runs its own replica of the layer on its own batch
+(weak scaling, no collective on the data path); the time is the max over ranks.
+
+``--impl reference`` times the reference's own x86 AVX2 kernel (compiled from the reference sources into
+``oracle/_ref``) on this host's cores, on the same workload (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 512 << 20
+WORKLOADS = {
+    "fwd": {"case": "c2_1024_4096_k512", "n": 4096, "dtype": "fp32"},
+    "fwd_bf16": {"case": "c2_1024_4096_k512", "n": 4096, "dtype": "bf16"},
+    "train": {"case": "c3_2048_8192_k1638", "n": 8192, "dtype": "fp32"},
+}
+CLOCK_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+               "clocks_event_reasons.sw_power_cap")
+
+
+def peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def dist_env() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int) -> None:
+        self.index, self.proc, self.rows = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={CLOCK_QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is None:
+            return
+        time.sleep(0.15)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        loaded = [s for s in sm if s > 0.5 * max(sm)] if sm else []
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[k] for r in self.rows for k in range(4) if r[5 + k].lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def reference_arm(args, workload: dict) -> dict:
+    """The reference x86 kernel on this host's cores: each step a bounded sample of the workload's tokens."""
+    from hffn_b200 import synth
+    from oracle import x86ref
+    case = synth.CASES[workload["case"]]
+    unit = "tokens/s"
+    metric = f"HFFN FFN layer tokens/s ({'forward' if args.workload != 'train' else 'train step'}, {workload['dtype']})"
+    if args.workload != "fwd" or not x86ref.available():
+        why = "oracle/_ref not built" if not x86ref.available() else \
+            "the reference x86 kernel is float32 inference only; no CPU arm for this workload"
+        return {"impl": "reference", "unavailable": why, "metric": metric}
+    layer = synth.make_layer(case)
+    threads = len(os.sched_getaffinity(0))
+    kernel = x86ref.X86Kernel(layer, threads=threads)
+    sample = args.ref_tokens
+    x = synth.make_input(case, workload["n"])[:sample]
+    for _ in range(args.warmup):
+        kernel.forward(x)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        kernel.forward(x)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = sample * args.steps / total
+    return {"metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": workload["case"], "tokens_per_step": sample, "parallelism": f"{threads} host threads"},
+            "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "reference",
+                             "sample": f"{sample} of the {workload['n']} tokens per step, dual route, <=96-token chunks"},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def cpu_baseline(workload: dict, seconds: float) -> dict | None:
+    """The reference x86 kernel on a bounded sample of the workload (rank 0, N = 1)."""
+    from hffn_b200 import synth
+    from oracle import x86ref
+    if not x86ref.available() or workload["dtype"] != "fp32" or workload["case"] != "c2_1024_4096_k512":
+        return None
+    case = synth.CASES[workload["case"]]
+    threads = len(os.sched_getaffinity(0))
+    kernel = x86ref.X86Kernel(synth.make_layer(case), threads=threads)
+    x = synth.make_input(case, workload["n"])
+    chunk = 512
+    kernel.forward(x[:chunk])
+    tokens, start = 0, time.perf_counter()
+    while time.perf_counter() - start < seconds:
+        lo = tokens % workload["n"]
+        kernel.forward(x[lo:lo + chunk])
+        tokens += chunk
+    elapsed = time.perf_counter() - start
+    return {"value": tokens / elapsed, "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": f"{tokens} tokens in 512-token slices of the workload's batch, {elapsed:.1f} s"}
+
+
+def algorithmic(case, n: int, elem: int) -> dict:
+    """Algorithmic bytes and FLOPs of the two forward kernels per launch (minimal traffic of each kernel)."""
+    e_up = case.d_ff * case.up_degree
+    e_down = case.d_ff * case.down_degree
+    up_bytes = n * case.d_model * elem + e_up * (2 + elem) + case.d_ff * (elem + 4) + 4 + case.d_ff * n * elem
+    down_bytes = case.d_ff * n * elem + e_down * (2 + elem) + case.d_model * (elem + 4) + 4 + n * case.d_model * elem
+    return {"up": {"bytes": up_bytes, "flops": 2.0 * e_up * n}, "down": {"bytes": down_bytes, "flops": 2.0 * e_down * n}}
+
+
+def fp32_gemm_peak(torch) -> float:
+    """Measured FP32 CUDA-core GEMM throughput (cuBLAS SGEMM 8192^3, TF32 off, best of 5), TFLOP/s."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    a = torch.randn(8192, 8192, device="cuda")
+    b = torch.randn(8192, 8192, device="cuda")
+    c = a @ b
+    best = float("inf")
+    for _ in range(5):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        torch.mm(a, b, out=c)
+        end.record()
+        end.synchronize()
+        best = min(best, start.elapsed_time(end) / 1e3)
+    del a, b, c
+    return 2 * 8192 ** 3 / best / 1e12
+
+
+def gpu_arm(args, workload: dict) -> dict | None:
+    import torch
+    import torch.distributed as dist
+
+    from hffn_b200 import _native as native
+    from hffn_b200 import synth
+    from hffn_b200.runtime import HFFNLayer, HFFNRuntime
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    case = synth.CASES[workload["case"]]
+    n = workload["n"]
+    dtype = torch.float32 if workload["dtype"] == "fp32" else torch.bfloat16
+    layer = synth.make_layer(case)
+    t = torch.from_numpy
+    kl = HFFNLayer.from_hidden_major(layer.d_model, layer.d_ff, t(layer.b_up), t(layer.up_offsets), t(layer.up_idx),
+                                     t(layer.up_val), t(layer.b_down), t(layer.down_offsets), t(layer.down_idx),
+                                     t(layer.down_val))
+    runtime = HFFNRuntime([kl], device, dtype)
+    x_host = t(synth.make_input(case, n)).to(dtype).pin_memory()
+    x = x_host.to(device)
+    runtime.forward(0, x)
+    up, down = runtime.modes(n)
+    code, struct = runtime._code, runtime._structs[0]
+    stream = torch.cuda.current_stream(device)
+    handle = stream.cuda_stream
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=device)
+
+    def step():
+        native.check(native.lib.hffn_up(code, native.UP_CODES[up], x.data_ptr(), struct.up_offsets, struct.up_idx,
+                                        struct.up_val, struct.b_up, runtime._act.data_ptr(), None, case.d_model,
+                                        case.d_ff, n, handle), "hffn_up")
+        marks[1].record(stream)
+        native.check(native.lib.hffn_down(code, native.DOWN_CODES[down], runtime._act.data_ptr(), struct.out_offsets,
+                                          struct.out_hidden, struct.out_val, struct.b_down, runtime._y.data_ptr(),
+                                          case.d_model, case.d_ff, n, handle), "hffn_down")
+
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    for _ in range(args.warmup):
+        flush.zero_()
+        marks[0].record(stream)
+        step()
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        for k in range(args.steps):
+            flush.zero_()
+            marks = events[k]
+            marks[0].record(stream)
+            step()
+            marks[2].record(stream)
+        torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    up_ms = [e[0].elapsed_time(e[1]) for e in events]
+    down_ms = [e[1].elapsed_time(e[2]) for e in events]
+    step_ms = [e[0].elapsed_time(e[2]) for e in events]
+    total_s = sum(step_ms) / 1e3
+
+    # end to end through the public API: pinned host x -> device, forward, y -> pinned host, every step
+    y_host = torch.empty(n, case.d_model, dtype=dtype).pin_memory()
+    e2e_ms = []
+    for k in range(args.warmup + args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        x.copy_(x_host, non_blocking=True)
+        y = runtime.forward(0, x)
+        y_host.copy_(y, non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        if k >= args.warmup:
+            e2e_ms.append(a.elapsed_time(b))
+    e2e_s = sum(e2e_ms) / 1e3
+
+    times = torch.tensor([total_s, e2e_s], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    total_s, e2e_s = float(times[0]), float(times[1])
+    pk, pk_source = peaks()
+    fp32_peak = fp32_gemm_peak(torch) if rank == 0 else None
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    elem = 4 if dtype == torch.float32 else 2
+    alg = algorithmic(case, n, elem)
+    kernel_ms = {"up": statistics.mean(up_ms), "down": statistics.mean(down_ms)}
+    top = max(kernel_ms, key=kernel_ms.get)
+    achieved_gbs = alg[top]["bytes"] / (kernel_ms[top] / 1e3) / 1e9
+    achieved_tflops = alg[top]["flops"] / (kernel_ms[top] / 1e3) / 1e12
+    tokens = n * world * args.steps
+    line = {
+        "metric": f"HFFN FFN layer tokens/s (forward, {workload['dtype']})",
+        "value": tokens / total_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total_s / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if elem == 4 else "bf16", "data": "synthetic",
+        "config": {"workload": f"{case.name}: d_model {case.d_model}, d_ff {case.d_ff}, support {case.up_degree}, "
+                               f"N {n} tokens per GPU per step", "modes": [up, down],
+                   "parallelism": "replicas" if world > 1 else "single", "l2": "flushed between steps (512 MiB write)"},
+        "roofline": {"bound": "hbm", "kernel": f"{top}_{up if top == 'up' else down}",
+                     "achieved": achieved_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved_gbs / pk["hbm_gbs"], "traffic": None,
+                     "algorithmic_bytes": alg[top]["bytes"], "launch_ms": kernel_ms[top], "peak_source": pk_source},
+        "compute_roofline": {"bound": "fp32_cuda_cores", "achieved": achieved_tflops, "unit": "TFLOP/s",
+                             "peak": fp32_peak, "frac": achieved_tflops / fp32_peak if fp32_peak else None,
+                             "peak_source": "cuBLAS SGEMM 8192^3 TF32 off, measured in this run",
+                             "algorithmic_flops": alg[top]["flops"]},
+        "kernels_ms": kernel_ms,
+        "e2e": {"value": tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": x_host.numel() * elem,
+                "d2h_bytes_per_step": y_host.numel() * elem},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(workload, args.cpu_seconds)
+    return line
+
+
+def main() -> int:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=("hffn", "reference"), default="hffn")
+    parser.add_argument("--workload", choices=tuple(WORKLOADS), default="fwd")
+    parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--ref-tokens", type=int, default=512)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    workload = WORKLOADS[args.workload]
+    rank, world, _ = dist_env()
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        print(json.dumps(reference_arm(args, workload)), flush=True)
+        return 0
+    line = gpu_arm(args, workload)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

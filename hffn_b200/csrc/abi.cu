@@ -1,0 +1,180 @@
+// The extern "C" entries of libhffn_b200.so (declared in include/hffn_b200.h): argument checks, device binding and
+// dispatch to the kernels. Nothing here allocates device memory or synchronises the host.
+#include <cstring>
+
+#include "common.cuh"
+
+namespace hffn {
+
+int launch_up(int dtype, int mode, const void* x, const int32_t* off, const int16_t* idx, const void* w,
+              const void* b, void* act, float* z, int d, int H, int64_t n, cudaStream_t s);
+int launch_down(int dtype, int mode, const void* act, const int32_t* off, const int16_t* hid, const void* v,
+                const void* bias, void* y, int d, int H, int64_t n, cudaStream_t s);
+int64_t max_staged_rows();
+int64_t backward_workspace(const hffn_layer* L, int64_t n);
+int launch_backward(const hffn_layer* L, const hffn_supports* S, const float* x, const float* gy, const float* z,
+                    const float* act, float* gz, float* gx, const hffn_train_params* P, const hffn_adamw_step* opt,
+                    float* work, int64_t n, cudaStream_t s);
+int launch_adamw(const hffn_param* P, const hffn_adamw_step* step, cudaStream_t s);
+int launch_mse(const float* y, const float* target, float* gy, float* loss, int64_t n, int d, float* work,
+               cudaStream_t s);
+int launch_validate(const hffn_layer* L, int32_t* flag, cudaStream_t s);
+
+static thread_local char g_error[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list args;
+  va_start(args, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, args);
+  va_end(args);
+}
+
+const char* last_error() { return g_error; }
+
+// Token counts: every kernel indexes tokens with 32-bit ints and act with 64-bit offsets.
+constexpr int64_t kMaxTokens = int64_t(1) << 30;
+constexpr int kCoopMaxTokens = 8;
+
+static int check_shape(int dtype, int32_t d, int32_t H, int64_t n) {
+  HFFN_REQUIRE(dtype == HFFN_F32 || dtype == HFFN_BF16, "unknown dtype %d", dtype);
+  HFFN_REQUIRE(d >= 1 && d <= 32767 && H >= 1 && H <= 32767, "d_model %d / d_ff %d out of range [1, 32767]", d, H);
+  HFFN_REQUIRE(n >= 1 && n <= kMaxTokens, "token count %lld out of range", (long long)n);
+  return HFFN_OK;
+}
+
+static int resolve_up(int mode, int64_t n, int32_t d) {
+  if (mode == HFFN_MODE_AUTO) return hffn_up_mode(n, d);
+  return mode;
+}
+
+static int resolve_down(int mode, int64_t n, int32_t H) {
+  if (mode == HFFN_MODE_AUTO) return hffn_down_mode(n, H);
+  return mode;
+}
+
+static int check_layer(const hffn_layer* L) {
+  HFFN_REQUIRE(L != nullptr, "null layer");
+  HFFN_REQUIRE(L->b_up && L->up_offsets && L->up_idx && L->up_val && L->b_down && L->out_offsets && L->out_hidden &&
+                   L->out_val,
+               "null layer array");
+  HFFN_REQUIRE(L->nnz_up >= 0 && L->nnz_down >= 0 && L->nnz_up < (int64_t(1) << 31) &&
+                   L->nnz_down < (int64_t(1) << 31),
+               "edge counts out of the int32 offset range");
+  return HFFN_OK;
+}
+
+}  // namespace hffn
+
+using namespace hffn;
+
+extern "C" {
+
+const char* hffn_version(void) { return "hffn_b200 0.1 sm_100a"; }
+
+const char* hffn_last_error(void) { return last_error(); }
+
+int hffn_up_mode(int64_t n, int32_t d_model) {
+  (void)d_model;
+  return n <= kCoopMaxTokens ? HFFN_UP_COOP : HFFN_UP_TILE;
+}
+
+int hffn_down_mode(int64_t n, int32_t d_ff) {
+  (void)d_ff;
+  return n <= kCoopMaxTokens ? HFFN_DOWN_COOP : HFFN_DOWN_BLOCKED;
+}
+
+int hffn_up(int dtype, int mode, const void* x, const int32_t* up_offsets, const int16_t* up_idx, const void* up_val,
+            const void* b_up, void* act, float* z, int32_t d_model, int32_t d_ff, int64_t n, void* stream) {
+  HFFN_TRY(check_shape(dtype, d_model, d_ff, n));
+  HFFN_REQUIRE(x && up_offsets && up_idx && up_val && b_up && act, "null pointer argument");
+  HFFN_REQUIRE(z == nullptr || dtype == HFFN_F32, "z is stored by the float32 path only");
+  mode = resolve_up(mode, n, d_model);
+  HFFN_REQUIRE(mode == HFFN_UP_COOP || mode == HFFN_UP_LANE || mode == HFFN_UP_TILE, "unknown up mode %d", mode);
+  HFFN_REQUIRE(mode == HFFN_UP_COOP || d_model <= max_staged_rows(), "d_model %d exceeds the staged tile", d_model);
+  HFFN_TRY(bind_stream_device(stream));
+  return launch_up(dtype, mode, x, up_offsets, up_idx, up_val, b_up, act, z, d_model, d_ff, n,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int hffn_down(int dtype, int mode, const void* act, const int32_t* out_offsets, const int16_t* out_hidden,
+              const void* out_val, const void* b_down, void* y, int32_t d_model, int32_t d_ff, int64_t n,
+              void* stream) {
+  HFFN_TRY(check_shape(dtype, d_model, d_ff, n));
+  HFFN_REQUIRE(act && out_offsets && out_hidden && out_val && b_down && y, "null pointer argument");
+  mode = resolve_down(mode, n, d_ff);
+  HFFN_REQUIRE(mode == HFFN_DOWN_COOP || mode == HFFN_DOWN_TILED || mode == HFFN_DOWN_BLOCKED,
+               "unknown down mode %d", mode);
+  HFFN_REQUIRE(mode == HFFN_DOWN_COOP || d_ff <= max_staged_rows(), "d_ff %d exceeds the staged tile", d_ff);
+  HFFN_TRY(bind_stream_device(stream));
+  return launch_down(dtype, mode, act, out_offsets, out_hidden, out_val, b_down, y, d_model, d_ff, n,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int hffn_forward(int dtype, const hffn_layer* layer, const void* x, void* y, void* act, float* z, int64_t n,
+                 int up_mode, int down_mode, void* stream) {
+  HFFN_TRY(check_layer(layer));
+  HFFN_TRY(hffn_up(dtype, up_mode, x, layer->up_offsets, layer->up_idx, layer->up_val, layer->b_up, act, z,
+                   layer->d_model, layer->d_ff, n, stream));
+  return hffn_down(dtype, down_mode, act, layer->out_offsets, layer->out_hidden, layer->out_val, layer->b_down, y,
+                   layer->d_model, layer->d_ff, n, stream);
+}
+
+int64_t hffn_backward_workspace(const hffn_layer* layer, int64_t n) {
+  if (layer == nullptr || n < 1) return -1;
+  return backward_workspace(layer, n);
+}
+
+static int check_param(const hffn_param& p, int64_t count, bool need_grad, bool need_state, const char* name) {
+  HFFN_REQUIRE(p.count == count, "%s: count %lld, expected %lld", name, (long long)p.count, (long long)count);
+  HFFN_REQUIRE(!need_grad || p.grad, "%s: null gradient", name);
+  HFFN_REQUIRE(!need_state || (p.value && p.m && p.v), "%s: null value or moment", name);
+  return HFFN_OK;
+}
+
+int hffn_backward(const hffn_layer* layer, const hffn_supports* supports, const float* x, const float* gy,
+                  const float* z, const float* act, float* gz, float* gx, const hffn_train_params* params,
+                  const hffn_adamw_step* adamw, float* work, int64_t n, void* stream) {
+  HFFN_TRY(check_layer(layer));
+  HFFN_TRY(check_shape(HFFN_F32, layer->d_model, layer->d_ff, n));
+  HFFN_REQUIRE(supports && supports->in_offsets && supports->in_pos && supports->in_hidden && supports->hid_offsets &&
+                   supports->hid_pos && supports->hid_output,
+               "null support array");
+  HFFN_REQUIRE(x && gy && z && act && gz && gx && params && work, "null pointer argument");
+  HFFN_REQUIRE(layer->d_model <= max_staged_rows() && layer->d_ff <= max_staged_rows(), "shape exceeds the staged tile");
+  const bool fused = adamw != nullptr;
+  HFFN_TRY(check_param(params->up_val, layer->nnz_up, !fused, fused, "up_val"));
+  HFFN_TRY(check_param(params->b_up, layer->d_ff, !fused, fused, "b_up"));
+  HFFN_TRY(check_param(params->out_val, layer->nnz_down, !fused, fused, "out_val"));
+  HFFN_TRY(check_param(params->b_down, layer->d_model, !fused, fused, "b_down"));
+  HFFN_REQUIRE(!fused || (params->up_val.value == layer->up_val && params->b_up.value == layer->b_up &&
+                          params->out_val.value == layer->out_val && params->b_down.value == layer->b_down),
+               "fused AdamW: the parameter values must be the layer's arrays");
+  HFFN_TRY(bind_stream_device(stream));
+  return launch_backward(layer, supports, x, gy, z, act, gz, gx, params, adamw, work, n,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int hffn_adamw(const hffn_param* param, const hffn_adamw_step* step, void* stream) {
+  HFFN_REQUIRE(param && step, "null pointer argument");
+  HFFN_REQUIRE(param->count >= 0, "negative count");
+  HFFN_REQUIRE(param->count == 0 || (param->value && param->grad && param->m && param->v), "null array");
+  HFFN_TRY(bind_stream_device(stream));
+  return launch_adamw(param, step, static_cast<cudaStream_t>(stream));
+}
+
+int hffn_mse(const float* y, const float* target, float* gy, float* loss, int64_t n, int32_t d_model, float* work,
+             void* stream) {
+  HFFN_REQUIRE(y && target && gy && loss && work, "null pointer argument");
+  HFFN_REQUIRE(n >= 1 && d_model >= 1, "empty shape");
+  HFFN_TRY(bind_stream_device(stream));
+  return launch_mse(y, target, gy, loss, n, d_model, work, static_cast<cudaStream_t>(stream));
+}
+
+int hffn_validate_layout(const hffn_layer* layer, int32_t* flag, void* stream) {
+  HFFN_TRY(check_layer(layer));
+  HFFN_REQUIRE(flag != nullptr, "null flag");
+  HFFN_TRY(bind_stream_device(stream));
+  return launch_validate(layer, flag, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,181 @@
+"""HFFN forward runtime for a stack of FFNs of one shape, on B200: the drop-in of the reference's
+``runtime/gpu/nvidia/common/kernels/hffn_cuda/runtime.py`` (``HFFNLayer``, ``HFFNRuntime``, ``up_mode``, ``down_mode``,
+``UP_MODES``, ``DOWN_MODES``, ``MAX_TOKENS``).
+
+One call runs the whole block of N tokens of one FFN through ``hffn_forward`` of ``libhffn_b200.so``: the fused
+up + bias + GELU kernel, then the down kernel, on the caller's current CUDA stream (any ``cuda:i``, any stream; the
+reference accepts only cuda:0 and the default stream, ``runtime.py:79-82``). Model arrays are compact and stay on
+the device; the work buffers (``act`` hidden-major ``[d_ff, N]`` and ``y``) are shared by all layers, sized for the
+largest N seen and reused. The output is a view of the runtime's buffer, overwritten by the next call, as in the
+reference (``runtime.py:118-121``). Storage is float32 (the reference's only type) or bfloat16 (``dtype=``); the
+kernels accumulate in float32 in both.
+
+Errors follow the reference: ``ValueError`` for a bad shape, dtype, device, contiguity, token count or mode;
+``hffn_b200._native.NativeError`` (a RuntimeError) when CUDA fails.
+"""
+from __future__ import annotations
+
+from collections import Counter
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as native
+
+UP_MODES = ("coop", "lane", "tile")
+DOWN_MODES = ("coop", "tiled", "blocked")
+MAX_TOKENS = 1 << 24        # the kernels index tokens with 32-bit ints and act with 64-bit offsets
+BLOCK = 512                 # threads of the tiled kernels
+UP_TILE = 32                # largest token tile of the up kernel
+DOWN_TILE = 32              # largest token tile of the down kernel
+DTYPES = {torch.float32: native.F32, torch.bfloat16: native.BF16}
+
+
+def up_mode(n: int, d_model: int = 0) -> str:
+    """The up kernel the policy runs for N tokens (``hffn_up_mode``): coop for N <= 8, else tile."""
+    return UP_MODES[native.lib.hffn_up_mode(n, d_model)]
+
+
+def down_mode(n: int, d_ff: int = 0) -> str:
+    """The down kernel the policy runs for N tokens (``hffn_down_mode``): coop for N <= 8, else blocked."""
+    return DOWN_MODES[native.lib.hffn_down_mode(n, d_ff)]
+
+
+@dataclass(frozen=True)
+class HFFNLayer:
+    """The kernel arrays of one FFN: up slots per hidden neuron, down edges in output order (``runtime.py:41-53``)."""
+    d_model: int
+    d_ff: int
+    b_up: torch.Tensor         # [d_ff]
+    up_offsets: torch.Tensor   # int32[d_ff + 1]
+    up_idx: torch.Tensor       # int16[nnz_up], input feature of each slot
+    up_val: torch.Tensor       # [nnz_up]
+    b_down: torch.Tensor       # [d_model]
+    out_offsets: torch.Tensor  # int32[d_model + 1]
+    out_hidden: torch.Tensor   # int16[nnz_down], hidden neuron of each edge
+    out_val: torch.Tensor      # [nnz_down]
+
+    @classmethod
+    def from_hidden_major(cls, d_model: int, d_ff: int, b_up: torch.Tensor, up_offsets: torch.Tensor,
+                          up_idx: torch.Tensor, up_val: torch.Tensor, b_down: torch.Tensor, down_offsets: torch.Tensor,
+                          down_idx: torch.Tensor, down_val: torch.Tensor) -> "HFFNLayer":
+        """From the canonical hidden-major storage (neuron r owns ``[offsets[r], offsets[r + 1])`` on both sides).
+
+        The up arrays are kept as given; the down slots are put in output-major order by a stable sort of their
+        output feature, so that the edges of one output keep ascending neuron order, the order the reference fixes
+        (``runtime.py:55-67``); ``out_offsets`` counts the edges of each output."""
+        output = down_idx.long().cpu()
+        order = torch.argsort(output, stable=True)
+        out_offsets = torch.zeros(d_model + 1, dtype=torch.int32)
+        out_offsets[1:] = torch.cumsum(torch.bincount(output, minlength=d_model), 0)
+        owner = torch.repeat_interleave(torch.arange(d_ff), down_offsets.cpu().diff().long())
+        return cls(d_model, d_ff, b_up, up_offsets, up_idx, up_val, b_down, out_offsets,
+                   owner[order].to(torch.int16), down_val.cpu()[order].contiguous())
+
+    def model_bytes(self) -> int:
+        return sum(v.numel() * v.element_size() for v in vars(self).values() if isinstance(v, torch.Tensor))
+
+    def validate(self) -> None:
+        """Refuse offsets that do not cover their arrays or indices out of range (ValueError)."""
+        for side, offsets, index, values, count, bound in (
+                ("up", self.up_offsets, self.up_idx, self.up_val, self.d_ff, self.d_model),
+                ("down", self.out_offsets, self.out_hidden, self.out_val, self.d_model, self.d_ff)):
+            offsets, index = offsets.cpu(), index.cpu()
+            if offsets.dtype != torch.int32 or index.dtype != torch.int16:
+                raise ValueError(f"{side}: offsets must be int32 and indices int16")
+            if offsets.numel() != count + 1 or int(offsets[0]) != 0 or int(offsets[-1]) != values.numel() \
+                    or index.numel() != values.numel():
+                raise ValueError(f"{side}: offsets do not cover the compact arrays")
+            if bool((offsets.diff() < 0).any()):
+                raise ValueError(f"{side}: offsets decrease")
+            if index.numel() and (int(index.min()) < 0 or int(index.max()) >= bound):
+                raise ValueError(f"{side}: index out of range")
+        if self.b_up.numel() != self.d_ff or self.b_down.numel() != self.d_model:
+            raise ValueError("bias dimensions do not match d_model / d_ff")
+
+
+ARRAYS = ("b_up", "up_offsets", "up_idx", "up_val", "b_down", "out_offsets", "out_hidden", "out_val")
+VALUES = ("b_up", "up_val", "b_down", "out_val")
+
+
+def layer_struct(tensors: dict, d_model: int, d_ff: int) -> native.Layer:
+    """The ``hffn_layer`` of the device tensors of one layer (pointers only; the tensors own the memory)."""
+    return native.Layer(d_model, d_ff, tensors["up_val"].numel(), tensors["out_val"].numel(),
+                        *(tensors[name].data_ptr() for name in ARRAYS))
+
+
+class HFFNRuntime:
+    def __init__(self, layers: list[HFFNLayer], device: str | torch.device = "cuda",
+                 dtype: torch.dtype = torch.float32) -> None:
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("the HFFN runtime runs on a CUDA device")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        if dtype not in DTYPES:
+            raise ValueError("dtype must be torch.float32 or torch.bfloat16")
+        self.dtype, self._code = dtype, DTYPES[dtype]
+        self.layers = layers
+        self.d_model, self.d_ff = layers[0].d_model, layers[0].d_ff
+        if any((layer.d_model, layer.d_ff) != (self.d_model, self.d_ff) for layer in layers):
+            raise ValueError("all layers of a runtime share d_model and d_ff")
+        if self.d_model % 16:
+            raise ValueError("d_model must be a multiple of 16")
+        for layer in layers:
+            layer.validate()
+        # The device tensors own the memory; the structs hold their pointers for the native calls.
+        self._tensors = [{name: (getattr(layer, name).to(self.device, dtype) if name in VALUES
+                                 else getattr(layer, name).to(self.device)).contiguous() for name in ARRAYS}
+                         for layer in layers]
+        self._structs = [layer_struct(t, self.d_model, self.d_ff) for t in self._tensors]
+        self.forced_up: str | None = None
+        self.forced_down: str | None = None
+        self.calls: Counter = Counter()
+        self._tokens = 0
+        self._reserve(1)
+
+    def force(self, up: str | None, down: str | None) -> None:
+        """Diagnostic: fix the up and/or the down kernel regardless of N (None: the policy)."""
+        if up not in (None, *UP_MODES) or down not in (None, *DOWN_MODES):
+            raise ValueError("unknown kernel mode")
+        self.forced_up, self.forced_down = up, down
+
+    def _reserve(self, n: int) -> None:
+        self._tokens = n
+        self._act = torch.empty(self.d_ff * n, device=self.device, dtype=self.dtype)   # [d_ff, n]
+        self._y = torch.empty(n, self.d_model, device=self.device, dtype=self.dtype)
+
+    def workspace_bytes(self) -> int:
+        return self._act.element_size() * (self._act.numel() + self._y.numel())
+
+    def _check_input(self, x: torch.Tensor) -> int:
+        if x.dim() != 2 or x.shape[1] != self.d_model or x.dtype != self.dtype or x.device != self._y.device \
+                or not x.is_contiguous():
+            raise ValueError(f"expected a contiguous {self.dtype} [N, d_model] tensor on the runtime's device")
+        n = x.shape[0]
+        if not 1 <= n <= MAX_TOKENS:
+            raise ValueError("unsupported token count")
+        return n
+
+    def forward(self, index: int, x: torch.Tensor) -> torch.Tensor:
+        """y[N, d_model] of layer ``index`` for x[N, d_model]; a view of the runtime's output buffer."""
+        n = self._check_input(x)
+        if n > self._tokens:
+            self._reserve(n)
+        up, down = self._launch(index, x, n, None)
+        self.calls[up, down] += 1
+        return self._y[:n]
+
+    def modes(self, n: int) -> tuple[str, str]:
+        return self.forced_up or up_mode(n, self.d_model), self.forced_down or down_mode(n, self.d_ff)
+
+    def _launch(self, index: int, x: torch.Tensor, n: int, z: torch.Tensor | None) -> tuple[str, str]:
+        """Queue the up then the down kernel of layer ``index`` for the ``n`` tokens of ``x`` (validated, buffers
+        reserved); ``z`` (float32, >= d_ff * n entries) also receives the pre-activations. Returns the modes."""
+        up, down = self.modes(n)
+        status = native.lib.hffn_forward(self._code, self._structs[index], x.data_ptr(), self._y.data_ptr(),
+                                         self._act.data_ptr(), None if z is None else z.data_ptr(), n,
+                                         native.UP_CODES[up], native.DOWN_CODES[down],
+                                         native.stream_handle(self.device))
+        native.check(status, "hffn_forward")
+        return up, down

@@ -1,0 +1,238 @@
+"""HFFN training step on B200 over the forward runtime: the drop-in of the reference's
+``runtime/gpu/nvidia/ffn/training/train_runtime.py`` (``HFFNTrainRuntime``, ``transposed_supports``, ``PARAMETERS``,
+``SUPPORTS``).
+
+The wrapped ``HFFNRuntime`` keeps its compact arrays, its dispatch policy and its work buffers; the step reads and
+updates them in place. Added here, allocated at construction or by ``reserve(n)``:
+- compact, per layer: the gradients of ``up_val``, ``b_up``, ``out_val``, ``b_down`` and their two AdamW moments, each
+  of the length and order of its array (``out_val`` output-major); the two transposed supports as positions into the
+  runtime's arrays;
+- dense, shared by the layers, sized for the largest N reserved: ``z``, ``gz`` ``[d_ff, N]``, ``gx`` ``[N, d_model]``
+  and the float32 workspace of ``hffn_backward`` (the transposed x and gy, and the token-group partials of the
+  weight gradients, at most 16 groups whatever N).
+No dense ``W_up``, ``W_down``, gradient or moment exists. ``step`` runs the fused backward + AdamW of
+``hffn_backward``: each gradient entry is applied by AdamW in the kernel that completes it (and also stored, so that
+``gradients()`` reads the step's gradients, unless ``store_gradients=False``). ``backward`` + ``adamw`` are the
+reference's two separate phases. Nothing allocates once ``reserve(n)`` has run for the largest N.
+
+``backward(index, gy)`` uses the state of the last ``forward(index, x, z)`` with a ``z`` buffer and must follow it
+with no other forward of the runtime in between (checked, ``RuntimeError``), as in the reference.
+"""
+from __future__ import annotations
+
+import math
+from collections import Counter
+
+import torch
+
+from . import _native as native
+from .runtime import MAX_TOKENS, HFFNLayer, HFFNRuntime
+
+PARAMETERS = ("up_val", "b_up", "out_val", "b_down")
+SUPPORTS = ("in_offsets", "in_pos", "in_hidden", "hid_offsets", "hid_pos", "hid_output")
+PARTIAL_MAX_TOKENS = 2048
+
+
+def transposed_supports(layer: HFFNLayer) -> dict[str, torch.Tensor]:
+    """Up slots input-major and down edges hidden-major, as positions into the runtime's arrays (host, once).
+
+    Stable sorts, so the up slots of one input keep ascending neuron order and the down edges of one neuron ascending
+    output order: the summation orders of ``gx`` and ``gz`` (``train_runtime.py:39-56`` of the reference)."""
+    up_offsets, up_idx = layer.up_offsets.cpu().long(), layer.up_idx.cpu().long()
+    out_offsets, out_hidden = layer.out_offsets.cpu().long(), layer.out_hidden.cpu().long()
+    up_owner = torch.repeat_interleave(torch.arange(layer.d_ff), up_offsets.diff())
+    by_input = torch.argsort(up_idx, stable=True)
+    in_offsets = torch.zeros(layer.d_model + 1, dtype=torch.int32)
+    in_offsets[1:] = torch.cumsum(torch.bincount(up_idx, minlength=layer.d_model), 0)
+    out_owner = torch.repeat_interleave(torch.arange(layer.d_model), out_offsets.diff())
+    by_hidden = torch.argsort(out_hidden, stable=True)
+    hid_offsets = torch.zeros(layer.d_ff + 1, dtype=torch.int32)
+    hid_offsets[1:] = torch.cumsum(torch.bincount(out_hidden, minlength=layer.d_ff), 0)
+    return {"in_offsets": in_offsets, "in_pos": by_input.to(torch.int32),
+            "in_hidden": up_owner[by_input].to(torch.int16),
+            "hid_offsets": hid_offsets, "hid_pos": by_hidden.to(torch.int32),
+            "hid_output": out_owner[by_hidden].to(torch.int16)}
+
+
+def adamw_scalars(lr: float, betas: tuple[float, float], eps: float, weight_decay: float, k: int) -> native.AdamWStep:
+    """The step scalars of update k, in float64 on the host, passed as float32 (``train_runtime.py:195-207``)."""
+    beta1, beta2 = betas
+    return native.AdamWStep(lr * weight_decay, beta1, 1.0 - beta1, beta2, 1.0 - beta2, lr / (1.0 - beta1 ** k),
+                            math.sqrt(1.0 - beta2 ** k), eps)
+
+
+class HFFNTrainRuntime:
+    def __init__(self, runtime: HFFNRuntime, lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999),
+                 eps: float = 1e-8, weight_decay: float = 1e-2, max_tokens: int = PARTIAL_MAX_TOKENS,
+                 store_gradients: bool = True) -> None:
+        if runtime.dtype != torch.float32:
+            raise ValueError("training runs on a float32 runtime (float32 master weights)")
+        self.runtime = runtime
+        self.d_model, self.d_ff = runtime.d_model, runtime.d_ff
+        self.lr, self.betas, self.eps, self.weight_decay = lr, betas, eps, weight_decay
+        self.store_gradients = store_gradients
+        device = runtime.device
+        self._supports, self._grads, self._moments = [], [], []
+        self._support_structs, self._param_structs = [], []
+        for layer, params in zip(runtime.layers, runtime._tensors):
+            supports = {name: t.to(device) for name, t in transposed_supports(layer).items()}
+            grads = {name: torch.zeros_like(params[name]) for name in PARAMETERS}
+            moments = {name: (torch.zeros_like(params[name]), torch.zeros_like(params[name])) for name in PARAMETERS}
+            self._supports.append(supports)
+            self._grads.append(grads)
+            self._moments.append(moments)
+            self._support_structs.append(native.Supports(*(supports[name].data_ptr() for name in SUPPORTS)))
+            self._param_structs.append(native.TrainParams(*(
+                native.Param(params[name].data_ptr(), grads[name].data_ptr(), moments[name][0].data_ptr(),
+                             moments[name][1].data_ptr(), params[name].numel()) for name in PARAMETERS)))
+        self._fused_structs = [native.TrainParams(*(
+            native.Param(p.value, p.grad if store_gradients else None, p.m, p.v, p.count)
+            for p in (s.up_val, s.b_up, s.out_val, s.b_down))) for s in self._param_structs]
+        self.steps = [0] * len(runtime.layers)
+        self.calls: Counter = Counter()
+        self._saved: tuple | None = None
+        self._tokens = 0
+        self._work_tokens = 0
+        self.growths = 0
+        self.reserve(1)
+        self._reserve_partials(max_tokens)
+        self.growths = 0
+
+    # -- buffers -------------------------------------------------------------------------------------------------
+    def reserve(self, n: int) -> None:
+        """Size every dense buffer for N tokens; allocates only when N grows (call it with the largest N)."""
+        runtime = self.runtime
+        if n > runtime._tokens:
+            runtime._reserve(n)
+            self._saved = None
+            self.growths += 1
+        if n > self._tokens:
+            self._tokens = n
+            self.growths += 1
+            device = runtime.device
+            self._z = torch.empty(self.d_ff * n, device=device)
+            self._gz = torch.empty(self.d_ff * n, device=device)
+            self._gx = torch.empty(n, self.d_model, device=device)
+            self._gy = torch.empty(n, self.d_model, device=device)
+            self._loss = torch.zeros(1, device=device)
+            self._saved = None
+        self._reserve_partials(n)
+
+    def _reserve_partials(self, n: int) -> None:
+        """Size the backward workspace for N tokens (grows only with N)."""
+        if n <= self._work_tokens:
+            return
+        floats = max(int(native.lib.hffn_backward_workspace(s, n)) for s in self.runtime._structs)
+        floats = max(floats, 1024)
+        self._work_tokens = n
+        self.growths += 1
+        self._work = torch.empty(floats, device=self.runtime.device)
+
+    def _check_tokens(self, t: torch.Tensor, what: str) -> int:
+        if (t.dim() != 2 or t.shape[1] != self.d_model or t.dtype != torch.float32 or t.device != self.runtime._y.device
+                or not t.is_contiguous()):
+            raise ValueError(f"expected a contiguous float32 [N, d_model] tensor {what} on the runtime's device")
+        if not 1 <= t.shape[0] <= MAX_TOKENS:
+            raise ValueError("unsupported token count")
+        return t.shape[0]
+
+    # -- the step and its pieces ---------------------------------------------------------------------------------
+    def forward(self, index: int, x: torch.Tensor, z: torch.Tensor | None = None) -> torch.Tensor:
+        """y[N, d_model] of layer ``index`` (a view of the runtime's output). With ``z`` (contiguous float32, at
+        least d_ff * N entries): the same kernels also write ``z`` hidden-major and the state of the backward is kept."""
+        runtime = self.runtime
+        if z is None:
+            return runtime.forward(index, x)
+        n = self._check_tokens(x, "x")
+        if z.dtype != torch.float32 or z.device != runtime._y.device or not z.is_contiguous() or z.numel() < self.d_ff * n:
+            raise ValueError("z must be a contiguous float32 device tensor of at least d_ff * N entries")
+        self.reserve(n)
+        up, down = runtime._launch(index, x, n, z)
+        runtime.calls[up, down] += 1
+        self.calls[up, down] += 1
+        self._saved = (index, n, z, x, sum(runtime.calls.values()))
+        return runtime._y[:n]
+
+    def _backward(self, index: int, gy: torch.Tensor, fused: native.AdamWStep | None) -> torch.Tensor:
+        runtime = self.runtime
+        if self._saved is None or self._saved[0] != index or self._saved[4] != sum(runtime.calls.values()):
+            raise RuntimeError("backward must follow a forward of the same layer with a z buffer, with no forward in between")
+        _, n, z, x, _ = self._saved
+        if self._check_tokens(gy, "gy") != n:
+            raise ValueError("gy must have the N of the forward")
+        params = self._fused_structs[index] if fused is not None else self._param_structs[index]
+        status = native.lib.hffn_backward(runtime._structs[index], self._support_structs[index], x.data_ptr(),
+                                          gy.data_ptr(), z.data_ptr(), runtime._act.data_ptr(), self._gz.data_ptr(),
+                                          self._gx.data_ptr(), params, fused, self._work.data_ptr(), n,
+                                          native.stream_handle(runtime.device))
+        native.check(status, "hffn_backward")
+        return self._gx[:n]
+
+    def backward(self, index: int, gy: torch.Tensor) -> torch.Tensor:
+        """Compact gradients of layer ``index`` (see ``gradients``) and gx[N, d_model] (a view of the step's buffer)
+        for the upstream gradient gy[N, d_model] of the last forward with a ``z`` buffer."""
+        return self._backward(index, gy, None)
+
+    def _next_step(self, index: int) -> native.AdamWStep:
+        self.steps[index] += 1
+        return adamw_scalars(self.lr, self.betas, self.eps, self.weight_decay, self.steps[index])
+
+    def adamw(self, index: int) -> None:
+        """One AdamW update of the four compact arrays of layer ``index`` from the gradients of the last backward."""
+        scalars = self._next_step(index)
+        stream = native.stream_handle(self.runtime.device)
+        params = self._param_structs[index]
+        for name in PARAMETERS:
+            native.check(native.lib.hffn_adamw(getattr(params, name), scalars, stream), "hffn_adamw")
+
+    def step(self, index: int, x: torch.Tensor, gy: torch.Tensor) -> torch.Tensor:
+        """Forward (z stored in the step's buffer), then the fused backward + AdamW. Returns gx (a view)."""
+        self.forward(index, x, self._z)
+        return self._backward(index, gy, self._next_step(index))
+
+    def step_mse(self, index: int, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+        """One step on the MSE loss ``mean((y - target)^2)``: forward, loss and its gradient
+        ``gy = 2 (y - target) / (N d_model)``, fused backward + AdamW. Returns the loss (a 1-element device view,
+        the loss of the parameters before the update)."""
+        n = self._check_tokens(target, "target")
+        y = self.forward(index, x, self._z)
+        if n != y.shape[0]:
+            raise ValueError("target must have the N of x")
+        gy = self._gy[:n]
+        native.check(native.lib.hffn_mse(y.data_ptr(), target.data_ptr(), gy.data_ptr(), self._loss.data_ptr(), n,
+                                         self.d_model, self._work.data_ptr(), native.stream_handle(self.runtime.device)),
+                     "hffn_mse")
+        self._backward(index, gy, self._next_step(index))
+        return self._loss
+
+    # -- read access for the checks (views, no copy) -------------------------------------------------------------
+    def parameters(self, index: int) -> dict[str, torch.Tensor]:
+        return {name: self.runtime._tensors[index][name] for name in PARAMETERS}
+
+    def gradients(self, index: int) -> dict[str, torch.Tensor]:
+        """Keyed by parameter: ``up_val`` hidden-major slot order, ``out_val`` output-major edge order."""
+        return self._grads[index]
+
+    def moments(self, index: int) -> dict[str, tuple[torch.Tensor, torch.Tensor]]:
+        return self._moments[index]
+
+    def supports(self, index: int) -> dict[str, torch.Tensor]:
+        return self._supports[index]
+
+    def activations(self, n: int) -> dict[str, torch.Tensor]:
+        """z, h, gz hidden-major [d_ff, N] and gx [N, d_model] of the last step on N tokens."""
+        return {"z": self._z[:self.d_ff * n].view(self.d_ff, n),
+                "h": self.runtime._act[:self.d_ff * n].view(self.d_ff, n),
+                "gz": self._gz[:self.d_ff * n].view(self.d_ff, n), "gx": self._gx[:n]}
+
+    def nbytes(self, index: int) -> dict[str, int]:
+        def size(tensors) -> int:
+            return sum(t.numel() * t.element_size() for t in tensors)
+        params = self.runtime._tensors[index]
+        return {"values": size(params[name] for name in PARAMETERS),
+                "gradients": size(self._grads[index].values()),
+                "moments": size(t for pair in self._moments[index].values() for t in pair),
+                "indices": size(params[name] for name in ("up_offsets", "up_idx", "out_offsets", "out_hidden"))
+                + size(self._supports[index].values()),
+                "workspace": self.runtime.workspace_bytes() + size((self._z, self._gz, self._gx, self._gy)),
+                "partials": size((self._work,))}

@@ -1,0 +1,146 @@
+/* HFFN fixed-support sparse FFN on B200 (sm_100a): the C ABI of libhffn_b200.so.
+ *
+ * One layer is y = W_down gelu(W_up x + b_up) + b_down stored per hidden neuron (compact supports, int16 indices,
+ * int32 offsets, float32 or bfloat16 values). No dense weight, mask, gradient or moment exists behind this ABI.
+ *
+ * Conventions of every entry:
+ *  - arguments are raw device pointers, sizes and a cudaStream_t passed as void* (NULL: the legacy default stream);
+ *  - the device of `stream` is made current for the call; launches are queued on `stream` and the host is never
+ *    synchronised; nothing is allocated: the caller passes every buffer, workspaces included;
+ *  - the return value is a status (HFFN_OK = 0); hffn_last_error() gives the message of the calling thread's last
+ *    failure. Argument errors are detected before any launch.
+ * Layouts: x, y, gy, gx token-major [n, d_model]; the hidden activations act (h), z and gz hidden-major [d_ff, n]
+ * (element r * n + t), as the reference runtime holds them (runtime/gpu/nvidia/ffn/training/kernels_train.py:9-11).
+ */
+#ifndef HFFN_B200_H
+#define HFFN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define HFFN_OK 0
+#define HFFN_ERR_ARGUMENT 1    /* bad shape, pointer, mode or range: nothing was launched */
+#define HFFN_ERR_CUDA 2        /* a CUDA call or launch failed */
+#define HFFN_ERR_LAYOUT 3      /* hffn_validate_layout found an invalid offset or index */
+
+/* Storage types of x, the values, the biases, act and y (arithmetic is float32 in both). */
+#define HFFN_F32 0
+#define HFFN_BF16 1
+
+/* Kernel modes, the names of the reference runtime (runtime/gpu/nvidia/common/kernels/hffn_cuda/runtime.py:22-38).
+ * up:   coop = warp per neuron reducing its slots over the lanes, for tiny n;
+ *       lane = token tile of 16 per neuron, x staged in shared memory;   tile = token tile of 32 per neuron.
+ * down: coop = warp per output reducing its edges over the lanes, for tiny n;
+ *       tiled = output owner over a 4-token tile of act staged in shared memory; blocked = 8-token tile.
+ * AUTO picks by n and the shape (hffn_up_mode / hffn_down_mode). */
+#define HFFN_MODE_AUTO (-1)
+#define HFFN_UP_COOP 0
+#define HFFN_UP_LANE 1
+#define HFFN_UP_TILE 2
+#define HFFN_DOWN_COOP 0
+#define HFFN_DOWN_TILED 1
+#define HFFN_DOWN_BLOCKED 2
+
+/* The kernel arrays of one layer (HFFNLayer, runtime.py:41-53): up slots hidden-major, down edges output-major.
+ * Value pointers are float* or __nv_bfloat16* per the call's dtype. */
+typedef struct hffn_layer {
+  int32_t d_model, d_ff;
+  int64_t nnz_up, nnz_down;
+  const void* b_up;            /* [d_ff] */
+  const int32_t* up_offsets;   /* [d_ff + 1] */
+  const int16_t* up_idx;       /* [nnz_up] input feature of each slot */
+  const void* up_val;          /* [nnz_up] */
+  const void* b_down;          /* [d_model] */
+  const int32_t* out_offsets;  /* [d_model + 1] */
+  const int16_t* out_hidden;   /* [nnz_down] hidden neuron of each edge */
+  const void* out_val;         /* [nnz_down] */
+} hffn_layer;
+
+/* Transposed supports of the backward, positions into the arrays above (transposed_supports,
+ * runtime/gpu/nvidia/ffn/training/train_runtime.py:39-56). */
+typedef struct hffn_supports {
+  const int32_t* in_offsets;   /* [d_model + 1] */
+  const int32_t* in_pos;       /* [nnz_up] position of each slot in up_* (input-major, hidden ascending) */
+  const int16_t* in_hidden;    /* [nnz_up] */
+  const int32_t* hid_offsets;  /* [d_ff + 1] */
+  const int32_t* hid_pos;      /* [nnz_down] position of each edge in out_* (hidden-major, output ascending) */
+  const int16_t* hid_output;   /* [nnz_down] */
+} hffn_supports;
+
+/* One compact float32 parameter array with its gradient and AdamW moments, all of `count` entries. */
+typedef struct hffn_param {
+  float* value;
+  float* grad;   /* may be NULL in the fused backward + AdamW: the gradient is then never stored */
+  float* m;
+  float* v;
+  int64_t count;
+} hffn_param;
+
+typedef struct hffn_train_params {
+  hffn_param up_val, b_up, out_val, b_down;
+} hffn_train_params;
+
+/* The step scalars of one AdamW update, computed in float64 on the host and passed as float32
+ * (runtime/gpu/nvidia/ffn/training/train_runtime.py:195-207):
+ * lr_decay = lr * wd, step_size = lr / (1 - beta1^k), bias2_sqrt = sqrt(1 - beta2^k). */
+typedef struct hffn_adamw_step {
+  float lr_decay, beta1, one_minus_beta1, beta2, one_minus_beta2, step_size, bias2_sqrt, eps;
+} hffn_adamw_step;
+
+const char* hffn_version(void);
+const char* hffn_last_error(void);
+
+/* Policy of the reference runtime's up_mode / down_mode (runtime.py:29-38), on this build's kernels. */
+int hffn_up_mode(int64_t n, int32_t d_model);
+int hffn_down_mode(int64_t n, int32_t d_ff);
+
+/* Up projection + bias + exact GELU, optional float32 pre-activation store.
+ * Replaces the up_coop / up_lane / up_tile (and _z) kernels (runtime/gpu/nvidia/common/kernels/hffn_cuda/
+ * kernels.py:102-143). act[r * n + t] = gelu(z), z[r * n + t] = b[r] + sum_e w[e] x[t, idx[e]] if z != NULL. */
+int hffn_up(int dtype, int mode, const void* x, const int32_t* up_offsets, const int16_t* up_idx, const void* up_val,
+            const void* b_up, void* act, float* z, int32_t d_model, int32_t d_ff, int64_t n, void* stream);
+
+/* Down projection, output owners: y[t, o] = sum over the edges of o of out_val * act[hid, t] + b_down[o].
+ * Replaces down_coop / down_tiled / down_blocked (kernels.py:145-191). */
+int hffn_down(int dtype, int mode, const void* act, const int32_t* out_offsets, const int16_t* out_hidden,
+              const void* out_val, const void* b_down, void* y, int32_t d_model, int32_t d_ff, int64_t n, void* stream);
+
+/* Whole forward of one layer: up then down. Replaces HFFNRuntime._launch (runtime.py:134-163).
+ * act: [d_ff, n] workspace of the dtype; z: NULL or float32 [d_ff, n]. */
+int hffn_forward(int dtype, const hffn_layer* layer, const void* x, void* y, void* act, float* z, int64_t n,
+                 int up_mode, int down_mode, void* stream);
+
+/* Float32 entries of the workspace hffn_backward needs for n tokens. */
+int64_t hffn_backward_workspace(const hffn_layer* layer, int64_t n);
+
+/* Backward of the last forward (z, act of that forward), float32. Computes gz [d_ff, n], gx [n, d_model] and the
+ * four compact gradients. With adamw == NULL the gradients are written to params->*.grad (the reference's backward,
+ * runtime/gpu/nvidia/ffn/training/train_runtime.py:163-193). With adamw != NULL each gradient entry is applied by
+ * AdamW as soon as it is complete (the reference's backward followed by adamw, train_runtime.py:195-214) and stored
+ * only where params->*.grad != NULL. params->*.value must be the layer's up_val, b_up, out_val, b_down. */
+int hffn_backward(const hffn_layer* layer, const hffn_supports* supports, const float* x, const float* gy,
+                  const float* z, const float* act, float* gz, float* gx, const hffn_train_params* params,
+                  const hffn_adamw_step* adamw, float* work, int64_t n, void* stream);
+
+/* AdamW on one compact array from its stored gradient. Replaces the adamw kernel (kernels_train.py:246-258). */
+int hffn_adamw(const hffn_param* param, const hffn_adamw_step* step, void* stream);
+
+/* MSE loss of the training benchmark (no counterpart in the reference, whose step takes gy from the caller):
+ * gy = 2 (y - target) / (n d_model); *loss = mean((y - target)^2), float32 on the device. work: 1024 floats. */
+int hffn_mse(const float* y, const float* target, float* gy, float* loss, int64_t n, int32_t d_model, float* work,
+             void* stream);
+
+/* Device-side check of a layer's arrays (offsets from 0 to nnz, non-decreasing, indices in range): sets *flag
+ * (device int32, cleared by the call) to 1 if any array is invalid. The export reader's checks
+ * (runtime/common/pythia/hffn_pythia/export.py:37-45) on device-resident arrays. */
+int hffn_validate_layout(const hffn_layer* layer, int32_t* flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HFFN_B200_H */
