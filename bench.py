@@ -197,7 +197,9 @@ def gpu_arm(args, workload: dict) -> dict | None:
     kl = HFFNLayer.from_hidden_major(layer.d_model, layer.d_ff, t(layer.b_up), t(layer.up_offsets), t(layer.up_idx),
                                      t(layer.up_val), t(layer.b_down), t(layer.down_offsets), t(layer.down_idx),
                                      t(layer.down_val))
-    runtime = HFFNRuntime([kl], device, dtype)
+    runtime = HFFNRuntime([kl], device, dtype, tensor_cores=False if args.path == "cuda_cores" else None)
+    if args.path == "tensor_cores":
+        runtime.force("tc", "tc")
     x_host = t(synth.make_input(case, n)).to(dtype).pin_memory()
     x = x_host.to(device)
     runtime.forward(0, x)
@@ -206,8 +208,26 @@ def gpu_arm(args, workload: dict) -> dict | None:
     stream = torch.cuda.current_stream(device)
     handle = stream.cuda_stream
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=device)
+    tc = up == "tc"
+    if tc:
+        dense, work, err = runtime._dense[0], runtime._tc_work.data_ptr(), runtime._err.data_ptr()
+        ptr = lambda v: None if v is None else v.data_ptr()  # noqa: E731
+        if dtype == torch.float32:
+            x_split, act_hi = work, work + 2 * n * case.d_model * 4
+            act_lo = act_hi + n * case.d_ff * 4
+        else:
+            x_split, act_hi, act_lo = None, work, None
 
     def step():
+        if tc:
+            native.check(native.lib.hffn_up_tc(code, x.data_ptr(), ptr(dense["up_hi"]), ptr(dense["up_lo"]),
+                                               struct.b_up, act_hi, act_lo, None, x_split, err, case.d_model,
+                                               case.d_ff, n, handle), "hffn_up_tc")
+            marks[1].record(stream)
+            native.check(native.lib.hffn_down_tc(code, act_hi, act_lo, ptr(dense["down_hi"]), ptr(dense["down_lo"]),
+                                                 struct.b_down, runtime._y.data_ptr(), err, case.d_model, case.d_ff,
+                                                 n, handle), "hffn_down_tc")
+            return
         native.check(native.lib.hffn_up(code, native.UP_CODES[up], x.data_ptr(), struct.up_offsets, struct.up_idx,
                                         struct.up_val, struct.b_up, runtime._act.data_ptr(), None, case.d_model,
                                         case.d_ff, n, handle), "hffn_up")
@@ -270,9 +290,37 @@ def gpu_arm(args, workload: dict) -> dict | None:
     alg = algorithmic(case, n, elem)
     kernel_ms = {"up": statistics.mean(up_ms), "down": statistics.mean(down_ms)}
     top = max(kernel_ms, key=kernel_ms.get)
-    achieved_gbs = alg[top]["bytes"] / (kernel_ms[top] / 1e3) / 1e9
-    achieved_tflops = alg[top]["flops"] / (kernel_ms[top] / 1e3) / 1e12
+    seconds = kernel_ms[top] / 1e3
+    achieved_gbs = alg[top]["bytes"] / seconds / 1e9
+    achieved_tflops = alg[top]["flops"] / seconds / 1e12
+    hbm = {"achieved_gbs": achieved_gbs, "peak_gbs": pk["hbm_gbs"], "frac": achieved_gbs / pk["hbm_gbs"],
+           "algorithmic_bytes": alg[top]["bytes"]}
     tokens = n * world * args.steps
+    if tc:
+        # useful (sparse) FLOPs against the measured dense bf16 tensor peak; executed MMA work beside it
+        passes = 3 if elem == 4 else 1
+        rows, cols = (case.d_ff, case.d_model)
+        dense_flops = 2.0 * n * rows * cols * passes
+        pipe_peak = pk["bf16_tflops"] / (2 if elem == 4 else 1)
+        roofline = {"bound": "tensor", "kernel": f"tc_{top}", "achieved": achieved_tflops, "peak": pk["bf16_tflops"],
+                    "unit": "TFLOP/s", "frac": achieved_tflops / pk["bf16_tflops"], "traffic": None,
+                    "algorithmic_flops": alg[top]["flops"], "launch_ms": kernel_ms[top], "peak_source": pk_source,
+                    "tensor_pipe": {"kind": "tf32 x3 (3xTF32 split)" if elem == 4 else "bf16",
+                                    "executed_tflops": dense_flops / seconds / 1e12,
+                                    "peak_tflops": pipe_peak,
+                                    "peak_note": "tf32 = half the measured bf16 peak (nominal ratio)" if elem == 4
+                                    else "measured bf16 burst",
+                                    "frac": dense_flops / seconds / 1e12 / pipe_peak},
+                    "hbm": hbm}
+        launches = (3 if elem == 4 else 2) * args.steps
+    else:
+        roofline = {"bound": "hbm", "kernel": f"{top}_{up if top == 'up' else down}", "achieved": achieved_gbs,
+                    "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved_gbs / pk["hbm_gbs"], "traffic": None,
+                    "algorithmic_bytes": alg[top]["bytes"], "launch_ms": kernel_ms[top], "peak_source": pk_source,
+                    "fp32_cuda_cores": {"achieved_tflops": achieved_tflops, "peak_tflops": fp32_peak,
+                                        "frac": achieved_tflops / fp32_peak if fp32_peak else None,
+                                        "peak_source": "cuBLAS SGEMM 8192^3 TF32 off, measured in this run"}}
+        launches = 2 * args.steps
     line = {
         "metric": f"HFFN FFN layer tokens/s (forward, {workload['dtype']})",
         "value": tokens / total_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -281,18 +329,13 @@ def gpu_arm(args, workload: dict) -> dict | None:
         "config": {"workload": f"{case.name}: d_model {case.d_model}, d_ff {case.d_ff}, support {case.up_degree}, "
                                f"N {n} tokens per GPU per step", "modes": [up, down],
                    "parallelism": "replicas" if world > 1 else "single", "l2": "flushed between steps (512 MiB write)"},
-        "roofline": {"bound": "hbm", "kernel": f"{top}_{up if top == 'up' else down}",
-                     "achieved": achieved_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved_gbs / pk["hbm_gbs"], "traffic": None,
-                     "algorithmic_bytes": alg[top]["bytes"], "launch_ms": kernel_ms[top], "peak_source": pk_source},
-        "compute_roofline": {"bound": "fp32_cuda_cores", "achieved": achieved_tflops, "unit": "TFLOP/s",
-                             "peak": fp32_peak, "frac": achieved_tflops / fp32_peak if fp32_peak else None,
-                             "peak_source": "cuBLAS SGEMM 8192^3 TF32 off, measured in this run",
-                             "algorithmic_flops": alg[top]["flops"]},
+        "roofline": roofline,
+        "fp32_gemm_peak_tflops": fp32_peak,
         "kernels_ms": kernel_ms,
         "e2e": {"value": tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": x_host.numel() * elem,
                 "d2h_bytes_per_step": y_host.numel() * elem},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": launches,
+        "device_errors": runtime.device_errors(),
         "clocks": clocks.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -310,6 +353,8 @@ def main() -> int:
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--ref-tokens", type=int, default=512)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--path", choices=("auto", "cuda_cores", "tensor_cores"), default="auto",
+                        help="forward kernels: the runtime policy, the CUDA-core gather kernels, or the tcgen05 path")
     args = parser.parse_args()
     workload = WORKLOADS[args.workload]
     rank, world, _ = dist_env()

@@ -39,6 +39,10 @@ class TrainParams(ctypes.Structure):
     _fields_ = [("up_val", Param), ("b_up", Param), ("out_val", Param), ("b_down", Param)]
 
 
+class Dense(ctypes.Structure):
+    _fields_ = [("up_hi", _P), ("up_lo", _P), ("down_hi", _P), ("down_lo", _P)]
+
+
 class AdamWStep(ctypes.Structure):
     _fields_ = [(name, ctypes.c_float) for name in
                 ("lr_decay", "beta1", "one_minus_beta1", "beta2", "one_minus_beta2", "step_size", "bias2_sqrt", "eps")]
@@ -60,6 +64,12 @@ SIGNATURES = {
     "hffn_adamw": (ctypes.c_int, [ctypes.POINTER(Param), ctypes.POINTER(AdamWStep), _P]),
     "hffn_mse": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _P, _P]),
     "hffn_validate_layout": (ctypes.c_int, [ctypes.POINTER(Layer), _P, _P]),
+    "hffn_densify": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _I32, _I32, _P, _P, _P]),
+    "hffn_up_tc": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I64, _P]),
+    "hffn_down_tc": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I64, _P]),
+    "hffn_forward_tc_workspace": (_I64, [ctypes.c_int, ctypes.POINTER(Layer), _I64]),
+    "hffn_forward_tc": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(Layer), ctypes.POINTER(Dense), _P, _P, _P, _P, _P,
+                                       _I64, _P]),
 }
 
 

@@ -19,6 +19,16 @@ int launch_adamw(const hffn_param* P, const hffn_adamw_step* step, cudaStream_t 
 int launch_mse(const float* y, const float* target, float* gy, float* loss, int64_t n, int d, float* work,
                cudaStream_t s);
 int launch_validate(const hffn_layer* L, int32_t* flag, cudaStream_t s);
+int tc_forward(int dtype, const hffn_layer* L, const void* up_hi, const void* up_lo, const void* down_hi,
+               const void* down_lo, const void* x, void* y, float* z, void* work, int* err, int64_t n,
+               cudaStream_t s);
+int64_t tc_forward_workspace(int dtype, const hffn_layer* L, int64_t n);
+int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const void* b, void* act_hi, void* act_lo,
+          float* z, void* x_split, int* err, int d, int H, int64_t n, cudaStream_t s);
+int tc_down(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo, const void* b,
+            void* y, int* err, int d, int H, int64_t n, cudaStream_t s);
+int tc_densify(int dtype, const int32_t* off, const int16_t* idx, const void* val, int rows, int cols, void* hi,
+               void* lo, cudaStream_t s);
 
 static thread_local char g_error[512] = "";
 
@@ -62,6 +72,8 @@ static int check_layer(const hffn_layer* L) {
                "edge counts out of the int32 offset range");
   return HFFN_OK;
 }
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace hffn
 
@@ -175,6 +187,71 @@ int hffn_validate_layout(const hffn_layer* layer, int32_t* flag, void* stream) {
   HFFN_REQUIRE(flag != nullptr, "null flag");
   HFFN_TRY(bind_stream_device(stream));
   return launch_validate(layer, flag, static_cast<cudaStream_t>(stream));
+}
+
+int hffn_densify(int dtype, const int32_t* offsets, const int16_t* idx, const void* val, int32_t rows, int32_t cols,
+                 void* hi, void* lo, void* stream) {
+  HFFN_REQUIRE(dtype == HFFN_F32 || dtype == HFFN_BF16, "unknown dtype %d", dtype);
+  HFFN_REQUIRE(rows >= 1 && cols >= 1 && rows <= 32767 && cols <= 32767, "dense shape out of range");
+  HFFN_REQUIRE(offsets && idx && val && hi && (dtype == HFFN_BF16 || lo), "null pointer argument");
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_densify(dtype, offsets, idx, val, rows, cols, hi, lo, static_cast<cudaStream_t>(stream));
+}
+
+int64_t hffn_forward_tc_workspace(int dtype, const hffn_layer* layer, int64_t n) {
+  if (layer == nullptr || n < 1 || (dtype != HFFN_F32 && dtype != HFFN_BF16)) return -1;
+  return tc_forward_workspace(dtype, layer, n);
+}
+
+int hffn_forward_tc(int dtype, const hffn_layer* layer, const hffn_dense* dense, const void* x, void* y, float* z,
+                    void* work, int32_t* err, int64_t n, void* stream) {
+  HFFN_TRY(check_layer(layer));
+  HFFN_TRY(check_shape(dtype, layer->d_model, layer->d_ff, n));
+  HFFN_REQUIRE(n <= (int64_t(1) << 31) - 1, "token count beyond 2^31 - 1");
+  HFFN_REQUIRE(layer->d_model % 8 == 0 && layer->d_ff % 8 == 0, "tensor-core path: d_model and d_ff multiples of 8");
+  HFFN_REQUIRE(dense && dense->up_hi && dense->down_hi && (dtype == HFFN_BF16 || (dense->up_lo && dense->down_lo)),
+               "null dense operand");
+  HFFN_REQUIRE(x && y && work && err, "null pointer argument");
+  HFFN_REQUIRE(z == nullptr || dtype == HFFN_F32, "z is stored by the float32 path only");
+  HFFN_REQUIRE(aligned16(x) && aligned16(work) && aligned16(dense->up_hi) && aligned16(dense->down_hi) &&
+                   (dtype == HFFN_BF16 || (aligned16(dense->up_lo) && aligned16(dense->down_lo))),
+               "tensor-core operands must be 16-byte aligned");
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_forward(dtype, layer, dense->up_hi, dense->up_lo, dense->down_hi, dense->down_lo, x, y, z, work, err, n,
+                    static_cast<cudaStream_t>(stream));
+}
+
+static int check_tc(int dtype, int32_t d_model, int32_t d_ff, int64_t n) {
+  HFFN_TRY(check_shape(dtype, d_model, d_ff, n));
+  HFFN_REQUIRE(n <= (int64_t(1) << 31) - 1, "token count beyond 2^31 - 1");
+  HFFN_REQUIRE(d_model % 8 == 0 && d_ff % 8 == 0, "tensor-core path: d_model and d_ff multiples of 8");
+  return HFFN_OK;
+}
+
+int hffn_up_tc(int dtype, const void* x, const void* w_hi, const void* w_lo, const void* b_up, void* act_hi,
+               void* act_lo, float* z, void* x_split, int32_t* err, int32_t d_model, int32_t d_ff, int64_t n,
+               void* stream) {
+  HFFN_TRY(check_tc(dtype, d_model, d_ff, n));
+  const bool f32 = dtype == HFFN_F32;
+  HFFN_REQUIRE(x && w_hi && b_up && act_hi && err && (!f32 || (w_lo && act_lo && x_split)), "null pointer argument");
+  HFFN_REQUIRE(z == nullptr || f32, "z is stored by the float32 path only");
+  HFFN_REQUIRE(aligned16(x) && aligned16(w_hi) && (!f32 || (aligned16(w_lo) && aligned16(x_split))),
+               "tensor-core operands must be 16-byte aligned");
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_up(dtype, x, w_hi, w_lo, b_up, act_hi, act_lo, z, x_split, err, d_model, d_ff, n,
+               static_cast<cudaStream_t>(stream));
+}
+
+int hffn_down_tc(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo,
+                 const void* b_down, void* y, int32_t* err, int32_t d_model, int32_t d_ff, int64_t n, void* stream) {
+  HFFN_TRY(check_tc(dtype, d_model, d_ff, n));
+  const bool f32 = dtype == HFFN_F32;
+  HFFN_REQUIRE(act_hi && w_hi && b_down && y && err && (!f32 || (act_lo && w_lo)), "null pointer argument");
+  HFFN_REQUIRE(aligned16(act_hi) && aligned16(w_hi) && (!f32 || (aligned16(act_lo) && aligned16(w_lo))),
+               "tensor-core operands must be 16-byte aligned");
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_down(dtype, act_hi, act_lo, w_hi, w_lo, b_down, y, err, d_model, d_ff, n,
+                 static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

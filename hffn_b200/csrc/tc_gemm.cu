@@ -1,0 +1,566 @@
+// HFFN forward on the 5th-generation tensor cores (tcgen05, TMEM accumulators, TMA operand staging), for supports
+// dense enough that a masked dense tile beats the gather path: W_up and W_down are materialised once as dense
+// matrices with zeros off the support ("densified"), and the layer becomes two GEMMs with fused epilogues:
+//   up    Z[r, t] = sum_i W_up[r, i] x[t, i]       epilogue: + b_up[r], exact GELU, (z store), act store
+//   down  Y[o, t] = sum_r W_down[o, r] act[t, r]   epilogue: + b_down[o], y store (token-major)
+// Both are D[M = features, N = tokens] = A[M, K] * B[N, K]^T with A and B K-major; the accumulator tile is
+// 128 features x BN tokens in TMEM (lane = feature, column = token).
+//
+// Precision. bfloat16 storage: one bf16 MMA (kind::f16, fp32 accumulate). float32 storage: the 3xTF32 split
+// (a published method: Ootomo & Yokota 2022, and CUTLASS's "3xTF32" fast-accurate GEMM): every operand v is stored as
+// two tf32 values hi = rna_tf32(v), lo = rna_tf32(v - hi), and a*b is computed as hi*hi + hi*lo + lo*hi (the lo*lo term,
+// ~2^-22 relative, is dropped), with fp32 accumulation in TMEM: products carry ~2^-21 relative error instead of tf32's
+// 2^-11. The conversions are the PTX instruction cvt.rna.tf32.f32.
+//
+// Kernel shape: persistent, one CTA per SM, 6 warps: warp 0 issues the TMA loads (one elected thread), warp 1 owns
+// the TMEM allocation and issues the MMAs (one elected thread), warps 2-5 run the epilogue (one TMEM lane = one
+// feature row per thread). Two accumulator buffers in TMEM let the epilogue of one tile overlap the MMAs of the
+// next. Shared-memory stages are recycled through mbarriers (full: TMA -> MMA, empty: MMA commit -> TMA); every wait
+// is bounded by a 2 s timer after which the kernel records an error code, stops issuing work, waits (bounded) for its
+// own copies in flight, frees its TMEM and returns. No TMA multicast is used.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace hffn {
+namespace tc {
+
+constexpr int kThreads = 192;
+constexpr int BM = 128;                  // features per tile (TMEM lanes)
+constexpr int kRowBytes = 128;           // K extent of one stage: one 128-byte swizzle atom per row
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+enum Epilogue { kUp = 0, kDown = 1 };
+
+// error codes written to the kernel's error flag
+constexpr int kErrTimeoutProducer = 101, kErrTimeoutMma = 102, kErrTimeoutEpilogue = 103;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase of parity `parity` to complete; false after the time limit (or once another role has aborted).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() - start > limit_ns) return false;
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c_inner, int c_row) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c_inner), "r"(c_row)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile in the 128-byte swizzle layout written by TMA:
+// rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte offset), descriptor version 1, layout type 2.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
+         ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: fp32 accumulator, A/B format (tf32 = 2, bf16 = 1), both K-major, N = bn, M = 128.
+__host__ __device__ constexpr uint32_t instr_desc(int fmt, int bn) {
+  return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((uint32_t)(bn >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
+
+template <bool kBf16>
+__device__ __forceinline__ void mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  if constexpr (kBf16) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+  }
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 32 TMEM lanes x 32 consecutive 32-bit columns: register j of lane l = column (taddr.col + j) of lane (taddr.lane + l).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+__device__ __forceinline__ float tf32_rna(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+
+struct EpilogueArgs {
+  const void* bias;   // [M] of the storage type
+  void* out_hi;       // up: act (hi part for fp32) [N, M]; down: y [N, M]
+  void* out_lo;       // up fp32: act lo part [N, M]
+  float* z;           // up fp32, optional: pre-activations [N, M]
+};
+
+template <bool kBf16>
+struct Stage {
+  static constexpr int kParts = kBf16 ? 1 : 2;
+};
+
+// Shared memory: [stages][A parts][128 rows x 128 B] then [stages][B parts][BN rows x 128 B], 1024-aligned.
+template <bool kBf16, int BN, int STAGES>
+struct Layout {
+  static constexpr int kParts = kBf16 ? 1 : 2;
+  static constexpr int kA = BM * kRowBytes;
+  static constexpr int kB = BN * kRowBytes;
+  static constexpr int kStageBytes = kParts * (kA + kB);
+  static constexpr int kOperandBytes = STAGES * kStageBytes;
+  static constexpr int kBarrierBytes = 8 * (2 * STAGES + 5) + 16;
+  static constexpr int kTotal = 1024 + kOperandBytes + kBarrierBytes;
+  static constexpr int kTmemCols = 2 * BN;
+};
+
+template <bool kBf16, int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_a_lo,
+               const __grid_constant__ CUtensorMap map_b_hi, const __grid_constant__ CUtensorMap map_b_lo, int M,
+               int N, int K, EpilogueArgs epi, int* err) {
+  using L = Layout<kBf16, BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* a_base = smem;
+  uint8_t* b_base = smem + STAGES * L::kParts * L::kA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOperandBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN, num_tiles = num_m * num_n;
+  const int num_kb = (K * (kBf16 ? 2 : 4) + kRowBytes - 1) / kRowBytes;
+  const int k_elems = kRowBytes / (kBf16 ? 2 : 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_map(&map_a_hi);
+    prefetch_map(&map_b_hi);
+    if (!kBf16) {
+      prefetch_map(&map_a_lo);
+      prefetch_map(&map_b_lo);
+    }
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(L::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0;   // bit s: stage s has been armed at least once
+      uint32_t armed_parity = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, kWaitNs)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[stage], L::kStageBytes);
+          armed |= 1u << stage;
+          armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          uint8_t* a = a_base + stage * L::kParts * L::kA;
+          uint8_t* b = b_base + stage * L::kParts * L::kB;
+          const int kc = kb * k_elems;
+          tma_load_2d(a, &map_a_hi, &full[stage], kc, m0);
+          tma_load_2d(b, &map_b_hi, &full[stage], kc, n0);
+          if (!kBf16) {
+            tma_load_2d(a + L::kA, &map_a_lo, &full[stage], kc, m0);
+            tma_load_2d(b + L::kB, &map_b_lo, &full[stage], kc, n0);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        atomicCAS(err, 0, kErrTimeoutProducer);
+        *abort_flag = 1;
+      }
+      // wait (bounded) until every armed stage's last load has landed, so no copy is in flight at exit
+      for (int s = 0; s < STAGES; ++s)
+        if (armed & (1u << s)) {
+          const uint64_t start = global_ns();
+          while (!mbar_try_wait(&full[s], (armed_parity >> s) & 1u) && global_ns() - start < kWaitNs) {
+          }
+        }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(kBf16 ? 1 : 2, BN);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, kWaitNs)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, kWaitNs)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t a = smem_u32(a_base + stage * L::kParts * L::kA);
+          const uint32_t b = smem_u32(b_base + stage * L::kParts * L::kB);
+#pragma unroll
+          for (int k = 0; k < kRowBytes / 32; ++k) {
+            const uint32_t acc_in = (kb | k) != 0;
+            const uint64_t ah = smem_desc(a + 32 * k), bh = smem_desc(b + 32 * k);
+            mma<kBf16>(d_tmem, ah, bh, idesc, acc_in);
+            if (!kBf16) {
+              const uint64_t al = smem_desc(a + L::kA + 32 * k), bl = smem_desc(b + L::kB + 32 * k);
+              mma<kBf16>(d_tmem, ah, bl, idesc, 1);
+              mma<kBf16>(d_tmem, al, bh, idesc, 1);
+            }
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok) {
+        atomicCAS(err, 0, kErrTimeoutMma);
+        *abort_flag = 1;
+      }
+      // every MMA issued by this thread has completed before the TMEM is freed (bounded wait)
+      mma_commit(done);
+      const uint64_t start = global_ns();
+      while (!mbar_try_wait(done, 0) && global_ns() - start < kWaitNs) {
+      }
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----------------
+    const int quarter = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, kWaitNs)) {
+        atomicCAS(err, 0, kErrTimeoutEpilogue);
+        *abort_flag = 1;
+        break;
+      }
+      fence_after();
+      const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
+      const int row = m0 + quarter * 32 + lane;
+      float bias = 0.f;
+      if (row < M) {
+        if constexpr (kBf16) bias = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(epi.bias)[row]);
+        else bias = reinterpret_cast<const float*>(epi.bias)[row];
+      }
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + c * 32, v);
+        if (row < M) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int t = n0 + c * 32 + j;
+            if (t < N) {
+              const int64_t at = (int64_t)t * M + row;
+              const float s = v[j] + bias;
+              if constexpr (EPI == kUp) {
+                if (!kBf16 && epi.z) epi.z[at] = s;
+                const float h = gelu(s);
+                if constexpr (kBf16) {
+                  reinterpret_cast<__nv_bfloat16*>(epi.out_hi)[at] = __float2bfloat16_rn(h);
+                } else {
+                  const float hi = tf32_rna(h);
+                  reinterpret_cast<float*>(epi.out_hi)[at] = hi;
+                  reinterpret_cast<float*>(epi.out_lo)[at] = tf32_rna(h - hi);
+                }
+              } else {
+                if constexpr (kBf16) reinterpret_cast<__nv_bfloat16*>(epi.out_hi)[at] = __float2bfloat16_rn(s);
+                else reinterpret_cast<float*>(epi.out_hi)[at] = s;
+              }
+            }
+          }
+        }
+      }
+      fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(L::kTmemCols));
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// operand preparation: densify a compact CSR-by-row layout, split float32 into tf32 hi/lo
+
+__global__ void densify_kernel(const int32_t* __restrict__ off, const int16_t* __restrict__ idx,
+                               const void* __restrict__ val, int rows, int cols, int bf16, void* hi, void* lo) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int64_t base = (int64_t)warp * cols;
+  for (int e = off[warp] + lane; e < off[warp + 1]; e += 32) {
+    const int c = idx[e];
+    if (bf16) {
+      reinterpret_cast<__nv_bfloat16*>(hi)[base + c] = reinterpret_cast<const __nv_bfloat16*>(val)[e];
+    } else {
+      const float v = reinterpret_cast<const float*>(val)[e];
+      const float h = tf32_rna(v);
+      reinterpret_cast<float*>(hi)[base + c] = h;
+      reinterpret_cast<float*>(lo)[base + c] = tf32_rna(v - h);
+    }
+  }
+}
+
+__global__ void split_kernel(const float4* __restrict__ x, float4* __restrict__ hi, float4* __restrict__ lo,
+                             int64_t count4) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = x[i];
+    float4 h, l;
+    h.x = tf32_rna(v.x); l.x = tf32_rna(v.x - h.x);
+    h.y = tf32_rna(v.y); l.y = tf32_rna(v.y - h.y);
+    h.z = tf32_rna(v.z); l.z = tf32_rna(v.z - h.z);
+    h.w = tf32_rna(v.w); l.w = tf32_rna(v.w - h.w);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// [rows, k] K-major operand, box = (128 bytes of K) x box_rows, 128-byte swizzle, zero fill outside.
+static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, bool bf16, int box_rows) {
+  auto fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled unavailable");
+    return HFFN_ERR_CUDA;
+  }
+  const int elem = bf16 ? 2 : 4;
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(k * elem)};
+  cuuint32_t box[2] = {(cuuint32_t)(kRowBytes / elem), (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for a [%lld, %lld] operand", (int)r, (long long)rows, (long long)k);
+    return HFFN_ERR_CUDA;
+  }
+  return HFFN_OK;
+}
+
+static int sm_count() {
+  static int count = 0;
+  if (count == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+    if (count <= 0) count = 148;
+  }
+  return count;
+}
+
+template <bool kBf16, int BN, int STAGES, int EPI>
+static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N, int K,
+                       const EpilogueArgs& epi, int* err, cudaStream_t s) {
+  using L = Layout<kBf16, BN, STAGES>;
+  CUtensorMap ma_hi, ma_lo, mb_hi, mb_lo;
+  HFFN_TRY(make_map(&ma_hi, a_hi, M, K, kBf16, BM));
+  HFFN_TRY(make_map(&mb_hi, b_hi, N, K, kBf16, BN));
+  if (!kBf16) {
+    HFFN_TRY(make_map(&ma_lo, a_lo, M, K, kBf16, BM));
+    HFFN_TRY(make_map(&mb_lo, b_lo, N, K, kBf16, BN));
+  } else {
+    ma_lo = ma_hi;
+    mb_lo = mb_hi;
+  }
+  auto kernel = tc_gemm_kernel<kBf16, BN, STAGES, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+    configured = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kernel<<<grid, kThreads, L::kTotal, s>>>(ma_hi, ma_lo, mb_hi, mb_lo, M, N, K, epi, err);
+  return launch_status(EPI == kUp ? "tc_up" : "tc_down");
+}
+
+}  // namespace tc
+
+// Tile shapes: float32 (3xTF32) BN = 128 with 3 stages (64 KB each); bfloat16 BN = 256 with 4 stages (48 KB each).
+// up: x [n, d] -> act [n, H] token-major (fp32: the split x_hi / x_lo [n, d] go to x_split, act as hi / lo parts).
+int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const void* b, void* act_hi, void* act_lo,
+          float* z, void* x_split, int* err, int d, int H, int64_t n, cudaStream_t s) {
+  const int nn = (int)n;
+  if (dtype == HFFN_BF16) {
+    tc::EpilogueArgs up{b, act_hi, nullptr, nullptr};
+    return tc::launch_gemm<true, 256, 4, tc::kUp>(w_hi, nullptr, x, nullptr, H, nn, d, up, err, s);
+  }
+  float* x_hi = reinterpret_cast<float*>(x_split);
+  float* x_lo = x_hi + (int64_t)n * d;
+  const int64_t count4 = (int64_t)n * d / 4;
+  const int blocks = (int)std::min<int64_t>(std::max<int64_t>(ceil_div(count4, 256), 1), 148 * 8);
+  tc::split_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(x_hi),
+                                          reinterpret_cast<float4*>(x_lo), count4);
+  HFFN_TRY(launch_status("tc_split"));
+  tc::EpilogueArgs up{b, act_hi, act_lo, z};
+  return tc::launch_gemm<false, 128, 3, tc::kUp>(w_hi, w_lo, x_hi, x_lo, H, nn, d, up, err, s);
+}
+
+// down: act [n, H] token-major -> y [n, d].
+int tc_down(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo, const void* b,
+            void* y, int* err, int d, int H, int64_t n, cudaStream_t s) {
+  const int nn = (int)n;
+  tc::EpilogueArgs dn{b, y, nullptr, nullptr};
+  if (dtype == HFFN_BF16) return tc::launch_gemm<true, 256, 4, tc::kDown>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s);
+  return tc::launch_gemm<false, 128, 3, tc::kDown>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err, s);
+}
+
+// Workspace of the whole forward: fp32 [x_hi, x_lo (n d each), act_hi, act_lo (n H each)] floats; bf16 act [n, H].
+int tc_forward(int dtype, const hffn_layer* L, const void* up_hi, const void* up_lo, const void* down_hi,
+               const void* down_lo, const void* x, void* y, float* z, void* work, int* err, int64_t n,
+               cudaStream_t s) {
+  const int d = L->d_model, H = L->d_ff;
+  if (dtype == HFFN_BF16) {
+    HFFN_TRY(tc_up(dtype, x, up_hi, nullptr, L->b_up, work, nullptr, nullptr, nullptr, err, d, H, n, s));
+    return tc_down(dtype, work, nullptr, down_hi, nullptr, L->b_down, y, err, d, H, n, s);
+  }
+  float* x_split = reinterpret_cast<float*>(work);
+  float* act_hi = x_split + 2 * n * d;
+  float* act_lo = act_hi + n * H;
+  HFFN_TRY(tc_up(dtype, x, up_hi, up_lo, L->b_up, act_hi, act_lo, z, x_split, err, d, H, n, s));
+  return tc_down(dtype, act_hi, act_lo, down_hi, down_lo, L->b_down, y, err, d, H, n, s);
+}
+
+int64_t tc_forward_workspace(int dtype, const hffn_layer* L, int64_t n) {
+  if (dtype == HFFN_BF16) return n * L->d_ff * 2;
+  return 4 * (2 * n * L->d_model + 2 * n * L->d_ff);
+}
+
+int tc_densify(int dtype, const int32_t* off, const int16_t* idx, const void* val, int rows, int cols, void* hi,
+               void* lo, cudaStream_t s) {
+  const size_t bytes = (size_t)rows * cols * (dtype == HFFN_BF16 ? 2 : 4);
+  if (cudaMemsetAsync(hi, 0, bytes, s) != cudaSuccess) return launch_status("densify memset");
+  if (dtype != HFFN_BF16 && cudaMemsetAsync(lo, 0, bytes, s) != cudaSuccess) return launch_status("densify memset");
+  const int blocks = (int)ceil_div((int64_t)rows * 32, 256);
+  tc::densify_kernel<<<blocks, 256, 0, s>>>(off, idx, val, rows, cols, dtype == HFFN_BF16, hi, lo);
+  return launch_status("densify");
+}
+
+}  // namespace hffn

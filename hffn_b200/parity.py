@@ -1,7 +1,8 @@
 """Parity of the runtime on one FFN against a float64 expectation: the drop-in of the reference's
 ``runtime/gpu/nvidia/common/kernels/hffn_cuda/parity.py`` (``PAIRS``, ``Parity``, ``check``).
 
-For one input, the runtime runs with its policy and with each of the nine forced (up, down) kernel pairs.
+For one input, the runtime runs with its policy and with each of the nine forced (up, down) kernel pairs, plus the
+tensor-core pair ("tc", "tc") when the runtime has dense operands.
 Criteria: two consecutive calls on the same input give the same bits; ``max |y - y_float64| / max(1, |y_float64|)`` is
 reported for the caller to compare with its guard. Reported without threshold: whether the four tiled pairs
 (up lane/tile, down tiled/blocked) give the same bits (they do here: those kernels share their summation order).
@@ -30,7 +31,8 @@ def check(runtime: HFFNRuntime, index: int, x: torch.Tensor, expected: torch.Ten
     expected = expected.to(x.device, torch.float64)
     scale = expected.abs().clamp(min=1.0)
     result, sequential = Parity(0.0, 0.0, True, True), None
-    for up, down in PAIRS:
+    pairs = PAIRS + ([("tc", "tc")] if getattr(runtime, "tensor_cores", False) else [])
+    for up, down in pairs:
         runtime.force(up, down)
         y = runtime.forward(index, x).clone()
         result.repeatable &= bool(torch.equal(y, runtime.forward(index, x)))

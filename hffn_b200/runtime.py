@@ -24,6 +24,8 @@ from . import _native as native
 
 UP_MODES = ("coop", "lane", "tile")
 DOWN_MODES = ("coop", "tiled", "blocked")
+TC = "tc"                   # the tensor-core path: up and down together, force("tc", "tc")
+TC_MIN_TOKENS = 256         # the policy's tensor-core threshold (dense operands available)
 MAX_TOKENS = 1 << 24        # the kernels index tokens with 32-bit ints and act with 64-bit offsets
 BLOCK = 512                 # threads of the tiled kernels
 UP_TILE = 32                # largest token tile of the up kernel
@@ -106,7 +108,7 @@ def layer_struct(tensors: dict, d_model: int, d_ff: int) -> native.Layer:
 
 class HFFNRuntime:
     def __init__(self, layers: list[HFFNLayer], device: str | torch.device = "cuda",
-                 dtype: torch.dtype = torch.float32) -> None:
+                 dtype: torch.dtype = torch.float32, tensor_cores: bool | None = None) -> None:
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("the HFFN runtime runs on a CUDA device")
@@ -128,15 +130,60 @@ class HFFNRuntime:
                                  else getattr(layer, name).to(self.device)).contiguous() for name in ARRAYS}
                          for layer in layers]
         self._structs = [layer_struct(t, self.d_model, self.d_ff) for t in self._tensors]
+        # Tensor-core operands: the supports densified once (W_up [d_ff, d_model], W_down [d_model, d_ff], zeros off
+        # the support; float32 as tf32 hi/lo pairs). Built when the shape allows it unless tensor_cores=False.
+        compatible = self.d_model % 8 == 0 and self.d_ff % 8 == 0
+        if tensor_cores and not compatible:
+            raise ValueError("the tensor-core path needs d_model and d_ff multiples of 8")
+        self.tensor_cores = compatible if tensor_cores is None else bool(tensor_cores)
+        self._dense: list[dict] = []
+        self._dense_structs: list = []
+        self._dense_stale: list[bool] = []
+        self._err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        if self.tensor_cores:
+            for index in range(len(layers)):
+                self._dense.append(self._alloc_dense())
+                self._dense_structs.append(native.Dense(*(self._dense[index][k].data_ptr() if self._dense[index][k] is not None
+                                                          else None for k in ("up_hi", "up_lo", "down_hi", "down_lo"))))
+                self._dense_stale.append(True)
         self.forced_up: str | None = None
         self.forced_down: str | None = None
         self.calls: Counter = Counter()
         self._tokens = 0
         self._reserve(1)
 
+    def _alloc_dense(self) -> dict:
+        f, d = self.d_ff, self.d_model
+        split = self.dtype == torch.float32
+        make = lambda rows, cols: torch.empty(rows, cols, device=self.device, dtype=self.dtype)  # noqa: E731
+        return {"up_hi": make(f, d), "up_lo": make(f, d) if split else None,
+                "down_hi": make(d, f), "down_lo": make(d, f) if split else None}
+
+    def _densify(self, index: int) -> None:
+        """(Re)build the dense tensor-core operands of layer ``index`` from its compact arrays."""
+        t, dense, stream = self._tensors[index], self._dense[index], native.stream_handle(self.device)
+        ptr = lambda v: None if v is None else v.data_ptr()  # noqa: E731
+        native.check(native.lib.hffn_densify(self._code, t["up_offsets"].data_ptr(), t["up_idx"].data_ptr(),
+                                             t["up_val"].data_ptr(), self.d_ff, self.d_model, ptr(dense["up_hi"]),
+                                             ptr(dense["up_lo"]), stream), "hffn_densify up")
+        native.check(native.lib.hffn_densify(self._code, t["out_offsets"].data_ptr(), t["out_hidden"].data_ptr(),
+                                             t["out_val"].data_ptr(), self.d_model, self.d_ff, ptr(dense["down_hi"]),
+                                             ptr(dense["down_lo"]), stream), "hffn_densify down")
+        self._dense_stale[index] = False
+
+    def mark_updated(self, index: int) -> None:
+        """The compact values of layer ``index`` changed (an optimiser step): the dense operands are rebuilt lazily."""
+        if self.tensor_cores:
+            self._dense_stale[index] = True
+
     def force(self, up: str | None, down: str | None) -> None:
-        """Diagnostic: fix the up and/or the down kernel regardless of N (None: the policy)."""
-        if up not in (None, *UP_MODES) or down not in (None, *DOWN_MODES):
+        """Diagnostic: fix the up and/or the down kernel regardless of N (None: the policy). ``("tc", "tc")`` forces the
+        tensor-core path, whose up and down run together."""
+        if (up == TC) != (down == TC):
+            raise ValueError("the tensor-core path is forced as the pair (\"tc\", \"tc\")")
+        if up == TC and not self.tensor_cores:
+            raise ValueError("this runtime has no tensor-core operands")
+        if up not in (None, TC, *UP_MODES) or down not in (None, TC, *DOWN_MODES):
             raise ValueError("unknown kernel mode")
         self.forced_up, self.forced_down = up, down
 
@@ -144,9 +191,18 @@ class HFFNRuntime:
         self._tokens = n
         self._act = torch.empty(self.d_ff * n, device=self.device, dtype=self.dtype)   # [d_ff, n]
         self._y = torch.empty(n, self.d_model, device=self.device, dtype=self.dtype)
+        self._tc_work = None
+        if self.tensor_cores:
+            size = int(native.lib.hffn_forward_tc_workspace(self._code, self._structs[0], n))
+            self._tc_work = torch.empty(size, dtype=torch.uint8, device=self.device)
 
     def workspace_bytes(self) -> int:
-        return self._act.element_size() * (self._act.numel() + self._y.numel())
+        extra = self._tc_work.numel() if self._tc_work is not None else 0
+        return self._act.element_size() * (self._act.numel() + self._y.numel()) + extra
+
+    def device_errors(self) -> int:
+        """The error flag of the tensor-core kernels (0: none; a wait timed out otherwise). Synchronises."""
+        return int(self._err.item())
 
     def _check_input(self, x: torch.Tensor) -> int:
         if x.dim() != 2 or x.shape[1] != self.d_model or x.dtype != self.dtype or x.device != self._y.device \
@@ -166,13 +222,29 @@ class HFFNRuntime:
         self.calls[up, down] += 1
         return self._y[:n]
 
-    def modes(self, n: int) -> tuple[str, str]:
-        return self.forced_up or up_mode(n, self.d_model), self.forced_down or down_mode(n, self.d_ff)
+    def modes(self, n: int, hidden_major: bool = False) -> tuple[str, str]:
+        """The (up, down) modes of a call on N tokens. ``hidden_major``: the caller needs the hidden-major activations
+        and z of the CUDA-core kernels (the training step), so the tensor-core pair is not taken."""
+        up, down = self.forced_up, self.forced_down
+        if hidden_major and up == TC:
+            up = down = None
+        if up is None and down is None and not hidden_major and self.tensor_cores and n >= TC_MIN_TOKENS:
+            return TC, TC
+        return up or up_mode(n, self.d_model), down or down_mode(n, self.d_ff)
 
     def _launch(self, index: int, x: torch.Tensor, n: int, z: torch.Tensor | None) -> tuple[str, str]:
         """Queue the up then the down kernel of layer ``index`` for the ``n`` tokens of ``x`` (validated, buffers
-        reserved); ``z`` (float32, >= d_ff * n entries) also receives the pre-activations. Returns the modes."""
-        up, down = self.modes(n)
+        reserved); ``z`` (float32, >= d_ff * n entries) also receives the pre-activations, hidden-major (the CUDA-core
+        kernels then run whatever the policy). Returns the modes."""
+        up, down = self.modes(n, hidden_major=z is not None)
+        if up == TC:
+            if self._dense_stale[index]:
+                self._densify(index)
+            status = native.lib.hffn_forward_tc(self._code, self._structs[index], self._dense_structs[index],
+                                                x.data_ptr(), self._y.data_ptr(), None, self._tc_work.data_ptr(),
+                                                self._err.data_ptr(), n, native.stream_handle(self.device))
+            native.check(status, "hffn_forward_tc")
+            return up, down
         status = native.lib.hffn_forward(self._code, self._structs[index], x.data_ptr(), self._y.data_ptr(),
                                          self._act.data_ptr(), None if z is None else z.data_ptr(), n,
                                          native.UP_CODES[up], native.DOWN_CODES[down],

@@ -144,6 +144,9 @@ class HFFNTrainRuntime:
         if z is None:
             return runtime.forward(index, x)
         n = self._check_tokens(x, "x")
+        if z is self._z:          # the step's own buffer: sized here for N (reserve may replace it)
+            self.reserve(n)
+            z = self._z
         if z.dtype != torch.float32 or z.device != runtime._y.device or not z.is_contiguous() or z.numel() < self.d_ff * n:
             raise ValueError("z must be a contiguous float32 device tensor of at least d_ff * N entries")
         self.reserve(n)
@@ -184,11 +187,14 @@ class HFFNTrainRuntime:
         params = self._param_structs[index]
         for name in PARAMETERS:
             native.check(native.lib.hffn_adamw(getattr(params, name), scalars, stream), "hffn_adamw")
+        self.runtime.mark_updated(index)
 
     def step(self, index: int, x: torch.Tensor, gy: torch.Tensor) -> torch.Tensor:
         """Forward (z stored in the step's buffer), then the fused backward + AdamW. Returns gx (a view)."""
         self.forward(index, x, self._z)
-        return self._backward(index, gy, self._next_step(index))
+        gx = self._backward(index, gy, self._next_step(index))
+        self.runtime.mark_updated(index)
+        return gx
 
     def step_mse(self, index: int, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
         """One step on the MSE loss ``mean((y - target)^2)``: forward, loss and its gradient
@@ -203,6 +209,7 @@ class HFFNTrainRuntime:
                                          self.d_model, self._work.data_ptr(), native.stream_handle(self.runtime.device)),
                      "hffn_mse")
         self._backward(index, gy, self._next_step(index))
+        self.runtime.mark_updated(index)
         return self._loss
 
     # -- read access for the checks (views, no copy) -------------------------------------------------------------

@@ -139,6 +139,44 @@ int hffn_mse(const float* y, const float* target, float* gy, float* loss, int64_
  * (runtime/common/pythia/hffn_pythia/export.py:37-45) on device-resident arrays. */
 int hffn_validate_layout(const hffn_layer* layer, int32_t* flag, void* stream);
 
+/* Dense tensor-core operands of one layer, built by hffn_densify: W_up [d_ff, d_model] and W_down [d_model, d_ff] with
+ * zeros off the support. float32: the tf32 hi and lo parts of the 3xTF32 split; bfloat16: hi only (lo NULL). */
+typedef struct hffn_dense {
+  void* up_hi;
+  void* up_lo;
+  void* down_hi;
+  void* down_lo;
+} hffn_dense;
+
+/* Materialise the dense [rows, cols] matrix of a CSR-by-row support (up: rows = d_ff over up_offsets / up_idx /
+ * up_val; down: rows = d_model over out_offsets / out_hidden / out_val). The reference has no dense path: this is the
+ * "support densified at high density" layout of the tensor-core forward, built once per layer. */
+int hffn_densify(int dtype, const int32_t* offsets, const int16_t* idx, const void* val, int32_t rows, int32_t cols,
+                 void* hi, void* lo, void* stream);
+
+/* The up projection on the tensor cores (same function as hffn_up; replaces the up_* kernels, kernels.py:102-143):
+ * act = gelu(W_up x + b_up), TOKEN-major [n, d_ff]. float32: x is split into tf32 hi/lo parts in x_split
+ * (2 n d_model floats) and act is written as its hi (act_hi) and lo (act_lo) parts; z NULL or float32 [n, d_ff].
+ * bfloat16: w_lo, act_lo, x_split and z NULL. err: device int32 set non-zero if a wait timed out. */
+int hffn_up_tc(int dtype, const void* x, const void* w_hi, const void* w_lo, const void* b_up, void* act_hi,
+               void* act_lo, float* z, void* x_split, int32_t* err, int32_t d_model, int32_t d_ff, int64_t n,
+               void* stream);
+
+/* The down projection on the tensor cores (same function as hffn_down; replaces the down_* kernels,
+ * kernels.py:145-191): y = W_down act + b_down from the token-major act of hffn_up_tc. */
+int hffn_down_tc(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo,
+                 const void* b_down, void* y, int32_t* err, int32_t d_model, int32_t d_ff, int64_t n, void* stream);
+
+/* Bytes of the workspace hffn_forward_tc needs for n tokens. */
+int64_t hffn_forward_tc_workspace(int dtype, const hffn_layer* layer, int64_t n);
+
+/* The forward on the tcgen05 tensor cores, the same function as hffn_forward (it replaces HFFNRuntime._launch,
+ * runtime.py:134-163, for large n): up GEMM with a bias + GELU epilogue, then down GEMM with a bias epilogue.
+ * y [n, d_model]; z NULL or float32 [n, d_ff] TOKEN-major; work: hffn_forward_tc_workspace bytes;
+ * err: device int32, set non-zero by a kernel whose wait timed out (never cleared by the call). */
+int hffn_forward_tc(int dtype, const hffn_layer* layer, const hffn_dense* dense, const void* x, void* y, float* z,
+                    void* work, int32_t* err, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

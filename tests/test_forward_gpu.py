@@ -27,9 +27,9 @@ def kernel_layer(layer):
                                        t(layer.down_val))
 
 
-def runtime_for(layer, dtype=torch.float32):
+def runtime_for(layer, dtype=torch.float32, tensor_cores=None):
     from hffn_b200.runtime import HFFNRuntime
-    return HFFNRuntime([kernel_layer(layer)], "cuda", dtype)
+    return HFFNRuntime([kernel_layer(layer)], "cuda", dtype, tensor_cores=tensor_cores)
 
 
 @pytest.mark.parametrize("name", sorted(synth.TEST_CASES))
@@ -71,19 +71,22 @@ def rows_subset(n):
     return np.r_[0:24, n // 2:n // 2 + 8, n - 24:n]
 
 
+@pytest.mark.parametrize("tensor_cores", [False, None])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_c2_config_full_size(dtype):
+def test_c2_config_full_size(dtype, tensor_cores):
     case = synth.CONFIGS["c2_1024_4096_k512"]
     layer = synth.make_layer(case)
     n = 4096
     x = synth.make_input(case, n)
-    runtime = runtime_for(layer, dtype)
+    runtime = runtime_for(layer, dtype, tensor_cores)
     y = runtime.forward(0, torch.from_numpy(x).cuda().to(dtype)).float().cpu().numpy()
     rows = rows_subset(n)
     expected = forward64.forward(layer, x[rows])
     relative = np.max(np.abs(y[rows] - expected) / np.maximum(1.0, np.abs(expected)))
     assert relative <= (REL_TOLERANCE if dtype == torch.float32 else BF16_TOLERANCE), relative
     assert np.isfinite(y).all()
+    assert runtime.modes(n)[0] == ("tc" if tensor_cores is None else "tile")
+    assert runtime.device_errors() == 0
 
 
 def test_side_stream_and_second_call_same_bits():

@@ -1,0 +1,99 @@
+"""GPU parity of the tensor-core (tcgen05) forward against the float64 oracle, through the C ABI.
+
+float32 runs the 3xTF32 split and must meet the float32 bar (relative 1e-5 with floor 1, absolute 2e-5); bfloat16
+storage relative 2e-2. The kernels' bounded waits must never fire (error flag 0)."""
+import numpy as np
+import pytest
+import torch
+
+from hffn_b200 import synth
+from oracle import forward64
+
+pytestmark = pytest.mark.gpu
+
+
+def kernel_layer(layer):
+    from hffn_b200.runtime import HFFNLayer
+    t = torch.from_numpy
+    return HFFNLayer.from_hidden_major(layer.d_model, layer.d_ff, t(layer.b_up), t(layer.up_offsets), t(layer.up_idx),
+                                       t(layer.up_val), t(layer.b_down), t(layer.down_offsets), t(layer.down_idx),
+                                       t(layer.down_val))
+
+
+def tc_runtime(layer, dtype=torch.float32):
+    from hffn_b200.runtime import HFFNRuntime
+    runtime = HFFNRuntime([kernel_layer(layer)], "cuda", dtype, tensor_cores=True)
+    runtime.force("tc", "tc")
+    return runtime
+
+
+def relative(y, expected):
+    return float(np.max(np.abs(y - expected) / np.maximum(1.0, np.abs(expected))))
+
+
+@pytest.mark.parametrize("n", [1, 7, 128, 129, 300])
+def test_small_layer(n):
+    case = synth.TEST_CASES["homog_256_1024"]
+    layer = synth.make_layer(case)
+    runtime = tc_runtime(layer)
+    x = synth.make_input(case, n)
+    y = runtime.forward(0, torch.from_numpy(x).cuda()).double().cpu().numpy()
+    expected = forward64.forward(layer, x)
+    assert runtime.device_errors() == 0
+    assert np.max(np.abs(y - expected)) <= 2e-5 and relative(y, expected) <= 1e-5, relative(y, expected)
+    assert runtime.calls[("tc", "tc")] == 1
+
+
+def test_irregular_layer_repeatable():
+    case = synth.TEST_CASES["irreg_512_2048"]
+    layer = synth.make_layer(case)
+    runtime = tc_runtime(layer)
+    x = torch.from_numpy(synth.make_input(case, 333)).cuda()
+    first = runtime.forward(0, x).clone()
+    assert torch.equal(first, runtime.forward(0, x))
+    assert relative(first.double().cpu().numpy(), forward64.forward(layer, x.cpu().numpy())) <= 1e-5
+    assert runtime.device_errors() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_c1_and_c2(dtype):
+    for name, n in (("c1_512_2048_k128", 256), ("c2_1024_4096_k512", 4096)):
+        case = synth.CONFIGS[name]
+        layer = synth.make_layer(case)
+        runtime = tc_runtime(layer, dtype)
+        x = synth.make_input(case, n)
+        y = runtime.forward(0, torch.from_numpy(x).cuda().to(dtype)).float().cpu().numpy()
+        rows = np.r_[0:16, n - 16:n]
+        rel = relative(y[rows], forward64.forward(layer, x[rows]))
+        assert rel <= (1e-5 if dtype == torch.float32 else 2e-2), (name, dtype, rel)
+        assert np.isfinite(y).all() and runtime.device_errors() == 0
+
+
+def test_policy_picks_tensor_cores_for_large_batches():
+    from hffn_b200.runtime import HFFNRuntime, TC_MIN_TOKENS
+    case = synth.TEST_CASES["homog_512_2048"]
+    runtime = HFFNRuntime([kernel_layer(synth.make_layer(case))], "cuda")
+    assert runtime.modes(TC_MIN_TOKENS) == ("tc", "tc")
+    assert runtime.modes(8) == ("coop", "coop")
+    assert runtime.modes(TC_MIN_TOKENS, hidden_major=True)[0] != "tc"
+
+
+def test_dense_operands_follow_optimizer_steps():
+    """After a training step updates the compact values, the tensor-core forward sees the new values."""
+    from hffn_b200.runtime import HFFNRuntime
+    from hffn_b200.train_runtime import HFFNTrainRuntime
+    case = synth.TEST_CASES["homog_256_1024"]
+    layer = synth.make_layer(case)
+    runtime = HFFNRuntime([kernel_layer(layer)], "cuda", tensor_cores=True)
+    train = HFFNTrainRuntime(runtime)
+    x = torch.from_numpy(synth.make_input(case, 300)).cuda()
+    gy = torch.from_numpy(synth.make_upstream(case, 300, 0)).cuda()
+    runtime.force("tc", "tc")
+    before = runtime.forward(0, x).clone()
+    train.step(0, x, gy)
+    after_tc = runtime.forward(0, x).clone()
+    runtime.force("tile", "blocked")
+    after_cuda_cores = runtime.forward(0, x).clone()
+    assert not torch.equal(before, after_tc)
+    assert float((after_tc - after_cuda_cores).abs().max()) <= 2e-5
+    assert runtime.device_errors() == 0

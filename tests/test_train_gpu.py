@@ -133,6 +133,19 @@ def test_gates(n):
     assert train.growths == growths
 
 
+def test_step_sizes_its_own_buffers():
+    """A runtime built for one token and stepped at N sizes its z / gz / gx buffers itself."""
+    from hffn_b200.runtime import HFFNRuntime
+    from hffn_b200.train_runtime import HFFNTrainRuntime
+    case = synth.TEST_CASES[LAYER]
+    layer = synth.make_layer(case)
+    train = HFFNTrainRuntime(HFFNRuntime([kernel_layer(layer)], "cuda"))
+    x = torch.from_numpy(synth.make_input(case, 37)).cuda()
+    gy = torch.from_numpy(synth.make_upstream(case, 37, 0)).cuda()
+    gx = train.step(0, x, gy)
+    assert gx.shape == (37, layer.d_model) and bool(torch.isfinite(gx).all())
+
+
 def test_backward_order_refused():
     case = synth.TEST_CASES[LAYER]
     layer = synth.make_layer(case)
