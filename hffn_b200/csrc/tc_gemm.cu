@@ -12,6 +12,9 @@
 // ~2^-22 relative, is dropped), with fp32 accumulation in TMEM: products carry ~2^-21 relative error instead of tf32's
 // 2^-11. The conversions are the PTX instruction cvt.rna.tf32.f32.
 //
+// float32 accumulation runs in K chunks of 64 (24 MMAs) into fresh TMEM accumulators that the epilogue adds into
+// float32 registers with round-to-nearest: the accumulation bias of the tensor core stays bounded by one chunk.
+//
 // Kernel shape: persistent, one CTA per SM, 6 warps: warp 0 issues the TMA loads (one elected thread), warp 1 owns
 // the TMEM allocation and issues the MMAs (one elected thread), warps 2-5 run the epilogue (one TMEM lane = one
 // feature row per thread). Two accumulator buffers in TMEM let the epilogue of one tile overlap the MMAs of the
@@ -174,7 +177,7 @@ struct Layout {
   static constexpr int kTmemCols = 2 * BN;
 };
 
-template <bool kBf16, int BN, int STAGES, int EPI>
+template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_a_lo,
                const __grid_constant__ CUtensorMap map_b_hi, const __grid_constant__ CUtensorMap map_b_lo, int M,
@@ -275,48 +278,54 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
+    // The K loop of a tile runs in chunks of chunk_kb k-blocks, each into a fresh accumulator buffer that the
+    // epilogue drains (float32: the chunk sums are added in registers with round-to-nearest; see the epilogue).
     if (lane == 0) {
       constexpr uint32_t idesc = instr_desc(kBf16 ? 1 : 2, BN);
+      const int chunk_kb = KCHUNK > 0 ? KCHUNK : num_kb;
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, kWaitNs)) {
-          ok = false;
-          break;
-        }
-        fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, kWaitNs)) {
+        for (int kc = 0; kc < num_kb && ok; kc += chunk_kb) {
+          const int kend = kc + chunk_kb < num_kb ? kc + chunk_kb : num_kb;
+          if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, kWaitNs)) {
             ok = false;
             break;
           }
           fence_after();
-          const uint32_t a = smem_u32(a_base + stage * L::kParts * L::kA);
-          const uint32_t b = smem_u32(b_base + stage * L::kParts * L::kB);
+          const uint32_t d_tmem = tmem_base + acc * BN;
+          for (int kb = kc; kb < kend; ++kb) {
+            if (!mbar_wait(&full[stage], phase, abort_flag, kWaitNs)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+            const uint32_t a = smem_u32(a_base + stage * L::kParts * L::kA);
+            const uint32_t b = smem_u32(b_base + stage * L::kParts * L::kB);
 #pragma unroll
-          for (int k = 0; k < kRowBytes / 32; ++k) {
-            const uint32_t acc_in = (kb | k) != 0;
-            const uint64_t ah = smem_desc(a + 32 * k), bh = smem_desc(b + 32 * k);
-            mma<kBf16>(d_tmem, ah, bh, idesc, acc_in);
-            if (!kBf16) {
-              const uint64_t al = smem_desc(a + L::kA + 32 * k), bl = smem_desc(b + L::kB + 32 * k);
-              mma<kBf16>(d_tmem, ah, bl, idesc, 1);
-              mma<kBf16>(d_tmem, al, bh, idesc, 1);
+            for (int k = 0; k < kRowBytes / 32; ++k) {
+              const uint32_t acc_in = (kb != kc || k != 0) ? 1u : 0u;
+              const uint64_t ah = smem_desc(a + 32 * k), bh = smem_desc(b + 32 * k);
+              mma<kBf16>(d_tmem, ah, bh, idesc, acc_in);
+              if (!kBf16) {
+                const uint64_t al = smem_desc(a + L::kA + 32 * k), bl = smem_desc(b + L::kB + 32 * k);
+                mma<kBf16>(d_tmem, ah, bl, idesc, 1);
+                mma<kBf16>(d_tmem, al, bh, idesc, 1);
+              }
+            }
+            mma_commit(&empty[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
             }
           }
-          mma_commit(&empty[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
+          if (!ok) break;
+          mma_commit(&tfull[acc]);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1;
           }
-        }
-        if (!ok) break;
-        mma_commit(&tfull[acc]);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1;
         }
       }
       if (!ok) {
@@ -332,15 +341,30 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
   } else {
     // ---------------- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----------------
     const int quarter = warp & 3;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, kWaitNs)) {
-        atomicCAS(err, 0, kErrTimeoutEpilogue);
-        *abort_flag = 1;
-        break;
+    bool ok = true;
+    // one value of the output tile: bias, then (up) GELU and the stores of act (and z)
+    auto emit = [&](int row, int t, float v, float bias) {
+      const int64_t at = (int64_t)t * M + row;
+      const float s = v + bias;
+      if constexpr (EPI == kUp) {
+        if (!kBf16 && epi.z) epi.z[at] = s;
+        const float h = gelu(s);
+        if constexpr (kBf16) {
+          reinterpret_cast<__nv_bfloat16*>(epi.out_hi)[at] = __float2bfloat16_rn(h);
+        } else {
+          const float hi = tf32_rna(h);
+          reinterpret_cast<float*>(epi.out_hi)[at] = hi;
+          reinterpret_cast<float*>(epi.out_lo)[at] = tf32_rna(h - hi);
+        }
+      } else {
+        if constexpr (kBf16) reinterpret_cast<__nv_bfloat16*>(epi.out_hi)[at] = __float2bfloat16_rn(s);
+        else reinterpret_cast<float*>(epi.out_hi)[at] = s;
       }
-      fence_after();
+    };
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
       const int row = m0 + quarter * 32 + lane;
       float bias = 0.f;
@@ -348,40 +372,63 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
         if constexpr (kBf16) bias = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(epi.bias)[row]);
         else bias = reinterpret_cast<const float*>(epi.bias)[row];
       }
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + c * 32, v);
-        if (row < M) {
+      if constexpr (KCHUNK > 0) {
+        // chunk partials summed in registers, chunk after chunk, round-to-nearest
+        float sum[BN];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int t = n0 + c * 32 + j;
-            if (t < N) {
-              const int64_t at = (int64_t)t * M + row;
-              const float s = v[j] + bias;
-              if constexpr (EPI == kUp) {
-                if (!kBf16 && epi.z) epi.z[at] = s;
-                const float h = gelu(s);
-                if constexpr (kBf16) {
-                  reinterpret_cast<__nv_bfloat16*>(epi.out_hi)[at] = __float2bfloat16_rn(h);
-                } else {
-                  const float hi = tf32_rna(h);
-                  reinterpret_cast<float*>(epi.out_hi)[at] = hi;
-                  reinterpret_cast<float*>(epi.out_lo)[at] = tf32_rna(h - hi);
-                }
-              } else {
-                if constexpr (kBf16) reinterpret_cast<__nv_bfloat16*>(epi.out_hi)[at] = __float2bfloat16_rn(s);
-                else reinterpret_cast<float*>(epi.out_hi)[at] = s;
-              }
-            }
+        for (int i = 0; i < BN; ++i) sum[i] = 0.f;
+        for (int kc = 0; kc < num_kb; kc += KCHUNK) {
+          if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, kWaitNs)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c) {
+            float v[32];
+            tmem_ld32(lane_base + acc * BN + c * 32, v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sum[c * 32 + j] += v[j];
+          }
+          fence_before();
+          mbar_arrive(&tempty[acc]);
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1;
           }
         }
+        if (!ok) break;
+        if (row < M) {
+#pragma unroll
+          for (int i = 0; i < BN; ++i)
+            if (n0 + i < N) emit(row, n0 + i, sum[i], bias);
+        }
+      } else {
+        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, kWaitNs)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(lane_base + acc * BN + c * 32, v);
+          if (row < M) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + c * 32 + j < N) emit(row, n0 + c * 32 + j, v[j], bias);
+          }
+        }
+        fence_before();
+        mbar_arrive(&tempty[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
       }
-      fence_before();
-      mbar_arrive(&tempty[acc]);
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1;
-      }
+    }
+    if (!ok) {
+      atomicCAS(err, 0, kErrTimeoutEpilogue);
+      *abort_flag = 1;
     }
   }
   fence_before();
@@ -475,7 +522,7 @@ static int sm_count() {
   return count;
 }
 
-template <bool kBf16, int BN, int STAGES, int EPI>
+template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK>
 static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N, int K,
                        const EpilogueArgs& epi, int* err, cudaStream_t s) {
   using L = Layout<kBf16, BN, STAGES>;
@@ -489,7 +536,7 @@ static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, con
     ma_lo = ma_hi;
     mb_lo = mb_hi;
   }
-  auto kernel = tc_gemm_kernel<kBf16, BN, STAGES, EPI>;
+  auto kernel = tc_gemm_kernel<kBf16, BN, STAGES, EPI, KCHUNK>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
@@ -504,13 +551,17 @@ static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, con
 }  // namespace tc
 
 // Tile shapes: float32 (3xTF32) BN = 128 with 3 stages (64 KB each); bfloat16 BN = 256 with 4 stages (48 KB each).
+// float32 accumulation: the tensor cores' fp32 accumulation in TMEM is not round-to-nearest at every add (measured
+// here: results biased toward zero by ~1e-5 relative over ~400 MMAs), so the K loop runs in chunks of kFp32Chunk
+// k-blocks (64 K values, 24 MMAs) into fresh accumulators whose values the epilogue adds in float32 registers.
+constexpr int kFp32Chunk = 2;
 // up: x [n, d] -> act [n, H] token-major (fp32: the split x_hi / x_lo [n, d] go to x_split, act as hi / lo parts).
 int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const void* b, void* act_hi, void* act_lo,
           float* z, void* x_split, int* err, int d, int H, int64_t n, cudaStream_t s) {
   const int nn = (int)n;
   if (dtype == HFFN_BF16) {
     tc::EpilogueArgs up{b, act_hi, nullptr, nullptr};
-    return tc::launch_gemm<true, 256, 4, tc::kUp>(w_hi, nullptr, x, nullptr, H, nn, d, up, err, s);
+    return tc::launch_gemm<true, 256, 4, tc::kUp, 0>(w_hi, nullptr, x, nullptr, H, nn, d, up, err, s);
   }
   float* x_hi = reinterpret_cast<float*>(x_split);
   float* x_lo = x_hi + (int64_t)n * d;
@@ -520,7 +571,7 @@ int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const vo
                                           reinterpret_cast<float4*>(x_lo), count4);
   HFFN_TRY(launch_status("tc_split"));
   tc::EpilogueArgs up{b, act_hi, act_lo, z};
-  return tc::launch_gemm<false, 128, 3, tc::kUp>(w_hi, w_lo, x_hi, x_lo, H, nn, d, up, err, s);
+  return tc::launch_gemm<false, 128, 3, tc::kUp, kFp32Chunk>(w_hi, w_lo, x_hi, x_lo, H, nn, d, up, err, s);
 }
 
 // down: act [n, H] token-major -> y [n, d].
@@ -528,8 +579,8 @@ int tc_down(int dtype, const void* act_hi, const void* act_lo, const void* w_hi,
             void* y, int* err, int d, int H, int64_t n, cudaStream_t s) {
   const int nn = (int)n;
   tc::EpilogueArgs dn{b, y, nullptr, nullptr};
-  if (dtype == HFFN_BF16) return tc::launch_gemm<true, 256, 4, tc::kDown>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s);
-  return tc::launch_gemm<false, 128, 3, tc::kDown>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err, s);
+  if (dtype == HFFN_BF16) return tc::launch_gemm<true, 256, 4, tc::kDown, 0>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s);
+  return tc::launch_gemm<false, 128, 3, tc::kDown, kFp32Chunk>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err, s);
 }
 
 // Workspace of the whole forward: fp32 [x_hi, x_lo (n d each), act_hi, act_lo (n H each)] floats; bf16 act [n, H].
