@@ -177,6 +177,18 @@ int64_t hffn_forward_tc_workspace(int dtype, const hffn_layer* layer, int64_t n)
 int hffn_forward_tc(int dtype, const hffn_layer* layer, const hffn_dense* dense, const void* x, void* y, float* z,
                     void* work, int32_t* err, int64_t n, void* stream);
 
+/* Forward that allocates nothing and needs no workspace from the caller. No counterpart in the reference.
+ * Some callers can hand this library only their input and output buffers: a plugin whose host framework owns every
+ * device allocation and exposes no allocator, or a caller that must not call cudaMalloc on its path (it can
+ * synchronise the device). This entry runs the same CUDA-core kernels as hffn_forward under its policy and keeps the
+ * hidden activations in a 16 MiB array that the library holds on every GPU that loads it, until the process exits.
+ * Limit: d_ff x n x sizeof(storage) <= hffn_forward_noalloc_max_bytes() (16 MiB); larger calls return
+ * HFFN_ERR_ARGUMENT before any launch. The first call on a device looks up the array's device address with that
+ * device current; make that first call before any stream capture. Every call uses the same array: calls that
+ * overlap on the GPU (other streams, other host threads) race on it. */
+int64_t hffn_forward_noalloc_max_bytes(void);
+int hffn_forward_noalloc(int dtype, const hffn_layer* layer, const void* x, void* y, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
