@@ -36,6 +36,7 @@ WORKLOADS = {
     "fwd": {"case": "c2_1024_4096_k512", "n": 4096, "dtype": "fp32"},
     "fwd_bf16": {"case": "c2_1024_4096_k512", "n": 4096, "dtype": "bf16"},
     "train": {"case": "c3_2048_8192_k1638", "n": 8192, "dtype": "fp32"},
+    "train_small": {"case": "c3_2048_8192_k1638", "n": 1024, "dtype": "fp32"},
 }
 CLOCK_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
                "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -176,118 +177,176 @@ def fp32_gemm_peak(torch) -> float:
     return 2 * 8192 ** 3 / best / 1e12
 
 
+def canonical(layer, torch) -> dict:
+    return {k: torch.from_numpy(getattr(layer, k).copy()) for k in
+            ("b_up", "up_offsets", "up_idx", "up_val", "b_down", "down_offsets", "down_idx", "down_val")}
+
+
+def rank_input(case, n: int, rank: int) -> np.ndarray:
+    """Rank 0's batch is the workload's seeded input; rank k > 0 draws its own from [seed, n, 1000 + k]."""
+    from hffn_b200 import synth
+    if rank == 0:
+        return synth.make_input(case, n)
+    rng = np.random.default_rng([case.seed, n, 1000 + rank])
+    return np.ascontiguousarray(rng.standard_normal((n, case.d_model)).astype(np.float32))
+
+
+def setup_dist(torch):
+    import datetime
+
+    import torch.distributed as dist
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    return rank, world, local, device
+
+
+def max_over_ranks(torch, values: list[float], world: int, device) -> list[float]:
+    import torch.distributed as dist
+    t = torch.tensor(values, device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
 def gpu_arm(args, workload: dict) -> dict | None:
     import torch
     import torch.distributed as dist
 
     from hffn_b200 import _native as native
     from hffn_b200 import synth
+    from hffn_b200.distributed import sharded_runtime
     from hffn_b200.runtime import HFFNLayer, HFFNRuntime
 
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=device)
+    rank, world, local, device = setup_dist(torch)
+    if args.workload.startswith("train"):
+        return train_arm(args, workload, rank, world, local, device)
     case = synth.CASES[workload["case"]]
     n = workload["n"]
     dtype = torch.float32 if workload["dtype"] == "fp32" else torch.bfloat16
+    elem = 4 if dtype == torch.float32 else 2
     layer = synth.make_layer(case)
-    t = torch.from_numpy
-    kl = HFFNLayer.from_hidden_major(layer.d_model, layer.d_ff, t(layer.b_up), t(layer.up_offsets), t(layer.up_idx),
-                                     t(layer.up_val), t(layer.b_down), t(layer.down_offsets), t(layer.down_idx),
-                                     t(layer.down_val))
-    runtime = HFFNRuntime([kl], device, dtype, tensor_cores=False if args.path == "cuda_cores" else None)
+    tensor_cores = False if args.path == "cuda_cores" else None
+    if world == 1:
+        t = torch.from_numpy
+        kl = HFFNLayer.from_hidden_major(layer.d_model, layer.d_ff, t(layer.b_up), t(layer.up_offsets),
+                                         t(layer.up_idx), t(layer.up_val), t(layer.b_down), t(layer.down_offsets),
+                                         t(layer.down_idx), t(layer.down_val))
+        runtime, shard, (lo, hi) = HFFNRuntime([kl], device, dtype, tensor_cores=tensor_cores), None, (0, case.d_ff)
+    else:
+        runtime, shard, (lo, hi) = sharded_runtime(case.d_model, canonical(layer, torch), device, dtype,
+                                                   tensor_cores=tensor_cores)
     if args.path == "tensor_cores":
         runtime.force("tc", "tc")
-    x_host = t(synth.make_input(case, n)).to(dtype).pin_memory()
+    d, f_local = case.d_model, hi - lo
+    n_kernel = n * world                       # a shard runs every rank's batch through its neurons
+    x_host = torch.from_numpy(rank_input(case, n, rank)).to(dtype).pin_memory()
     x = x_host.to(device)
-    runtime.forward(0, x)
-    up, down = runtime.modes(n)
+    x_all = torch.from_numpy(np.concatenate([rank_input(case, n, k) for k in range(world)])).to(dtype).to(device) \
+        if world > 1 else x
+    runtime.forward(0, x_all)
+    up, down = runtime.modes(n_kernel)
     code, struct = runtime._code, runtime._structs[0]
     stream = torch.cuda.current_stream(device)
     handle = stream.cuda_stream
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=device)
     tc = up == "tc"
+    ptr = lambda v: None if v is None else v.data_ptr()  # noqa: E731
     if tc:
         dense, work, err = runtime._dense[0], runtime._tc_work.data_ptr(), runtime._err.data_ptr()
-        ptr = lambda v: None if v is None else v.data_ptr()  # noqa: E731
         if dtype == torch.float32:
-            x_split, act_hi = work, work + 2 * n * case.d_model * 4
-            act_lo = act_hi + n * case.d_ff * 4
+            x_split, act_hi = work, work + 2 * n_kernel * d * 4
+            act_lo = act_hi + n_kernel * f_local * 4
         else:
             x_split, act_hi, act_lo = None, work, None
 
-    def step():
+    def kernels(marks):
+        """The two kernels of one forward of the local runtime over x_all, an event between them."""
         if tc:
-            native.check(native.lib.hffn_up_tc(code, x.data_ptr(), ptr(dense["up_hi"]), ptr(dense["up_lo"]),
-                                               struct.b_up, act_hi, act_lo, None, x_split, err, case.d_model,
-                                               case.d_ff, n, handle), "hffn_up_tc")
+            native.check(native.lib.hffn_up_tc(code, x_all.data_ptr(), ptr(dense["up_hi"]), ptr(dense["up_lo"]),
+                                               struct.b_up, act_hi, act_lo, None, x_split, err, d, f_local,
+                                               n_kernel, handle), "hffn_up_tc")
             marks[1].record(stream)
             native.check(native.lib.hffn_down_tc(code, act_hi, act_lo, ptr(dense["down_hi"]), ptr(dense["down_lo"]),
-                                                 struct.b_down, runtime._y.data_ptr(), err, case.d_model, case.d_ff,
-                                                 n, handle), "hffn_down_tc")
+                                                 struct.b_down, runtime._y.data_ptr(), err, d, f_local, n_kernel,
+                                                 handle), "hffn_down_tc")
             return
-        native.check(native.lib.hffn_up(code, native.UP_CODES[up], x.data_ptr(), struct.up_offsets, struct.up_idx,
-                                        struct.up_val, struct.b_up, runtime._act.data_ptr(), None, case.d_model,
-                                        case.d_ff, n, handle), "hffn_up")
+        native.check(native.lib.hffn_up(code, native.UP_CODES[up], x_all.data_ptr(), struct.up_offsets,
+                                        struct.up_idx, struct.up_val, struct.b_up, runtime._act.data_ptr(), None, d,
+                                        f_local, n_kernel, handle), "hffn_up")
         marks[1].record(stream)
         native.check(native.lib.hffn_down(code, native.DOWN_CODES[down], runtime._act.data_ptr(), struct.out_offsets,
-                                          struct.out_hidden, struct.out_val, struct.b_down, runtime._y.data_ptr(),
-                                          case.d_model, case.d_ff, n, handle), "hffn_down")
+                                          struct.out_hidden, struct.out_val, struct.b_down, runtime._y.data_ptr(), d,
+                                          f_local, n_kernel, handle), "hffn_down")
 
-    marks = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-    for _ in range(args.warmup):
+    def events(k):
+        return [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(k)]
+
+    # kernel loop: the local forward's two kernels, per-kernel events (the roofline's timing); for one GPU it is
+    # also the timed step
+    for marks in events(args.warmup):
         flush.zero_()
         marks[0].record(stream)
-        step()
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+        kernels(marks)
+    kernel_events = events(args.steps)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
     with ClockSampler(local) as clocks:
-        for k in range(args.steps):
+        for marks in kernel_events:
             flush.zero_()
-            marks = events[k]
             marks[0].record(stream)
-            step()
+            kernels(marks)
             marks[2].record(stream)
         torch.cuda.synchronize(device)
+        step_events = None
+        if world > 1:
+            # the sharded step: broadcast / compute / reduce pipeline over the ranks' batches
+            for _ in range(args.warmup):
+                flush.zero_()
+                shard.forward(x)
+            step_events = events(args.steps)
+            dist.barrier()
+            torch.cuda.synchronize(device)
+            for marks in step_events:
+                flush.zero_()
+                marks[0].record(stream)
+                shard.forward(x)
+                marks[2].record(stream)
+            torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
-    up_ms = [e[0].elapsed_time(e[1]) for e in events]
-    down_ms = [e[1].elapsed_time(e[2]) for e in events]
-    step_ms = [e[0].elapsed_time(e[2]) for e in events]
-    total_s = sum(step_ms) / 1e3
+    up_ms = [e[0].elapsed_time(e[1]) for e in kernel_events]
+    down_ms = [e[1].elapsed_time(e[2]) for e in kernel_events]
+    step_ms = [e[0].elapsed_time(e[2]) for e in (step_events or kernel_events)]
 
     # end to end through the public API: pinned host x -> device, forward, y -> pinned host, every step
-    y_host = torch.empty(n, case.d_model, dtype=dtype).pin_memory()
+    y_host = torch.empty(n, d, dtype=dtype).pin_memory()
     e2e_ms = []
     for k in range(args.warmup + args.steps):
         flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         x.copy_(x_host, non_blocking=True)
-        y = runtime.forward(0, x)
+        y = runtime.forward(0, x) if world == 1 else shard.forward(x)
         y_host.copy_(y, non_blocking=True)
         b.record(stream)
         b.synchronize()
         if k >= args.warmup:
             e2e_ms.append(a.elapsed_time(b))
-    e2e_s = sum(e2e_ms) / 1e3
-
-    times = torch.tensor([total_s, e2e_s], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    total_s, e2e_s = float(times[0]), float(times[1])
+    total_s, e2e_s = max_over_ranks(torch, [sum(step_ms) / 1e3, sum(e2e_ms) / 1e3], world, device)
     pk, pk_source = peaks()
     fp32_peak = fp32_gemm_peak(torch) if rank == 0 else None
+    errors = runtime.device_errors()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return None
-    elem = 4 if dtype == torch.float32 else 2
-    alg = algorithmic(case, n, elem)
+    local_case = type(case)(case.name, d, f_local, case.up_degree, case.down_degree, False, case.seed)
+    alg = algorithmic(local_case, n_kernel, elem)
     kernel_ms = {"up": statistics.mean(up_ms), "down": statistics.mean(down_ms)}
     top = max(kernel_ms, key=kernel_ms.get)
     seconds = kernel_ms[top] / 1e3
@@ -295,24 +354,21 @@ def gpu_arm(args, workload: dict) -> dict | None:
     achieved_tflops = alg[top]["flops"] / seconds / 1e12
     hbm = {"achieved_gbs": achieved_gbs, "peak_gbs": pk["hbm_gbs"], "frac": achieved_gbs / pk["hbm_gbs"],
            "algorithmic_bytes": alg[top]["bytes"]}
-    tokens = n * world * args.steps
     if tc:
-        # useful (sparse) FLOPs against the measured dense bf16 tensor peak; executed MMA work beside it
         passes = 3 if elem == 4 else 1
-        rows, cols = (case.d_ff, case.d_model)
-        dense_flops = 2.0 * n * rows * cols * passes
+        dense_flops = 2.0 * n_kernel * f_local * d * passes
         pipe_peak = pk["bf16_tflops"] / (2 if elem == 4 else 1)
-        roofline = {"bound": "tensor", "kernel": f"tc_{top}", "achieved": achieved_tflops, "peak": pk["bf16_tflops"],
-                    "unit": "TFLOP/s", "frac": achieved_tflops / pk["bf16_tflops"], "traffic": None,
-                    "algorithmic_flops": alg[top]["flops"], "launch_ms": kernel_ms[top], "peak_source": pk_source,
+        roofline = {"bound": "tensor", "kernel": f"tc_gemm_{top}", "achieved": achieved_tflops,
+                    "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved_tflops / pk["bf16_tflops"],
+                    "traffic": None, "algorithmic_flops": alg[top]["flops"], "launch_ms": kernel_ms[top],
+                    "peak_source": pk_source,
                     "tensor_pipe": {"kind": "tf32 x3 (3xTF32 split)" if elem == 4 else "bf16",
-                                    "executed_tflops": dense_flops / seconds / 1e12,
-                                    "peak_tflops": pipe_peak,
+                                    "executed_tflops": dense_flops / seconds / 1e12, "peak_tflops": pipe_peak,
                                     "peak_note": "tf32 = half the measured bf16 peak (nominal ratio)" if elem == 4
                                     else "measured bf16 burst",
                                     "frac": dense_flops / seconds / 1e12 / pipe_peak},
                     "hbm": hbm}
-        launches = (3 if elem == 4 else 2) * args.steps
+        launches_per_kernel_step = 3 if elem == 4 else 2
     else:
         roofline = {"bound": "hbm", "kernel": f"{top}_{up if top == 'up' else down}", "achieved": achieved_gbs,
                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved_gbs / pk["hbm_gbs"], "traffic": None,
@@ -320,27 +376,121 @@ def gpu_arm(args, workload: dict) -> dict | None:
                     "fp32_cuda_cores": {"achieved_tflops": achieved_tflops, "peak_tflops": fp32_peak,
                                         "frac": achieved_tflops / fp32_peak if fp32_peak else None,
                                         "peak_source": "cuBLAS SGEMM 8192^3 TF32 off, measured in this run"}}
-        launches = 2 * args.steps
+        launches_per_kernel_step = 2
+    tokens = n * world * args.steps
     line = {
         "metric": f"HFFN FFN layer tokens/s (forward, {workload['dtype']})",
         "value": tokens / total_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * total_s / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32" if elem == 4 else "bf16", "data": "synthetic",
-        "config": {"workload": f"{case.name}: d_model {case.d_model}, d_ff {case.d_ff}, support {case.up_degree}, "
+        "config": {"workload": f"{case.name}: d_model {d}, d_ff {case.d_ff}, support {case.up_degree}, "
                                f"N {n} tokens per GPU per step", "modes": [up, down],
-                   "parallelism": "replicas" if world > 1 else "single", "l2": "flushed between steps (512 MiB write)"},
+                   "parallelism": f"neuron-sharded x{world} (broadcast / reduce over NCCL)" if world > 1 else "single",
+                   "l2": "flushed between steps (512 MiB write)"},
         "roofline": roofline,
         "fp32_gemm_peak_tflops": fp32_peak,
         "kernels_ms": kernel_ms,
-        "e2e": {"value": tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": x_host.numel() * elem,
-                "d2h_bytes_per_step": y_host.numel() * elem},
-        "gpu_launches": launches,
-        "device_errors": runtime.device_errors(),
+        "e2e": {"value": n * world * args.steps / e2e_s, "unit": "tokens/s",
+                "h2d_bytes_per_step": x_host.numel() * elem, "d2h_bytes_per_step": y_host.numel() * elem},
+        "gpu_launches": launches_per_kernel_step * args.steps,
+        "device_errors": errors,
         "clocks": clocks.summary(),
     }
+    if world > 1:
+        line["kernel_loop_ms_per_step"] = statistics.mean(a + b for a, b in zip(up_ms, down_ms))
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(workload, args.cpu_seconds)
     return line
+
+
+def train_arm(args, workload: dict, rank: int, world: int, local: int, device) -> dict | None:
+    """The MSE training step (d_model 2048, d_ff 8192, 80 %, N per GPU), data parallel over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from hffn_b200 import synth
+    from hffn_b200.distributed import DataParallelTrainer
+    from hffn_b200.runtime import HFFNLayer, HFFNRuntime
+    from hffn_b200.train_runtime import HFFNTrainRuntime
+
+    case = synth.CASES[workload["case"]]
+    n = workload["n"]
+    layer = synth.make_layer(case)
+    t = torch.from_numpy
+    kl = HFFNLayer.from_hidden_major(layer.d_model, layer.d_ff, t(layer.b_up), t(layer.up_offsets), t(layer.up_idx),
+                                     t(layer.up_val), t(layer.b_down), t(layer.down_offsets), t(layer.down_idx),
+                                     t(layer.down_val))
+    runtime = HFFNRuntime([kl], device, tensor_cores=False)
+    train = HFFNTrainRuntime(runtime, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-2, max_tokens=n,
+                             store_gradients=world > 1)
+    train.reserve(n)
+    x_host = t(rank_input(case, n, rank)).pin_memory()
+    target_host = t(synth.make_target(case, n) if rank == 0 else rank_input(case, n, rank + 500)).pin_memory()
+    x, target = x_host.to(device), target_host.to(device)
+    dp = DataParallelTrainer(train) if world > 1 else None
+    step = (lambda: dp.step_mse(0, x, target)) if dp else (lambda: train.step_mse(0, x, target))
+    stream = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        step()
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        for a, b in marks:
+            a.record(stream)
+            loss = step()
+            b.record(stream)
+        torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    step_ms = [a.elapsed_time(b) for a, b in marks]
+    loss_host = torch.empty(1, dtype=loss.dtype).pin_memory()
+    e2e_ms = []
+    for _ in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        x.copy_(x_host, non_blocking=True)
+        target.copy_(target_host, non_blocking=True)
+        loss = step()
+        loss_host.copy_(loss, non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        e2e_ms.append(a.elapsed_time(b))
+    total_s, e2e_s = max_over_ranks(torch, [sum(step_ms) / 1e3, sum(e2e_ms) / 1e3], world, device)
+    pk, pk_source = peaks()
+    fp32_peak = fp32_gemm_peak(torch) if rank == 0 else None
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    e = case.d_ff * case.up_degree
+    flops = 12.0 * e * n                       # forward 2 x 2En, backward 2x the forward
+    step_bytes = (4 * n * case.d_model * 4      # x, target, gy, gx
+                  + 2 * case.d_ff * n * 4 * 2   # z written and read
+                  + 2 * e * 6 * 2               # both supports (index + value), forward and backward
+                  + 2 * e * 24)                 # AdamW: p, m, v read and written, both value arrays
+    seconds = total_s / args.steps
+    achieved = step_bytes / seconds / 1e9
+    return {
+        "metric": "HFFN FFN layer tokens/s (train step, fp32)", "value": n * world * args.steps / total_s,
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * seconds, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{case.name}: d_model {case.d_model}, d_ff {case.d_ff}, support {case.up_degree}, "
+                               f"N {n} tokens per GPU per step, MSE loss, AdamW", "path": "cuda_cores",
+                   "parallelism": f"data parallel x{world}, gradient all-reduce over NCCL" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (z and act alone 537 MB)"},
+        "roofline": {"bound": "hbm", "kernel": "whole step", "achieved": achieved, "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                     "algorithmic_bytes": step_bytes, "peak_source": pk_source,
+                     "fp32_cuda_cores": {"achieved_tflops": flops / seconds / 1e12, "peak_tflops": fp32_peak,
+                                         "frac": flops / seconds / 1e12 / fp32_peak if fp32_peak else None}},
+        "e2e": {"value": n * world * args.steps / e2e_s, "unit": "tokens/s",
+                "h2d_bytes_per_step": 2 * x_host.numel() * 4, "d2h_bytes_per_step": loss_host.numel() * 8},
+        "gpu_launches": None, "device_errors": runtime.device_errors(), "clocks": clocks.summary(),
+        "loss_last": float(loss_host),
+    }
 
 
 def main() -> int:

@@ -16,8 +16,8 @@
 // float32 registers with round-to-nearest: the accumulation bias of the tensor core stays bounded by one chunk.
 //
 // Kernel shape: persistent, one CTA per SM, 6 warps: warp 0 issues the TMA loads (one elected thread), warp 1 owns
-// the TMEM allocation and issues the MMAs (one elected thread), warps 2-5 run the epilogue (one TMEM lane = one
-// feature row per thread). Two accumulator buffers in TMEM let the epilogue of one tile overlap the MMAs of the
+// the TMEM allocation and issues the MMAs (one elected thread), warps 2-9 run the epilogue (one TMEM lane = one
+// feature row per thread, two warps per lane quarter splitting the token columns). Two accumulator buffers in TMEM let the epilogue of one tile overlap the MMAs of the
 // next. Shared-memory stages are recycled through mbarriers (full: TMA -> MMA, empty: MMA commit -> TMA); every wait
 // is bounded by a 2 s timer after which the kernel records an error code, stops issuing work, waits (bounded) for its
 // own copies in flight, frees its TMEM and returns. No TMA multicast is used.
@@ -29,7 +29,8 @@
 namespace hffn {
 namespace tc {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;          // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kEpilogueThreads = 256;
 constexpr int BM = 128;                  // features per tile (TMEM lanes)
 constexpr int kRowBytes = 128;           // K extent of one stage: one 128-byte swizzle atom per row
 constexpr uint64_t kWaitNs = 2000000000ull;
@@ -159,10 +160,27 @@ struct EpilogueArgs {
   float* z;           // up fp32, optional: pre-activations [N, M]
 };
 
-template <bool kBf16>
-struct Stage {
-  static constexpr int kParts = kBf16 ? 1 : 2;
-};
+// One value of the output tile: bias added, then (up) GELU and the stores of act (float32: tf32 hi and lo parts) and
+// of z, or (down) the store of y. Out of line: the epilogue calls it once per value, and an inlined copy per value
+// of an unrolled tile overflows the instruction cache.
+template <bool kBf16, int EPI>
+__device__ __noinline__ void emit_value(const EpilogueArgs& epi, int64_t at, float v, float bias) {
+  const float s = v + bias;
+  if constexpr (EPI == kUp) {
+    if (!kBf16 && epi.z) epi.z[at] = s;
+    const float h = gelu(s);
+    if constexpr (kBf16) {
+      reinterpret_cast<__nv_bfloat16*>(epi.out_hi)[at] = __float2bfloat16_rn(h);
+    } else {
+      const float hi = tf32_rna(h);
+      reinterpret_cast<float*>(epi.out_hi)[at] = hi;
+      reinterpret_cast<float*>(epi.out_lo)[at] = tf32_rna(h - hi);
+    }
+  } else {
+    if constexpr (kBf16) reinterpret_cast<__nv_bfloat16*>(epi.out_hi)[at] = __float2bfloat16_rn(s);
+    else reinterpret_cast<float*>(epi.out_hi)[at] = s;
+  }
+}
 
 // Shared memory: [stages][A parts][128 rows x 128 B] then [stages][B parts][BN rows x 128 B], 1024-aligned.
 template <bool kBf16, int BN, int STAGES>
@@ -207,7 +225,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], kEpilogueThreads);
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -339,33 +357,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
       }
     }
   } else {
-    // ---------------- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----------------
-    const int quarter = warp & 3;
-    const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    // ---------------- epilogue: warps 2..9; TMEM lane quarter = warp % 4, column half = (warp - 2) / 4 ----------------
+    constexpr int HALF = BN / 2;
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * HALF;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    // one value of the output tile: bias, then (up) GELU and the stores of act (and z)
-    auto emit = [&](int row, int t, float v, float bias) {
-      const int64_t at = (int64_t)t * M + row;
-      const float s = v + bias;
-      if constexpr (EPI == kUp) {
-        if (!kBf16 && epi.z) epi.z[at] = s;
-        const float h = gelu(s);
-        if constexpr (kBf16) {
-          reinterpret_cast<__nv_bfloat16*>(epi.out_hi)[at] = __float2bfloat16_rn(h);
-        } else {
-          const float hi = tf32_rna(h);
-          reinterpret_cast<float*>(epi.out_hi)[at] = hi;
-          reinterpret_cast<float*>(epi.out_lo)[at] = tf32_rna(h - hi);
-        }
-      } else {
-        if constexpr (kBf16) reinterpret_cast<__nv_bfloat16*>(epi.out_hi)[at] = __float2bfloat16_rn(s);
-        else reinterpret_cast<float*>(epi.out_hi)[at] = s;
-      }
-    };
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
+      const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN + half * HALF;
       const int row = m0 + quarter * 32 + lane;
       float bias = 0.f;
       if (row < M) {
@@ -374,9 +374,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
       }
       if constexpr (KCHUNK > 0) {
         // chunk partials summed in registers, chunk after chunk, round-to-nearest
-        float sum[BN];
+        float sum[HALF];
 #pragma unroll
-        for (int i = 0; i < BN; ++i) sum[i] = 0.f;
+        for (int i = 0; i < HALF; ++i) sum[i] = 0.f;
         for (int kc = 0; kc < num_kb; kc += KCHUNK) {
           if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, kWaitNs)) {
             ok = false;
@@ -384,7 +384,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
           }
           fence_after();
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c) {
+          for (int c = 0; c < HALF / 32; ++c) {
             float v[32];
             tmem_ld32(lane_base + acc * BN + c * 32, v);
 #pragma unroll
@@ -400,8 +400,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
         if (!ok) break;
         if (row < M) {
 #pragma unroll
-          for (int i = 0; i < BN; ++i)
-            if (n0 + i < N) emit(row, n0 + i, sum[i], bias);
+          for (int i = 0; i < HALF; ++i)
+            if (n0 + i < N) emit_value<kBf16, EPI>(epi, (int64_t)(n0 + i) * M + row, sum[i], bias);
         }
       } else {
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, kWaitNs)) {
@@ -409,13 +409,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
           break;
         }
         fence_after();
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < HALF / 32; ++c) {
           float v[32];
           tmem_ld32(lane_base + acc * BN + c * 32, v);
           if (row < M) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (n0 + c * 32 + j < N) emit(row, n0 + c * 32 + j, v[j], bias);
+              if (n0 + c * 32 + j < N) emit_value<kBf16, EPI>(epi, (int64_t)(n0 + c * 32 + j) * M + row, v[j], bias);
           }
         }
         fence_before();

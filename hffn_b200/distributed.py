@@ -1,0 +1,148 @@
+"""Multi-GPU HFFN on one box: hidden neurons sharded across ranks for inference, data parallelism for training.
+
+One process per GPU, ``torch.distributed`` for the plumbing (NCCL over NVLink on GPUs; gloo on CPU for the tests).
+
+Inference (the north star's natural shard). Rank k owns a contiguous range of hidden neurons, balanced by edge
+count (up + down slots) and rounded to multiples of 8 so that every shard keeps the tensor-core path: its up slots
+and biases, and the down edges of its neurons only (re-sorted output-major by ``HFFNLayer.from_hidden_major``).
+``b_down`` is added by rank 0 only, so the sum over ranks of the partial outputs is the layer's output. Two forms:
+- ``forward_replicated(x)``: x identical on every rank (already broadcast); partial y all-reduced; every rank gets y.
+- ``forward(x_local)``: weak scaling, each rank holds its own batch. The batch of rank c is broadcast from c, every
+  rank runs its neuron shard on it and the partial outputs are reduced to rank c, chunk after chunk; the collectives
+  are queued asynchronously so that the broadcast of the next chunk and the reduction of the previous one overlap
+  the compute of the current one. Every rank returns y of its own batch.
+Training: data parallel over tokens with full compact replicas (``DataParallelTrainer``): forward, MSE loss on the
+rank's tokens, backward with the gradients stored, one all-reduce (sum) of the four compact gradient arrays scaled
+by 1 / world (the mean over all tokens), then AdamW. The fused backward + AdamW of one GPU does not apply: the update
+must wait for the exchange.
+
+Every rank calls the same collectives in the same order, in warm-up and in timing.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+GRANULE = 8
+
+
+def balanced_partition(cost: torch.Tensor, parts: int, granule: int = GRANULE) -> list[int]:
+    """Offsets ``[0 = b_0 <= b_1 <= ... <= b_parts = len(cost)]`` of contiguous groups of nearly equal total cost; inner
+    boundaries are multiples of ``granule`` (the last group takes the remainder)."""
+    count = int(cost.numel())
+    cumulative = torch.cumsum(cost.to(torch.float64), 0)
+    total = float(cumulative[-1]) if count else 0.0
+    bounds = [0]
+    for k in range(1, parts):
+        target = total * k / parts
+        cut = int(torch.searchsorted(cumulative, torch.tensor(target, dtype=torch.float64))) + 1
+        cut = min(count, max(bounds[-1], int(round(cut / granule)) * granule))
+        bounds.append(cut)
+    bounds.append(count)
+    return bounds
+
+
+def shard_hidden_major(d_model: int, arrays: dict, lo: int, hi: int, with_bias: bool) -> dict:
+    """The canonical hidden-major arrays of neurons ``[lo, hi)``: offsets rebased to 0, ``b_down`` zeroed unless
+    ``with_bias``. ``arrays`` holds ``b_up, up_offsets, up_idx, up_val, b_down, down_offsets, down_idx, down_val``."""
+    up_off, dn_off = arrays["up_offsets"], arrays["down_offsets"]
+    u0, u1 = int(up_off[lo]), int(up_off[hi])
+    d0, d1 = int(dn_off[lo]), int(dn_off[hi])
+    b_down = arrays["b_down"].clone() if with_bias else torch.zeros_like(arrays["b_down"])
+    return {"d_model": d_model, "d_ff": hi - lo, "b_up": arrays["b_up"][lo:hi].clone(),
+            "up_offsets": (up_off[lo:hi + 1] - u0).to(torch.int32), "up_idx": arrays["up_idx"][u0:u1].clone(),
+            "up_val": arrays["up_val"][u0:u1].clone(), "b_down": b_down,
+            "down_offsets": (dn_off[lo:hi + 1] - d0).to(torch.int32), "down_idx": arrays["down_idx"][d0:d1].clone(),
+            "down_val": arrays["down_val"][d0:d1].clone()}
+
+
+def neuron_partition(arrays: dict, world: int) -> list[int]:
+    cost = arrays["up_offsets"].diff().long() + arrays["down_offsets"].diff().long()
+    return balanced_partition(cost, world)
+
+
+class ShardedFFN:
+    """The collectives of the neuron-sharded forward around a rank-local forward ``local_forward(x) -> partial y``
+    (the rank's neuron shard, ``b_down`` on rank 0 only). ``group`` None: the default process group."""
+
+    def __init__(self, local_forward: Callable[[torch.Tensor], torch.Tensor], d_model: int, group=None) -> None:
+        self.local_forward = local_forward
+        self.d_model = d_model
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self._ranks = [dist.get_global_rank(group, k) if group is not None else k for k in range(self.world)]
+
+    def forward_replicated(self, x: torch.Tensor) -> torch.Tensor:
+        """``y`` of an ``x`` that every rank holds: partial outputs all-reduced (sum)."""
+        y = self.local_forward(x).clone()
+        dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
+        return y
+
+    def forward(self, x_local: torch.Tensor) -> torch.Tensor:
+        """``y`` of this rank's own batch ``x_local`` (every rank passes a batch of the same shape)."""
+        n = x_local.shape[0]
+        chunks = [x_local if c == self.rank else torch.empty_like(x_local) for c in range(self.world)]
+        pending = [dist.broadcast(chunks[c], src=self._ranks[c], group=self.group, async_op=True)
+                   for c in range(self.world)]
+        out = torch.empty(n, self.d_model, dtype=x_local.dtype, device=x_local.device)
+        partials, reductions = [], []
+        for c in range(self.world):
+            pending[c].wait()
+            partial = self.local_forward(chunks[c]).clone()
+            partials.append(partial)
+            reductions.append(dist.reduce(partial, dst=self._ranks[c], op=dist.ReduceOp.SUM, group=self.group,
+                                          async_op=True))
+        for c, work in enumerate(reductions):
+            work.wait()
+            if c == self.rank:
+                out.copy_(partials[c])
+        return out
+
+
+def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, tensor_cores=None, group=None):
+    """The rank's ``HFFNRuntime`` over its neuron shard and the ``ShardedFFN`` around it."""
+    from .runtime import HFFNLayer, HFFNRuntime
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    bounds = neuron_partition(arrays, world)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    if hi <= lo:
+        raise ValueError(f"rank {rank} owns no hidden neuron (d_ff {arrays['b_up'].numel()} over {world} ranks)")
+    shard = shard_hidden_major(d_model, arrays, lo, hi, with_bias=rank == 0)
+    layer = HFFNLayer.from_hidden_major(shard["d_model"], shard["d_ff"], shard["b_up"], shard["up_offsets"],
+                                        shard["up_idx"], shard["up_val"], shard["b_down"], shard["down_offsets"],
+                                        shard["down_idx"], shard["down_val"])
+    runtime = HFFNRuntime([layer], device, dtype, tensor_cores=tensor_cores)
+    return runtime, ShardedFFN(lambda x: runtime.forward(0, x), d_model, group), (lo, hi)
+
+
+class DataParallelTrainer:
+    """Data-parallel MSE training step over an ``HFFNTrainRuntime`` replica per rank."""
+
+    def __init__(self, train, group=None) -> None:
+        self.train = train
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self._loss = torch.zeros(1, dtype=torch.float64, device=train.runtime.device)
+
+    def step_mse(self, index: int, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+        """One step on this rank's tokens; returns the mean loss over all ranks' tokens (before the update)."""
+        from . import _native as native
+        train = self.train
+        n = train._check_tokens(target, "target")
+        y = train.forward(index, x, train._z)
+        gy = train._gy[:n]
+        native.check(native.lib.hffn_mse(y.data_ptr(), target.data_ptr(), gy.data_ptr(), train._loss.data_ptr(), n,
+                                         train.d_model, train._work.data_ptr(),
+                                         native.stream_handle(train.runtime.device)), "hffn_mse")
+        train.backward(index, gy)
+        grads = train.gradients(index)
+        for name in ("up_val", "b_up", "out_val", "b_down"):
+            dist.all_reduce(grads[name], op=dist.ReduceOp.SUM, group=self.group)
+            grads[name].mul_(1.0 / self.world)
+        train.adamw(index)
+        self._loss.copy_(train._loss)
+        dist.all_reduce(self._loss, op=dist.ReduceOp.SUM, group=self.group)
+        return self._loss / self.world

@@ -1,0 +1,96 @@
+"""CPU, gloo, world size 2: the neuron-sharded forward's partition and collectives (hffn_b200.distributed).
+
+Each rank runs its neuron shard through the float64 oracle (standing in for the GPU kernels, which need a B200);
+the collectives are the product's. The sum over ranks of the shard outputs must equal the whole layer's output,
+for a replicated batch (all-reduce) and for per-rank batches (broadcast / reduce pipeline)."""
+import os
+import socket
+import types
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from hffn_b200 import synth
+from hffn_b200.distributed import balanced_partition, neuron_partition, shard_hidden_major
+
+
+def canonical(layer) -> dict:
+    t = torch.from_numpy
+    return {k: t(getattr(layer, k).copy()) for k in ("b_up", "up_offsets", "up_idx", "up_val", "b_down",
+                                                       "down_offsets", "down_idx", "down_val")}
+
+
+def as_layer(shard: dict):
+    return types.SimpleNamespace(d_model=shard["d_model"], d_ff=shard["d_ff"],
+                                 **{k: v.numpy() for k, v in shard.items() if isinstance(v, torch.Tensor)})
+
+
+def test_balanced_partition():
+    cost = torch.tensor([5, 1, 1, 1, 9, 0, 0, 3] * 16)
+    bounds = balanced_partition(cost, 4)
+    assert bounds[0] == 0 and bounds[-1] == cost.numel() and bounds == sorted(bounds)
+    assert all(b % 8 == 0 for b in bounds[:-1])
+    shares = [int(cost[a:b].sum()) for a, b in zip(bounds, bounds[1:])]
+    assert max(shares) - min(shares) <= 2 * 20      # within one granule of cost of each other
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_shards_sum_to_layer(world):
+    from oracle import forward64
+    case = synth.TEST_CASES["irreg_512_2048"]
+    layer = synth.make_layer(case)
+    arrays = canonical(layer)
+    bounds = neuron_partition(arrays, world)
+    x = synth.make_input(case, 5)
+    total = sum(forward64.forward(as_layer(shard_hidden_major(layer.d_model, arrays, lo, hi, k == 0)), x)
+                for k, (lo, hi) in enumerate(zip(bounds, bounds[1:])))
+    assert np.allclose(total, forward64.forward(layer, x), rtol=0, atol=1e-12)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, results) -> None:
+    import torch.distributed as dist
+
+    from hffn_b200.distributed import ShardedFFN
+    from oracle import forward64
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        case = synth.TEST_CASES["homog_256_1024"]
+        layer = synth.make_layer(case)
+        arrays = canonical(layer)
+        bounds = neuron_partition(arrays, world)
+        shard = as_layer(shard_hidden_major(layer.d_model, arrays, bounds[rank], bounds[rank + 1], rank == 0))
+        ffn = ShardedFFN(lambda x: torch.from_numpy(forward64.forward(shard, x.numpy())), layer.d_model)
+        x_shared = torch.from_numpy(synth.make_input(case, 6)).double()
+        y_rep = ffn.forward_replicated(x_shared)
+        x_own = torch.from_numpy(synth.make_input(case, 7 + 100 * rank)[:7]).double()
+        y_own = ffn.forward(x_own)
+        ok_rep = np.allclose(y_rep.numpy(), forward64.forward(layer, x_shared.numpy()), atol=1e-12, rtol=0)
+        ok_own = np.allclose(y_own.numpy(), forward64.forward(layer, x_own.numpy()), atol=1e-12, rtol=0)
+        results[rank] = (ok_rep, ok_own)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gloo_two_ranks():
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(rank, 2, port, results)) for rank in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert dict(results) == {0: (True, True), 1: (True, True)}

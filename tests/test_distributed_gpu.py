@@ -1,0 +1,107 @@
+"""GPU, NCCL, 2 ranks (skipped with fewer than 2 GPUs): the neuron-sharded forward and the data-parallel training
+step against one GPU.
+
+Sharded forward (both the replicated and the per-rank-batch forms, tensor cores and CUDA cores) equals the single-GPU
+runtime's output within the forward tolerance (the partial sums are added in another order). The data-parallel MSE
+step of two ranks equals, after the update, a single-GPU step on the concatenation of their batches within float32
+tolerance."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _kernel_layer(layer):
+    from hffn_b200.runtime import HFFNLayer
+    t = torch.from_numpy
+    return HFFNLayer.from_hidden_major(layer.d_model, layer.d_ff, t(layer.b_up), t(layer.up_offsets), t(layer.up_idx),
+                                       t(layer.up_val), t(layer.b_down), t(layer.down_offsets), t(layer.down_idx),
+                                       t(layer.down_val))
+
+
+def _worker(rank: int, world: int, port: int, results) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    from hffn_b200 import synth
+    from hffn_b200.distributed import DataParallelTrainer, sharded_runtime
+    from hffn_b200.runtime import HFFNRuntime
+    from hffn_b200.train_runtime import HFFNTrainRuntime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=device,
+                            timeout=datetime.timedelta(seconds=120))
+    out = {}
+    try:
+        case = synth.TEST_CASES["irreg_512_2048"]
+        layer = synth.make_layer(case)
+        arrays = {k: torch.from_numpy(getattr(layer, k).copy()) for k in
+                  ("b_up", "up_offsets", "up_idx", "up_val", "b_down", "down_offsets", "down_idx", "down_val")}
+        full = HFFNRuntime([_kernel_layer(layer)], device)
+        for tensor_cores in (True, False):
+            runtime, ffn, _ = sharded_runtime(layer.d_model, arrays, device, tensor_cores=tensor_cores)
+            x_shared = torch.from_numpy(synth.make_input(case, 300)).to(device)
+            y_rep = ffn.forward_replicated(x_shared)
+            expected = full.forward(0, x_shared).double()
+            rel_rep = float(((y_rep.double() - expected).abs() / expected.abs().clamp(min=1)).max())
+            x_own = torch.from_numpy(synth.make_input(case, 260 + rank)[:260]).to(device)
+            y_own = ffn.forward(x_own)
+            expected = full.forward(0, x_own).double()
+            rel_own = float(((y_own.double() - expected).abs() / expected.abs().clamp(min=1)).max())
+            out[f"sharded_tc{int(tensor_cores)}"] = max(rel_rep, rel_own)
+            out[f"errors_tc{int(tensor_cores)}"] = runtime.device_errors()
+
+        # data-parallel training: 2 x 64 tokens against one GPU on the 128 concatenated tokens
+        n = 64
+        xs = [synth.make_input(case, 128)[k * n:(k + 1) * n] for k in range(world)]
+        ts = [synth.make_target(case, 128)[k * n:(k + 1) * n] for k in range(world)]
+        dp_train = HFFNTrainRuntime(HFFNRuntime([_kernel_layer(layer)], device, tensor_cores=False), max_tokens=n)
+        dp = DataParallelTrainer(dp_train)
+        loss = float(dp.step_mse(0, torch.from_numpy(xs[rank]).to(device), torch.from_numpy(ts[rank]).to(device)))
+        one = HFFNTrainRuntime(HFFNRuntime([_kernel_layer(layer)], device, tensor_cores=False), max_tokens=2 * n)
+        loss_one = float(one.step_mse(0, torch.from_numpy(np.concatenate(xs)).to(device),
+                                      torch.from_numpy(np.concatenate(ts)).to(device)))
+        worst = 0.0
+        for name, p in dp_train.parameters(0).items():
+            q = one.parameters(0)[name]
+            worst = max(worst, float(((p - q).abs() / q.abs().clamp(min=1e-3)).max()))
+        out["dp_param_rel"] = worst
+        out["dp_loss_rel"] = abs(loss - loss_one) / loss_one
+        results[rank] = out
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_ranks():
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(rank, 2, port, results)) for rank in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for rank in range(2):
+        r = results[rank]
+        assert r["sharded_tc1"] <= 1e-5 and r["sharded_tc0"] <= 1e-5, r
+        assert r["errors_tc1"] == 0 and r["errors_tc0"] == 0, r
+        assert r["dp_param_rel"] <= 1e-5 and r["dp_loss_rel"] <= 1e-5, r
