@@ -29,10 +29,9 @@
 namespace hffn {
 namespace tc {
 
-constexpr int kThreads = 320;          // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
-constexpr int kEpilogueThreads = 256;
+// warp 0 TMA, warp 1 MMA, then EW epilogue warps (EW / 4 per TMEM lane quarter, splitting the token columns)
+__host__ __device__ constexpr int threads_for(int ew) { return 64 + 32 * ew; }
 constexpr int BM = 128;                  // features per tile (TMEM lanes)
-constexpr int kRowBytes = 128;           // K extent of one stage: one 128-byte swizzle atom per row
 constexpr uint64_t kWaitNs = 2000000000ull;
 
 enum Epilogue { kUp = 0, kDown = 1 };
@@ -95,11 +94,15 @@ __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
-// Shared-memory matrix descriptor of a K-major operand tile in the 128-byte swizzle layout written by TMA:
-// rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte offset), descriptor version 1, layout type 2.
+// Shared-memory matrix descriptor of a K-major operand tile in the swizzle layout TMA writes for rows of RB bytes
+// (RB = 128: 128-byte swizzle, layout type 2; RB = 64: 64-byte swizzle, layout type 4): 8-row groups 8 x RB bytes
+// apart (stride byte offset), descriptor version 1.
+template <int RB>
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
-  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
-         ((uint64_t)2 << 61);
+  static_assert(RB == 128 || RB == 64, "row bytes");
+  constexpr uint64_t layout = RB == 128 ? 2 : 4;
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)((8 * RB) >> 4) << 32) |
+         ((uint64_t)1 << 46) | (layout << 61);
 }
 
 // Instruction descriptor: fp32 accumulator, A/B format (tf32 = 2, bf16 = 1), both K-major, N = bn, M = 128.
@@ -164,30 +167,30 @@ struct EpilogueArgs {
 // of z, or (down) the store of y. Out of line: the epilogue calls it once per value, and an inlined copy per value
 // of an unrolled tile overflows the instruction cache.
 template <bool kBf16, int EPI>
-__device__ __noinline__ void emit_value(const EpilogueArgs& epi, int64_t at, float v, float bias) {
+__device__ __noinline__ void emit_value(void* out_hi, void* out_lo, float* z, int64_t at, float v, float bias) {
   const float s = v + bias;
   if constexpr (EPI == kUp) {
-    if (!kBf16 && epi.z) epi.z[at] = s;
+    if (!kBf16 && z) z[at] = s;
     const float h = gelu(s);
     if constexpr (kBf16) {
-      reinterpret_cast<__nv_bfloat16*>(epi.out_hi)[at] = __float2bfloat16_rn(h);
+      reinterpret_cast<__nv_bfloat16*>(out_hi)[at] = __float2bfloat16_rn(h);
     } else {
       const float hi = tf32_rna(h);
-      reinterpret_cast<float*>(epi.out_hi)[at] = hi;
-      reinterpret_cast<float*>(epi.out_lo)[at] = tf32_rna(h - hi);
+      reinterpret_cast<float*>(out_hi)[at] = hi;
+      reinterpret_cast<float*>(out_lo)[at] = tf32_rna(h - hi);
     }
   } else {
-    if constexpr (kBf16) reinterpret_cast<__nv_bfloat16*>(epi.out_hi)[at] = __float2bfloat16_rn(s);
-    else reinterpret_cast<float*>(epi.out_hi)[at] = s;
+    if constexpr (kBf16) reinterpret_cast<__nv_bfloat16*>(out_hi)[at] = __float2bfloat16_rn(s);
+    else reinterpret_cast<float*>(out_hi)[at] = s;
   }
 }
 
 // Shared memory: [stages][A parts][128 rows x 128 B] then [stages][B parts][BN rows x 128 B], 1024-aligned.
-template <bool kBf16, int BN, int STAGES>
+template <bool kBf16, int BN, int STAGES, int RB>
 struct Layout {
   static constexpr int kParts = kBf16 ? 1 : 2;
-  static constexpr int kA = BM * kRowBytes;
-  static constexpr int kB = BN * kRowBytes;
+  static constexpr int kA = BM * RB;
+  static constexpr int kB = BN * RB;
   static constexpr int kStageBytes = kParts * (kA + kB);
   static constexpr int kOperandBytes = STAGES * kStageBytes;
   static constexpr int kBarrierBytes = 8 * (2 * STAGES + 5) + 16;
@@ -195,12 +198,13 @@ struct Layout {
   static constexpr int kTmemCols = 2 * BN;
 };
 
-template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK>
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK, int RB, int EW>
+__global__ void __launch_bounds__(threads_for(EW), 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_a_lo,
                const __grid_constant__ CUtensorMap map_b_hi, const __grid_constant__ CUtensorMap map_b_lo, int M,
                int N, int K, EpilogueArgs epi, int* err) {
-  using L = Layout<kBf16, BN, STAGES>;
+  using L = Layout<kBf16, BN, STAGES, RB>;
+  constexpr int kRowBytes = RB;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* a_base = smem;
@@ -225,7 +229,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpilogueThreads);
+      mbar_init(&tempty[a], 32 * EW);
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -324,10 +328,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
 #pragma unroll
             for (int k = 0; k < kRowBytes / 32; ++k) {
               const uint32_t acc_in = (kb != kc || k != 0) ? 1u : 0u;
-              const uint64_t ah = smem_desc(a + 32 * k), bh = smem_desc(b + 32 * k);
+              const uint64_t ah = smem_desc<RB>(a + 32 * k), bh = smem_desc<RB>(b + 32 * k);
               mma<kBf16>(d_tmem, ah, bh, idesc, acc_in);
               if (!kBf16) {
-                const uint64_t al = smem_desc(a + L::kA + 32 * k), bl = smem_desc(b + L::kB + 32 * k);
+                const uint64_t al = smem_desc<RB>(a + L::kA + 32 * k), bl = smem_desc<RB>(b + L::kB + 32 * k);
                 mma<kBf16>(d_tmem, ah, bl, idesc, 1);
                 mma<kBf16>(d_tmem, al, bh, idesc, 1);
               }
@@ -357,8 +361,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
       }
     }
   } else {
-    // ---------------- epilogue: warps 2..9; TMEM lane quarter = warp % 4, column half = (warp - 2) / 4 ----------------
-    constexpr int HALF = BN / 2;
+    // ---------------- epilogue: warps 2 .. EW + 1; TMEM lane quarter = warp % 4, column part = (warp - 2) / 4 ----------
+    constexpr int HALF = BN / (EW / 4);
+    static_assert(HALF % 32 == 0, "column part of an epilogue warp");
+    void* const out_hi = epi.out_hi;
+    void* const out_lo = epi.out_lo;
+    float* const zp = epi.z;
     const int quarter = warp & 3, half = (warp - 2) >> 2;
     const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * HALF;
     int acc = 0;
@@ -401,7 +409,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
         if (row < M) {
 #pragma unroll
           for (int i = 0; i < HALF; ++i)
-            if (n0 + i < N) emit_value<kBf16, EPI>(epi, (int64_t)(n0 + i) * M + row, sum[i], bias);
+            if (n0 + i < N) emit_value<kBf16, EPI>(out_hi, out_lo, zp, (int64_t)(n0 + i) * M + row, sum[i], bias);
         }
       } else {
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, kWaitNs)) {
@@ -415,7 +423,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
           if (row < M) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (n0 + c * 32 + j < N) emit_value<kBf16, EPI>(epi, (int64_t)(n0 + c * 32 + j) * M + row, v[j], bias);
+              if (n0 + c * 32 + j < N) emit_value<kBf16, EPI>(out_hi, out_lo, zp, (int64_t)(n0 + c * 32 + j) * M + row, v[j], bias);
           }
         }
         fence_before();
@@ -490,7 +498,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // [rows, k] K-major operand, box = (128 bytes of K) x box_rows, 128-byte swizzle, zero fill outside.
-static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, bool bf16, int box_rows) {
+static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, bool bf16, int box_rows,
+                    int row_bytes) {
   auto fn = encode_fn();
   if (fn == nullptr) {
     set_error("cuTensorMapEncodeTiled unavailable");
@@ -499,11 +508,12 @@ static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k,
   const int elem = bf16 ? 2 : 4;
   cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(k * elem)};
-  cuuint32_t box[2] = {(cuuint32_t)(kRowBytes / elem), (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)(row_bytes / elem), (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d) for a [%lld, %lld] operand", (int)r, (long long)rows, (long long)k);
     return HFFN_ERR_CUDA;
@@ -522,21 +532,21 @@ static int sm_count() {
   return count;
 }
 
-template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK>
+template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK, int RB, int EW>
 static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N, int K,
                        const EpilogueArgs& epi, int* err, cudaStream_t s) {
-  using L = Layout<kBf16, BN, STAGES>;
+  using L = Layout<kBf16, BN, STAGES, RB>;
   CUtensorMap ma_hi, ma_lo, mb_hi, mb_lo;
-  HFFN_TRY(make_map(&ma_hi, a_hi, M, K, kBf16, BM));
-  HFFN_TRY(make_map(&mb_hi, b_hi, N, K, kBf16, BN));
+  HFFN_TRY(make_map(&ma_hi, a_hi, M, K, kBf16, BM, RB));
+  HFFN_TRY(make_map(&mb_hi, b_hi, N, K, kBf16, BN, RB));
   if (!kBf16) {
-    HFFN_TRY(make_map(&ma_lo, a_lo, M, K, kBf16, BM));
-    HFFN_TRY(make_map(&mb_lo, b_lo, N, K, kBf16, BN));
+    HFFN_TRY(make_map(&ma_lo, a_lo, M, K, kBf16, BM, RB));
+    HFFN_TRY(make_map(&mb_lo, b_lo, N, K, kBf16, BN, RB));
   } else {
     ma_lo = ma_hi;
     mb_lo = mb_hi;
   }
-  auto kernel = tc_gemm_kernel<kBf16, BN, STAGES, EPI, KCHUNK>;
+  auto kernel = tc_gemm_kernel<kBf16, BN, STAGES, EPI, KCHUNK, RB, EW>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
@@ -544,24 +554,26 @@ static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, con
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kernel<<<grid, kThreads, L::kTotal, s>>>(ma_hi, ma_lo, mb_hi, mb_lo, M, N, K, epi, err);
+  kernel<<<grid, threads_for(EW), L::kTotal, s>>>(ma_hi, ma_lo, mb_hi, mb_lo, M, N, K, epi, err);
   return launch_status(EPI == kUp ? "tc_up" : "tc_down");
 }
 
 }  // namespace tc
 
-// Tile shapes: float32 (3xTF32) BN = 128 with 3 stages (64 KB each); bfloat16 BN = 256 with 4 stages (48 KB each).
+// Tile shapes: float32 (3xTF32) 128 x 256 tiles, stages of 16 K values (64-byte rows, 48 KB: A hi/lo + B hi/lo), 4
+// stages, 8 epilogue warps; bfloat16 128 x 256 tiles, stages of 64 K values (128-byte rows, 48 KB), 4 stages,
+// 16 epilogue warps.
 // float32 accumulation: the tensor cores' fp32 accumulation in TMEM is not round-to-nearest at every add (measured
 // here: results biased toward zero by ~1e-5 relative over ~400 MMAs), so the K loop runs in chunks of kFp32Chunk
 // k-blocks (64 K values, 24 MMAs) into fresh accumulators whose values the epilogue adds in float32 registers.
-constexpr int kFp32Chunk = 2;
+constexpr int kFp32Chunk = 4;
 // up: x [n, d] -> act [n, H] token-major (fp32: the split x_hi / x_lo [n, d] go to x_split, act as hi / lo parts).
 int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const void* b, void* act_hi, void* act_lo,
           float* z, void* x_split, int* err, int d, int H, int64_t n, cudaStream_t s) {
   const int nn = (int)n;
   if (dtype == HFFN_BF16) {
     tc::EpilogueArgs up{b, act_hi, nullptr, nullptr};
-    return tc::launch_gemm<true, 256, 4, tc::kUp, 0>(w_hi, nullptr, x, nullptr, H, nn, d, up, err, s);
+    return tc::launch_gemm<true, 256, 4, tc::kUp, 0, 128, 16>(w_hi, nullptr, x, nullptr, H, nn, d, up, err, s);
   }
   float* x_hi = reinterpret_cast<float*>(x_split);
   float* x_lo = x_hi + (int64_t)n * d;
@@ -571,7 +583,7 @@ int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const vo
                                           reinterpret_cast<float4*>(x_lo), count4);
   HFFN_TRY(launch_status("tc_split"));
   tc::EpilogueArgs up{b, act_hi, act_lo, z};
-  return tc::launch_gemm<false, 128, 3, tc::kUp, kFp32Chunk>(w_hi, w_lo, x_hi, x_lo, H, nn, d, up, err, s);
+  return tc::launch_gemm<false, 256, 4, tc::kUp, kFp32Chunk, 64, 8>(w_hi, w_lo, x_hi, x_lo, H, nn, d, up, err, s);
 }
 
 // down: act [n, H] token-major -> y [n, d].
@@ -579,8 +591,8 @@ int tc_down(int dtype, const void* act_hi, const void* act_lo, const void* w_hi,
             void* y, int* err, int d, int H, int64_t n, cudaStream_t s) {
   const int nn = (int)n;
   tc::EpilogueArgs dn{b, y, nullptr, nullptr};
-  if (dtype == HFFN_BF16) return tc::launch_gemm<true, 256, 4, tc::kDown, 0>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s);
-  return tc::launch_gemm<false, 128, 3, tc::kDown, kFp32Chunk>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err, s);
+  if (dtype == HFFN_BF16) return tc::launch_gemm<true, 256, 4, tc::kDown, 0, 128, 16>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s);
+  return tc::launch_gemm<false, 256, 4, tc::kDown, kFp32Chunk, 64, 8>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err, s);
 }
 
 // Workspace of the whole forward: fp32 [x_hi, x_lo (n d each), act_hi, act_lo (n H each)] floats; bf16 act [n, H].
