@@ -167,8 +167,7 @@ struct EpilogueArgs {
 // of z, or (down) the store of y. Out of line: the epilogue calls it once per value, and an inlined copy per value
 // of an unrolled tile overflows the instruction cache.
 template <bool kBf16, int EPI>
-__device__ __noinline__ void emit_value(void* out_hi, void* out_lo, float* z, int64_t at, float v, float bias) {
-  const float s = v + bias;
+__device__ __forceinline__ void emit_one(void* out_hi, void* out_lo, float* z, int64_t at, float s) {
   if constexpr (EPI == kUp) {
     if (!kBf16 && z) z[at] = s;
     const float h = gelu(s);
@@ -183,6 +182,25 @@ __device__ __noinline__ void emit_value(void* out_hi, void* out_lo, float* z, in
     if constexpr (kBf16) reinterpret_cast<__nv_bfloat16*>(out_hi)[at] = __float2bfloat16_rn(s);
     else reinterpret_cast<float*>(out_hi)[at] = s;
   }
+}
+
+// Four values of one output row (tokens t0 .. t0 + 3, count of them valid): bias added, then (up) GELU and the stores
+// of act (float32: tf32 hi and lo parts) and z, or (down) the store of y. Out of line: the epilogue calls it once
+// per 4 values (an inlined copy per value of an unrolled tile overflows the instruction cache); the four values are
+// independent, so their GELU chains interleave.
+template <bool kBf16, int EPI>
+__device__ __noinline__ void emit4(void* out_hi, void* out_lo, float* z, int64_t at, int64_t stride, int count,
+                                   float bias, float v0, float v1, float v2, float v3) {
+  if (count >= 4) {
+    emit_one<kBf16, EPI>(out_hi, out_lo, z, at, v0 + bias);
+    emit_one<kBf16, EPI>(out_hi, out_lo, z, at + stride, v1 + bias);
+    emit_one<kBf16, EPI>(out_hi, out_lo, z, at + 2 * stride, v2 + bias);
+    emit_one<kBf16, EPI>(out_hi, out_lo, z, at + 3 * stride, v3 + bias);
+    return;
+  }
+  if (count > 0) emit_one<kBf16, EPI>(out_hi, out_lo, z, at, v0 + bias);
+  if (count > 1) emit_one<kBf16, EPI>(out_hi, out_lo, z, at + stride, v1 + bias);
+  if (count > 2) emit_one<kBf16, EPI>(out_hi, out_lo, z, at + 2 * stride, v2 + bias);
 }
 
 // Shared memory: [stages][A parts][128 rows x 128 B] then [stages][B parts][BN rows x 128 B], 1024-aligned.
@@ -408,8 +426,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
         if (!ok) break;
         if (row < M) {
 #pragma unroll
-          for (int i = 0; i < HALF; ++i)
-            if (n0 + i < N) emit_value<kBf16, EPI>(out_hi, out_lo, zp, (int64_t)(n0 + i) * M + row, sum[i], bias);
+          for (int i = 0; i < HALF; i += 4)
+            if (n0 + i < N)
+              emit4<kBf16, EPI>(out_hi, out_lo, zp, (int64_t)(n0 + i) * M + row, M, N - (n0 + i), bias, sum[i],
+                                sum[i + 1], sum[i + 2], sum[i + 3]);
         }
       } else {
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, kWaitNs)) {
@@ -422,8 +442,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
           tmem_ld32(lane_base + acc * BN + c * 32, v);
           if (row < M) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + c * 32 + j < N) emit_value<kBf16, EPI>(out_hi, out_lo, zp, (int64_t)(n0 + c * 32 + j) * M + row, v[j], bias);
+            for (int j = 0; j < 32; j += 4) {
+              const int t = n0 + c * 32 + j;
+              if (t < N)
+                emit4<kBf16, EPI>(out_hi, out_lo, zp, (int64_t)t * M + row, M, N - t, bias, v[j], v[j + 1], v[j + 2],
+                                  v[j + 3]);
+            }
           }
         }
         fence_before();
