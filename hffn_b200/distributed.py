@@ -7,10 +7,10 @@ count (up + down slots) and rounded to multiples of 8 so that every shard keeps 
 and biases, and the down edges of its neurons only (re-sorted output-major by ``HFFNLayer.from_hidden_major``).
 ``b_down`` is added by rank 0 only, so the sum over ranks of the partial outputs is the layer's output. Two forms:
 - ``forward_replicated(x)``: x identical on every rank (already broadcast); partial y all-reduced; every rank gets y.
-- ``forward(x_local)``: weak scaling, each rank holds its own batch. The batch of rank c is broadcast from c, every
-  rank runs its neuron shard on it and the partial outputs are reduced to rank c, chunk after chunk; the collectives
-  are queued asynchronously so that the broadcast of the next chunk and the reduction of the previous one overlap
-  the compute of the current one. Every rank returns y of its own batch.
+- ``forward(x_local)``: weak scaling, each rank holds its own batch. Per segment of the batch: all-gather of every
+  rank's sub-batch, one call of the rank's shard over all of them, reduce-scatter of the partial outputs back to
+  their ranks; the collectives are asynchronous, so the gather of the next segment and the reduction of the previous
+  one overlap the compute of the current one. Every rank returns y of its own batch.
 Training: data parallel over tokens with full compact replicas (``DataParallelTrainer``): forward, MSE loss on the
 rank's tokens, backward with the gradients stored, one all-reduce (sum) of the four compact gradient arrays scaled
 by 1 / world (the mean over all tokens), then AdamW. The fused backward + AdamW of one GPU does not apply: the update
@@ -64,42 +64,69 @@ def neuron_partition(arrays: dict, world: int) -> list[int]:
 
 
 class ShardedFFN:
-    """The collectives of the neuron-sharded forward around a rank-local forward ``local_forward(x) -> partial y``
-    (the rank's neuron shard, ``b_down`` on rank 0 only). ``group`` None: the default process group."""
+    """The collectives of the neuron-sharded forward around a rank-local forward ``local_forward(x, out)`` that writes
+    the partial y of the rank's neuron shard (``b_down`` on rank 0 only) into ``out``. ``group`` None: the default
+    process group."""
 
-    def __init__(self, local_forward: Callable[[torch.Tensor], torch.Tensor], d_model: int, group=None) -> None:
+    def __init__(self, local_forward: Callable[[torch.Tensor, torch.Tensor], None], d_model: int, group=None,
+                 segments: int | None = None) -> None:
         self.local_forward = local_forward
         self.d_model = d_model
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        # The exchange grows with the world size while a segment's GEMMs shrink with the segment count: one segment at
+        # two ranks (the exchange is a few percent of the compute), up to four at eight.
+        self.segments = segments or max(1, min(4, self.world // 2))
+        self._buffers: dict = {}
         self._ranks = [dist.get_global_rank(group, k) if group is not None else k for k in range(self.world)]
 
     def forward_replicated(self, x: torch.Tensor) -> torch.Tensor:
         """``y`` of an ``x`` that every rank holds: partial outputs all-reduced (sum)."""
-        y = self.local_forward(x).clone()
+        y = torch.empty(x.shape[0], self.d_model, dtype=x.dtype, device=x.device)
+        self.local_forward(x, y)
         dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
         return y
 
-    def forward(self, x_local: torch.Tensor) -> torch.Tensor:
-        """``y`` of this rank's own batch ``x_local`` (every rank passes a batch of the same shape)."""
-        n = x_local.shape[0]
-        chunks = [x_local if c == self.rank else torch.empty_like(x_local) for c in range(self.world)]
-        pending = [dist.broadcast(chunks[c], src=self._ranks[c], group=self.group, async_op=True)
-                   for c in range(self.world)]
-        out = torch.empty(n, self.d_model, dtype=x_local.dtype, device=x_local.device)
-        partials, reductions = [], []
-        for c in range(self.world):
-            pending[c].wait()
-            partial = self.local_forward(chunks[c]).clone()
-            partials.append(partial)
-            reductions.append(dist.reduce(partial, dst=self._ranks[c], op=dist.ReduceOp.SUM, group=self.group,
-                                          async_op=True))
-        for c, work in enumerate(reductions):
-            work.wait()
-            if c == self.rank:
-                out.copy_(partials[c])
+    def forward(self, x_local: torch.Tensor, segments: int | None = None) -> torch.Tensor:
+        """``y`` of this rank's own batch ``x_local`` (every rank passes a batch of the same shape).
+
+        The batch is cut into ``segments`` sub-batches; for each, every rank's sub-batch is all-gathered, this rank's
+        neuron shard runs on all of them in one call, and the partial outputs are reduce-scattered back to their
+        ranks. The collectives are queued asynchronously, so the gather of segment s + 1 and the reduction of
+        segment s - 1 overlap the compute of segment s."""
+        n, d = x_local.shape[0], self.d_model
+        segments = max(1, min(segments or self.segments, n))
+        bounds = [n * k // segments for k in range(segments + 1)]
+        key = (n, segments, x_local.dtype, x_local.device)
+        if key not in self._buffers:     # exchange buffers, reused by every call of this shape
+            self._buffers[key] = [(torch.empty(self.world * (bounds[s + 1] - bounds[s]), d, dtype=x_local.dtype,
+                                               device=x_local.device),
+                                   torch.empty(self.world * (bounds[s + 1] - bounds[s]), d, dtype=x_local.dtype,
+                                               device=x_local.device)) for s in range(segments)]
+        buffers = self._buffers[key]
+        gathers = []
+        for s in range(segments):
+            part = x_local[bounds[s]:bounds[s + 1]]
+            gathers.append(dist.all_gather_into_tensor(buffers[s][0], part, group=self.group, async_op=True))
+        out = torch.empty(n, d, dtype=x_local.dtype, device=x_local.device)
+        scatters = []
+        for s in range(segments):
+            gathers[s].wait()
+            self.local_forward(buffers[s][0], buffers[s][1])
+            scatters.append(self._reduce_scatter(out[bounds[s]:bounds[s + 1]], buffers[s][1]))
+        for work in scatters:
+            if work is not None:
+                work.wait()
         return out
+
+    def _reduce_scatter(self, out: torch.Tensor, partial: torch.Tensor):
+        if dist.get_backend(self.group) == "gloo":      # gloo has no reduce-scatter: all-reduce and keep the slice
+            dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
+            m = out.shape[0]
+            out.copy_(partial[self.rank * m:(self.rank + 1) * m])
+            return None
+        return dist.reduce_scatter_tensor(out, partial, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
 
 
 def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, tensor_cores=None, group=None):
@@ -115,7 +142,7 @@ def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, ten
                                         shard["up_idx"], shard["up_val"], shard["b_down"], shard["down_offsets"],
                                         shard["down_idx"], shard["down_val"])
     runtime = HFFNRuntime([layer], device, dtype, tensor_cores=tensor_cores)
-    return runtime, ShardedFFN(lambda x: runtime.forward(0, x), d_model, group), (lo, hi)
+    return runtime, ShardedFFN(lambda x, out: runtime.forward(0, x, out=out), d_model, group), (lo, hi)
 
 
 class DataParallelTrainer:

@@ -213,14 +213,18 @@ class HFFNRuntime:
             raise ValueError("unsupported token count")
         return n
 
-    def forward(self, index: int, x: torch.Tensor) -> torch.Tensor:
-        """y[N, d_model] of layer ``index`` for x[N, d_model]; a view of the runtime's output buffer."""
+    def forward(self, index: int, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """y[N, d_model] of layer ``index`` for x[N, d_model]: a view of the runtime's output buffer (overwritten by
+        the next call), or ``out`` (contiguous [N, d_model] of the runtime's dtype and device) when given."""
         n = self._check_input(x)
+        if out is not None and (out.shape != (n, self.d_model) or out.dtype != self.dtype or out.device != self._y.device
+                                or not out.is_contiguous()):
+            raise ValueError("out must be a contiguous [N, d_model] tensor of the runtime's dtype and device")
         if n > self._tokens:
             self._reserve(n)
-        up, down = self._launch(index, x, n, None)
+        up, down = self._launch(index, x, n, None, out)
         self.calls[up, down] += 1
-        return self._y[:n]
+        return self._y[:n] if out is None else out
 
     def modes(self, n: int, hidden_major: bool = False) -> tuple[str, str]:
         """The (up, down) modes of a call on N tokens. ``hidden_major``: the caller needs the hidden-major activations
@@ -232,20 +236,22 @@ class HFFNRuntime:
             return TC, TC
         return up or up_mode(n, self.d_model), down or down_mode(n, self.d_ff)
 
-    def _launch(self, index: int, x: torch.Tensor, n: int, z: torch.Tensor | None) -> tuple[str, str]:
+    def _launch(self, index: int, x: torch.Tensor, n: int, z: torch.Tensor | None,
+                out: torch.Tensor | None = None) -> tuple[str, str]:
         """Queue the up then the down kernel of layer ``index`` for the ``n`` tokens of ``x`` (validated, buffers
         reserved); ``z`` (float32, >= d_ff * n entries) also receives the pre-activations, hidden-major (the CUDA-core
         kernels then run whatever the policy). Returns the modes."""
         up, down = self.modes(n, hidden_major=z is not None)
+        y = self._y if out is None else out
         if up == TC:
             if self._dense_stale[index]:
                 self._densify(index)
             status = native.lib.hffn_forward_tc(self._code, self._structs[index], self._dense_structs[index],
-                                                x.data_ptr(), self._y.data_ptr(), None, self._tc_work.data_ptr(),
+                                                x.data_ptr(), y.data_ptr(), None, self._tc_work.data_ptr(),
                                                 self._err.data_ptr(), n, native.stream_handle(self.device))
             native.check(status, "hffn_forward_tc")
             return up, down
-        status = native.lib.hffn_forward(self._code, self._structs[index], x.data_ptr(), self._y.data_ptr(),
+        status = native.lib.hffn_forward(self._code, self._structs[index], x.data_ptr(), y.data_ptr(),
                                          self._act.data_ptr(), None if z is None else z.data_ptr(), n,
                                          native.UP_CODES[up], native.DOWN_CODES[down],
                                          native.stream_handle(self.device))

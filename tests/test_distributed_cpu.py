@@ -68,7 +68,8 @@ def _worker(rank: int, world: int, port: int, results) -> None:
         arrays = canonical(layer)
         bounds = neuron_partition(arrays, world)
         shard = as_layer(shard_hidden_major(layer.d_model, arrays, bounds[rank], bounds[rank + 1], rank == 0))
-        ffn = ShardedFFN(lambda x: torch.from_numpy(forward64.forward(shard, x.numpy())), layer.d_model)
+        ffn = ShardedFFN(lambda x, out: out.copy_(torch.from_numpy(forward64.forward(shard, x.numpy()))),
+                         layer.d_model, segments=3)
         x_shared = torch.from_numpy(synth.make_input(case, 6)).double()
         y_rep = ffn.forward_replicated(x_shared)
         x_own = torch.from_numpy(synth.make_input(case, 7 + 100 * rank)[:7]).double()

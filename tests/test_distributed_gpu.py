@@ -3,8 +3,8 @@ step against one GPU.
 
 Sharded forward (both the replicated and the per-rank-batch forms, tensor cores and CUDA cores) equals the single-GPU
 runtime's output within the forward tolerance (the partial sums are added in another order). The data-parallel MSE
-step of two ranks equals, after the update, a single-GPU step on the concatenation of their batches within float32
-tolerance."""
+step of two ranks gives the gradients (all-reduced mean) and the loss of a single-GPU step on the concatenation of
+their batches within float32 tolerance (the update itself is AdamW of those gradients, tested on one GPU)."""
 import os
 import socket
 
@@ -75,9 +75,9 @@ def _worker(rank: int, world: int, port: int, results) -> None:
         loss_one = float(one.step_mse(0, torch.from_numpy(np.concatenate(xs)).to(device),
                                       torch.from_numpy(np.concatenate(ts)).to(device)))
         worst = 0.0
-        for name, p in dp_train.parameters(0).items():
-            q = one.parameters(0)[name]
-            worst = max(worst, float(((p - q).abs() / q.abs().clamp(min=1e-3)).max()))
+        for name, g in dp_train.gradients(0).items():    # the all-reduced mean gradient against one GPU's
+            h = one.gradients(0)[name]
+            worst = max(worst, float((g - h).abs().max() / h.abs().max()))
         out["dp_param_rel"] = worst
         out["dp_loss_rel"] = abs(loss - loss_one) / loss_one
         results[rank] = out
