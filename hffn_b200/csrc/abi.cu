@@ -25,6 +25,11 @@ int tc_forward(int dtype, const hffn_layer* L, const void* up_hi, const void* up
 int64_t tc_forward_workspace(int dtype, const hffn_layer* L, int64_t n);
 int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const void* b, void* act_hi, void* act_lo,
           float* z, void* x_split, int* err, int d, int H, int64_t n, cudaStream_t s);
+int64_t tc_train_workspace(const hffn_layer* L, int64_t n);
+int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, const void* down_hi, const void* down_lo,
+                  const float* x, const float* target, float* y, float* gx, const hffn_train_params* P,
+                  const hffn_adamw_step* opt, float* loss, void* work, int* err, int64_t n, int64_t n_total,
+                  cudaStream_t s);
 int tc_down(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo, const void* b,
             void* y, int* err, int d, int H, int64_t n, cudaStream_t s);
 int tc_densify(int dtype, const int32_t* off, const int16_t* idx, const void* val, int rows, int cols, void* hi,
@@ -252,6 +257,35 @@ int hffn_down_tc(int dtype, const void* act_hi, const void* act_lo, const void* 
   HFFN_TRY(bind_stream_device(stream));
   return tc_down(dtype, act_hi, act_lo, w_hi, w_lo, b_down, y, err, d_model, d_ff, n,
                  static_cast<cudaStream_t>(stream));
+}
+
+int64_t hffn_train_step_tc_workspace(const hffn_layer* layer, int64_t n) {
+  if (layer == nullptr || n < 1) return -1;
+  return tc_train_workspace(layer, n);
+}
+
+int hffn_train_step_tc(const hffn_layer* layer, const hffn_dense* dense, const float* x, const float* target,
+                       float* y, float* gx, const hffn_train_params* params, const hffn_adamw_step* adamw,
+                       float* loss, void* work, int32_t* err, int64_t n, int64_t n_total, void* stream) {
+  HFFN_TRY(check_layer(layer));
+  HFFN_TRY(check_tc(HFFN_F32, layer->d_model, layer->d_ff, n));
+  HFFN_REQUIRE(layer->d_model % 32 == 0 && layer->d_ff % 32 == 0,
+               "tensor-core training: d_model and d_ff multiples of 32");
+  HFFN_REQUIRE(n_total >= n, "n_total below n");
+  HFFN_REQUIRE(dense && dense->up_hi && dense->up_lo && dense->down_hi && dense->down_lo, "null dense operand");
+  HFFN_REQUIRE(x && target && y && gx && params && loss && work && err, "null pointer argument");
+  HFFN_REQUIRE(aligned16(x) && aligned16(work), "x and the workspace must be 16-byte aligned");
+  const bool fused = adamw != nullptr;
+  HFFN_TRY(check_param(params->up_val, layer->nnz_up, !fused, fused, "up_val"));
+  HFFN_TRY(check_param(params->b_up, layer->d_ff, !fused, fused, "b_up"));
+  HFFN_TRY(check_param(params->out_val, layer->nnz_down, !fused, fused, "out_val"));
+  HFFN_TRY(check_param(params->b_down, layer->d_model, !fused, fused, "b_down"));
+  HFFN_REQUIRE(params->up_val.value == layer->up_val && params->out_val.value == layer->out_val &&
+                   params->b_up.value == layer->b_up && params->b_down.value == layer->b_down,
+               "the parameter values must be the layer's arrays");
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_train_step(layer, dense->up_hi, dense->up_lo, dense->down_hi, dense->down_lo, x, target, y, gx, params,
+                       adamw, loss, work, err, n, n_total, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

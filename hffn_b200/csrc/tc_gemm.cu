@@ -24,6 +24,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <climits>
+
 #include "common.cuh"
 
 namespace hffn {
@@ -34,7 +36,12 @@ __host__ __device__ constexpr int threads_for(int ew) { return 64 + 32 * ew; }
 constexpr int BM = 128;                  // features per tile (TMEM lanes)
 constexpr uint64_t kWaitNs = 2000000000ull;
 
-enum Epilogue { kUp = 0, kDown = 1 };
+// kUp: + b_up, GELU, act (and z) stores. kDown: + bias (optional), y store. kDownMse: + b_down, y store, the MSE
+// gradient gy = scale (y - target) as tf32 hi/lo, per-thread partial sums of (y - target)^2 and of gy per output.
+// kGradHidden: gz = acc * gelu'(z) as tf32 hi/lo, per-thread partial sums of gz per neuron. kSampled: the weight
+// gradient sampled at the support entries of each row (CSR, columns ascending), stored and / or applied by AdamW, the
+// dense operand refreshed with the new value.
+enum Epilogue { kUp = 0, kDown = 1, kDownMse = 2, kGradHidden = 3, kSampled = 4 };
 
 // error codes written to the kernel's error flag
 constexpr int kErrTimeoutProducer = 101, kErrTimeoutMma = 102, kErrTimeoutEpilogue = 103;
@@ -105,10 +112,18 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
          ((uint64_t)1 << 46) | (layout << 61);
 }
 
-// Instruction descriptor: fp32 accumulator, A/B format (tf32 = 2, bf16 = 1), both K-major, N = bn, M = 128.
-__host__ __device__ constexpr uint32_t instr_desc(int fmt, int bn) {
-  return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((uint32_t)(bn >> 3) << 17) |
-         ((uint32_t)(BM >> 4) << 24);
+// Shared-memory matrix descriptor of an MN-major operand: blocks of 32 MN elements (128 bytes) x BK K rows written by
+// TMA with the 128-byte swizzle; MN blocks `lbo` bytes apart (leading byte offset), 8-row K groups 1024 bytes apart
+// (stride byte offset), descriptor version 1, layout type 2.
+__device__ __forceinline__ uint64_t smem_desc_mn(uint32_t addr, uint32_t lbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: fp32 accumulator, A/B format (tf32 = 2, bf16 = 1), A/B major (0 K, 1 MN), N = bn, M = 128.
+__host__ __device__ constexpr uint32_t instr_desc(int fmt, int bn, bool a_mn = false, bool b_mn = false) {
+  return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
 template <bool kBf16>
@@ -157,50 +172,107 @@ __device__ __forceinline__ float tf32_rna(float v) {
 }
 
 struct EpilogueArgs {
-  const void* bias;   // [M] of the storage type
-  void* out_hi;       // up: act (hi part for fp32) [N, M]; down: y [N, M]
-  void* out_lo;       // up fp32: act lo part [N, M]
-  float* z;           // up fp32, optional: pre-activations [N, M]
+  const void* bias;   // [M] of the storage type (NULL: none)
+  void* out_hi;       // kUp: act (hi part for fp32) [N, M]; kDown / kDownMse: y [N, M]; kGradHidden: gz hi [N, M]
+  void* out_lo;       // kUp fp32: act lo part; kGradHidden: gz lo
+  float* z;           // kUp fp32, optional: pre-activations [N, M]
+  // kDownMse
+  const float* target;   // [N, M]
+  float* gy_hi;          // [N, M]
+  float* gy_lo;
+  float scale;           // 2 / (N_total M)
+  float* loss_partial;   // [num_n * parts, M]
+  float* col_partial;    // kDownMse / kGradHidden: [num_n * parts, M] partial sums of gy / gz per row
+  // kGradHidden
+  const float* z_in;     // [N, M] pre-activations of the forward
+  // kSampled: support of each row (offsets [M + 1], ascending columns), compact values / gradient / moments
+  const int32_t* offsets;
+  const int16_t* cols;
+  float* value;
+  float* grad;           // NULL: not stored
+  float* m;
+  float* v;
+  float* dense_hi;       // [M, N] refreshed with the updated value (tf32 hi / lo)
+  float* dense_lo;
+  int adam;              // apply AdamW
+  hffn_adamw_step step;
 };
 
 // One value of the output tile: bias added, then (up) GELU and the stores of act (float32: tf32 hi and lo parts) and
 // of z, or (down) the store of y. Out of line: the epilogue calls it once per value, and an inlined copy per value
 // of an unrolled tile overflows the instruction cache.
 template <bool kBf16, int EPI>
-__device__ __forceinline__ void emit_one(void* out_hi, void* out_lo, float* z, int64_t at, float s) {
+__device__ __forceinline__ float2 emit_one(const EpilogueArgs* e, int64_t at, float s) {
   if constexpr (EPI == kUp) {
-    if (!kBf16 && z) z[at] = s;
+    if (!kBf16 && e->z) e->z[at] = s;
     const float h = gelu(s);
     if constexpr (kBf16) {
-      reinterpret_cast<__nv_bfloat16*>(out_hi)[at] = __float2bfloat16_rn(h);
+      reinterpret_cast<__nv_bfloat16*>(e->out_hi)[at] = __float2bfloat16_rn(h);
     } else {
       const float hi = tf32_rna(h);
-      reinterpret_cast<float*>(out_hi)[at] = hi;
-      reinterpret_cast<float*>(out_lo)[at] = tf32_rna(h - hi);
+      reinterpret_cast<float*>(e->out_hi)[at] = hi;
+      reinterpret_cast<float*>(e->out_lo)[at] = tf32_rna(h - hi);
     }
-  } else {
-    if constexpr (kBf16) reinterpret_cast<__nv_bfloat16*>(out_hi)[at] = __float2bfloat16_rn(s);
-    else reinterpret_cast<float*>(out_hi)[at] = s;
+    return make_float2(0.f, 0.f);
+  } else if constexpr (EPI == kDown) {
+    if constexpr (kBf16) reinterpret_cast<__nv_bfloat16*>(e->out_hi)[at] = __float2bfloat16_rn(s);
+    else reinterpret_cast<float*>(e->out_hi)[at] = s;
+    return make_float2(0.f, 0.f);
+  } else if constexpr (EPI == kDownMse) {
+    reinterpret_cast<float*>(e->out_hi)[at] = s;
+    const float diff = s - e->target[at];
+    const float g = e->scale * diff;
+    const float hi = tf32_rna(g);
+    e->gy_hi[at] = hi;
+    e->gy_lo[at] = tf32_rna(g - hi);
+    return make_float2(diff * diff, g);
+  } else {   // kGradHidden
+    const float g = s * gelu_grad(e->z_in[at]);
+    const float hi = tf32_rna(g);
+    reinterpret_cast<float*>(e->out_hi)[at] = hi;
+    reinterpret_cast<float*>(e->out_lo)[at] = tf32_rna(g - hi);
+    return make_float2(0.f, g);
   }
 }
 
-// Four values of one output row (tokens t0 .. t0 + 3, count of them valid): bias added, then (up) GELU and the stores
-// of act (float32: tf32 hi and lo parts) and z, or (down) the store of y. Out of line: the epilogue calls it once
-// per 4 values (an inlined copy per value of an unrolled tile overflows the instruction cache); the four values are
-// independent, so their GELU chains interleave.
+// Four values of one output row (tokens t0 .. t0 + 3 at `stride` apart, `count` of them valid): bias added, then
+// the epilogue's stores; returns the partial sums it contributes (loss, column sum). Out of line: the epilogue calls
+// it once per 4 values (an inlined copy per value of an unrolled tile overflows the instruction cache); the four
+// values are independent, so their chains interleave.
 template <bool kBf16, int EPI>
-__device__ __noinline__ void emit4(void* out_hi, void* out_lo, float* z, int64_t at, int64_t stride, int count,
-                                   float bias, float v0, float v1, float v2, float v3) {
+__device__ __noinline__ float2 emit4(const EpilogueArgs* e, int64_t at, int64_t stride, int count, float bias,
+                                     float v0, float v1, float v2, float v3) {
+  float2 acc = make_float2(0.f, 0.f), r;
   if (count >= 4) {
-    emit_one<kBf16, EPI>(out_hi, out_lo, z, at, v0 + bias);
-    emit_one<kBf16, EPI>(out_hi, out_lo, z, at + stride, v1 + bias);
-    emit_one<kBf16, EPI>(out_hi, out_lo, z, at + 2 * stride, v2 + bias);
-    emit_one<kBf16, EPI>(out_hi, out_lo, z, at + 3 * stride, v3 + bias);
-    return;
+    r = emit_one<kBf16, EPI>(e, at, v0 + bias); acc.x += r.x; acc.y += r.y;
+    r = emit_one<kBf16, EPI>(e, at + stride, v1 + bias); acc.x += r.x; acc.y += r.y;
+    r = emit_one<kBf16, EPI>(e, at + 2 * stride, v2 + bias); acc.x += r.x; acc.y += r.y;
+    r = emit_one<kBf16, EPI>(e, at + 3 * stride, v3 + bias); acc.x += r.x; acc.y += r.y;
+    return acc;
   }
-  if (count > 0) emit_one<kBf16, EPI>(out_hi, out_lo, z, at, v0 + bias);
-  if (count > 1) emit_one<kBf16, EPI>(out_hi, out_lo, z, at + stride, v1 + bias);
-  if (count > 2) emit_one<kBf16, EPI>(out_hi, out_lo, z, at + 2 * stride, v2 + bias);
+  if (count > 0) { r = emit_one<kBf16, EPI>(e, at, v0 + bias); acc.x += r.x; acc.y += r.y; }
+  if (count > 1) { r = emit_one<kBf16, EPI>(e, at + stride, v1 + bias); acc.x += r.x; acc.y += r.y; }
+  if (count > 2) { r = emit_one<kBf16, EPI>(e, at + 2 * stride, v2 + bias); acc.x += r.x; acc.y += r.y; }
+  return acc;
+}
+
+// One support entry q of row `row`, column `col`, gradient g: stored and / or applied by AdamW (PyTorch's fused order),
+// and the dense operand [row, col] refreshed with the new value as tf32 hi / lo.
+__device__ __noinline__ void sampled_entry(const EpilogueArgs* e, int q, int64_t dense_at, float g) {
+  if (e->grad) e->grad[q] = g;
+  if (!e->adam) return;
+  const hffn_adamw_step& st = e->step;
+  float p = e->value[q];
+  p -= st.lr_decay * p;
+  const float mi = st.beta1 * e->m[q] + st.one_minus_beta1 * g;
+  const float vi = st.beta2 * e->v[q] + st.one_minus_beta2 * g * g;
+  e->m[q] = mi;
+  e->v[q] = vi;
+  p -= st.step_size * mi / (sqrtf(vi) / st.bias2_sqrt + st.eps);
+  e->value[q] = p;
+  const float hi = tf32_rna(p);
+  e->dense_hi[dense_at] = hi;
+  e->dense_lo[dense_at] = tf32_rna(p - hi);
 }
 
 // Shared memory: [stages][A parts][128 rows x 128 B] then [stages][B parts][BN rows x 128 B], 1024-aligned.
@@ -216,11 +288,11 @@ struct Layout {
   static constexpr int kTmemCols = 2 * BN;
 };
 
-template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK, int RB, int EW>
+template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK, int RB, int EW, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(threads_for(EW), 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_a_lo,
                const __grid_constant__ CUtensorMap map_b_hi, const __grid_constant__ CUtensorMap map_b_lo, int M,
-               int N, int K, EpilogueArgs epi, int* err) {
+               int N, int K, const __grid_constant__ EpilogueArgs epi, int* err) {
   using L = Layout<kBf16, BN, STAGES, RB>;
   constexpr int kRowBytes = RB;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -292,11 +364,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
           uint8_t* a = a_base + stage * L::kParts * L::kA;
           uint8_t* b = b_base + stage * L::kParts * L::kB;
           const int kc = kb * k_elems;
-          tma_load_2d(a, &map_a_hi, &full[stage], kc, m0);
-          tma_load_2d(b, &map_b_hi, &full[stage], kc, n0);
+          // K-major: one box (K extent x rows); MN-major: one box (32 MN x K extent) per 32-element MN block
+          auto load = [&](uint8_t* dst, const CUtensorMap* map, int mn0, int rows, bool mn_major) {
+            if (!mn_major) {
+              tma_load_2d(dst, map, &full[stage], kc, mn0);
+            } else {
+              for (int blk = 0; blk < rows / 32; ++blk)
+                tma_load_2d(dst + blk * (k_elems * 128), map, &full[stage], mn0 + 32 * blk, kc);
+            }
+          };
+          load(a, &map_a_hi, m0, BM, A_MN);
+          load(b, &map_b_hi, n0, BN, B_MN);
           if (!kBf16) {
-            tma_load_2d(a + L::kA, &map_a_lo, &full[stage], kc, m0);
-            tma_load_2d(b + L::kB, &map_b_lo, &full[stage], kc, n0);
+            load(a + L::kA, &map_a_lo, m0, BM, A_MN);
+            load(b + L::kB, &map_b_lo, n0, BN, B_MN);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -321,7 +402,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
     // The K loop of a tile runs in chunks of chunk_kb k-blocks, each into a fresh accumulator buffer that the
     // epilogue drains (float32: the chunk sums are added in registers with round-to-nearest; see the epilogue).
     if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(kBf16 ? 1 : 2, BN);
+      constexpr uint32_t idesc = instr_desc(kBf16 ? 1 : 2, BN, A_MN, B_MN);
+      const uint32_t mn_lbo = (uint32_t)(k_elems * 128);    // bytes between 32-element MN blocks of a stage
       const int chunk_kb = KCHUNK > 0 ? KCHUNK : num_kb;
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
@@ -346,10 +428,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
 #pragma unroll
             for (int k = 0; k < kRowBytes / 32; ++k) {
               const uint32_t acc_in = (kb != kc || k != 0) ? 1u : 0u;
-              const uint64_t ah = smem_desc<RB>(a + 32 * k), bh = smem_desc<RB>(b + 32 * k);
+              const uint64_t ah = A_MN ? smem_desc_mn(a + 1024 * k, mn_lbo) : smem_desc<RB>(a + 32 * k);
+              const uint64_t bh = B_MN ? smem_desc_mn(b + 1024 * k, mn_lbo) : smem_desc<RB>(b + 32 * k);
               mma<kBf16>(d_tmem, ah, bh, idesc, acc_in);
               if (!kBf16) {
-                const uint64_t al = smem_desc<RB>(a + L::kA + 32 * k), bl = smem_desc<RB>(b + L::kB + 32 * k);
+                const uint64_t al = A_MN ? smem_desc_mn(a + L::kA + 1024 * k, mn_lbo) : smem_desc<RB>(a + L::kA + 32 * k);
+                const uint64_t bl = B_MN ? smem_desc_mn(b + L::kB + 1024 * k, mn_lbo) : smem_desc<RB>(b + L::kB + 32 * k);
                 mma<kBf16>(d_tmem, ah, bl, idesc, 1);
                 mma<kBf16>(d_tmem, al, bh, idesc, 1);
               }
@@ -380,24 +464,24 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
     }
   } else {
     // ---------------- epilogue: warps 2 .. EW + 1; TMEM lane quarter = warp % 4, column part = (warp - 2) / 4 ----------
-    constexpr int HALF = BN / (EW / 4);
+    constexpr int PARTS = EW / 4;
+    constexpr int HALF = BN / PARTS;
     static_assert(HALF % 32 == 0, "column part of an epilogue warp");
-    void* const out_hi = epi.out_hi;
-    void* const out_lo = epi.out_lo;
-    float* const zp = epi.z;
+    const EpilogueArgs* e = &epi;
     const int quarter = warp & 3, half = (warp - 2) >> 2;
     const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * HALF;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN + half * HALF;
+      const int m0 = (tile % num_m) * BM, n_blk = tile / num_m, n0 = n_blk * BN + half * HALF;
       const int row = m0 + quarter * 32 + lane;
       float bias = 0.f;
-      if (row < M) {
-        if constexpr (kBf16) bias = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(epi.bias)[row]);
-        else bias = reinterpret_cast<const float*>(epi.bias)[row];
+      if (row < M && e->bias != nullptr) {
+        if constexpr (kBf16) bias = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(e->bias)[row]);
+        else bias = reinterpret_cast<const float*>(e->bias)[row];
       }
+      float2 partial = make_float2(0.f, 0.f);
       if constexpr (KCHUNK > 0) {
         // chunk partials summed in registers, chunk after chunk, round-to-nearest
         float sum[HALF];
@@ -424,12 +508,37 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
           }
         }
         if (!ok) break;
-        if (row < M) {
+        if constexpr (EPI == kSampled) {
+          // the support entries of this row within columns [n0, n0 + HALF), ascending: binary search, then a walk
+          if (row < M) {
+            const int q_begin = e->offsets[row], q_end = e->offsets[row + 1];
+            int lo = q_begin, hi = q_end;
+            while (lo < hi) {
+              const int mid = (lo + hi) >> 1;
+              if ((int)e->cols[mid] < n0) lo = mid + 1;
+              else hi = mid;
+            }
+            int q = lo;
+            int next = q < q_end ? (int)e->cols[q] : INT_MAX;
+            const int64_t dense_row = (int64_t)row * N;
+#pragma unroll
+            for (int i = 0; i < HALF; ++i) {
+              if (next == n0 + i) {
+                sampled_entry(e, q, dense_row + n0 + i, sum[i]);
+                ++q;
+                next = q < q_end ? (int)e->cols[q] : INT_MAX;
+              }
+            }
+          }
+        } else if (row < M) {
 #pragma unroll
           for (int i = 0; i < HALF; i += 4)
-            if (n0 + i < N)
-              emit4<kBf16, EPI>(out_hi, out_lo, zp, (int64_t)(n0 + i) * M + row, M, N - (n0 + i), bias, sum[i],
-                                sum[i + 1], sum[i + 2], sum[i + 3]);
+            if (n0 + i < N) {
+              const float2 r = emit4<kBf16, EPI>(e, (int64_t)(n0 + i) * M + row, M, N - (n0 + i), bias, sum[i],
+                                                 sum[i + 1], sum[i + 2], sum[i + 3]);
+              partial.x += r.x;
+              partial.y += r.y;
+            }
         }
       } else {
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, kWaitNs)) {
@@ -444,9 +553,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
               const int t = n0 + c * 32 + j;
-              if (t < N)
-                emit4<kBf16, EPI>(out_hi, out_lo, zp, (int64_t)t * M + row, M, N - t, bias, v[j], v[j + 1], v[j + 2],
-                                  v[j + 3]);
+              if (t < N) {
+                const float2 r = emit4<kBf16, EPI>(e, (int64_t)t * M + row, M, N - t, bias, v[j], v[j + 1],
+                                                   v[j + 2], v[j + 3]);
+                partial.x += r.x;
+                partial.y += r.y;
+              }
             }
           }
         }
@@ -455,6 +567,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
+        }
+      }
+      if constexpr (EPI == kDownMse || EPI == kGradHidden) {
+        // one partial per (token block, column part, row): summed in a fixed order by the reduction kernel
+        if (row < M) {
+          const int64_t at = (int64_t)(n_blk * PARTS + half) * M + row;
+          e->col_partial[at] = partial.y;
+          if constexpr (EPI == kDownMse) e->loss_partial[at] = partial.x;
         }
       }
     }
@@ -556,21 +676,51 @@ static int sm_count() {
   return count;
 }
 
-template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK, int RB, int EW>
+// [rows, k] K-major operand, or, mn_major, an operand whose element (mn, k) sits at base + k * ld + mn: boxes of 32 MN
+// elements x k_box K rows (128-byte swizzle). Zero fill outside.
+static int make_map_mn(CUtensorMap* map, const void* base, int64_t mn, int64_t k, int64_t ld, int k_box) {
+  auto fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled unavailable");
+    return HFFN_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)mn, (cuuint64_t)k};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+  cuuint32_t box[2] = {32, (cuuint32_t)k_box};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for an MN-major [%lld, %lld] operand", (int)r, (long long)mn,
+              (long long)k);
+    return HFFN_ERR_CUDA;
+  }
+  return HFFN_OK;
+}
+
+// D[M, N] = A[M, K] B[N, K]^T. K-major operands are [rows, K] with K contiguous; an MN-major operand A (B) is stored
+// [K, M] ([K, N]), its leading dimension lda (ldb) elements.
+template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK, int RB, int EW, bool A_MN = false, bool B_MN = false>
 static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N, int K,
-                       const EpilogueArgs& epi, int* err, cudaStream_t s) {
+                       const EpilogueArgs& epi, int* err, cudaStream_t s, int64_t lda = 0, int64_t ldb = 0) {
   using L = Layout<kBf16, BN, STAGES, RB>;
+  static_assert(!(kBf16 && (A_MN || B_MN)), "MN-major operands are float32 only");
+  constexpr int k_box = RB / 4;
   CUtensorMap ma_hi, ma_lo, mb_hi, mb_lo;
-  HFFN_TRY(make_map(&ma_hi, a_hi, M, K, kBf16, BM, RB));
-  HFFN_TRY(make_map(&mb_hi, b_hi, N, K, kBf16, BN, RB));
+  auto map = [&](CUtensorMap* m, const void* base, int rows, int box_rows, bool mn, int64_t ld) {
+    return mn ? make_map_mn(m, base, rows, K, ld, k_box) : make_map(m, base, rows, K, kBf16, box_rows, RB);
+  };
+  HFFN_TRY(map(&ma_hi, a_hi, M, BM, A_MN, lda));
+  HFFN_TRY(map(&mb_hi, b_hi, N, BN, B_MN, ldb));
   if (!kBf16) {
-    HFFN_TRY(make_map(&ma_lo, a_lo, M, K, kBf16, BM, RB));
-    HFFN_TRY(make_map(&mb_lo, b_lo, N, K, kBf16, BN, RB));
+    HFFN_TRY(map(&ma_lo, a_lo, M, BM, A_MN, lda));
+    HFFN_TRY(map(&mb_lo, b_lo, N, BN, B_MN, ldb));
   } else {
     ma_lo = ma_hi;
     mb_lo = mb_hi;
   }
-  auto kernel = tc_gemm_kernel<kBf16, BN, STAGES, EPI, KCHUNK, RB, EW>;
+  auto kernel = tc_gemm_kernel<kBf16, BN, STAGES, EPI, KCHUNK, RB, EW, A_MN, B_MN>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
@@ -579,7 +729,7 @@ static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, con
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
   kernel<<<grid, threads_for(EW), L::kTotal, s>>>(ma_hi, ma_lo, mb_hi, mb_lo, M, N, K, epi, err);
-  return launch_status(EPI == kUp ? "tc_up" : "tc_down");
+  return launch_status("tc_gemm");
 }
 
 }  // namespace tc
@@ -596,7 +746,9 @@ int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const vo
           float* z, void* x_split, int* err, int d, int H, int64_t n, cudaStream_t s) {
   const int nn = (int)n;
   if (dtype == HFFN_BF16) {
-    tc::EpilogueArgs up{b, act_hi, nullptr, nullptr};
+    tc::EpilogueArgs up{};
+    up.bias = b;
+    up.out_hi = act_hi;
     return tc::launch_gemm<true, 256, 4, tc::kUp, 0, 128, 16>(w_hi, nullptr, x, nullptr, H, nn, d, up, err, s);
   }
   float* x_hi = reinterpret_cast<float*>(x_split);
@@ -606,7 +758,11 @@ int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const vo
   tc::split_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(x_hi),
                                           reinterpret_cast<float4*>(x_lo), count4);
   HFFN_TRY(launch_status("tc_split"));
-  tc::EpilogueArgs up{b, act_hi, act_lo, z};
+  tc::EpilogueArgs up{};
+  up.bias = b;
+  up.out_hi = act_hi;
+  up.out_lo = act_lo;
+  up.z = z;
   return tc::launch_gemm<false, 256, 4, tc::kUp, kFp32Chunk, 64, 8>(w_hi, w_lo, x_hi, x_lo, H, nn, d, up, err, s);
 }
 
@@ -614,7 +770,9 @@ int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const vo
 int tc_down(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo, const void* b,
             void* y, int* err, int d, int H, int64_t n, cudaStream_t s) {
   const int nn = (int)n;
-  tc::EpilogueArgs dn{b, y, nullptr, nullptr};
+  tc::EpilogueArgs dn{};
+  dn.bias = b;
+  dn.out_hi = y;
   if (dtype == HFFN_BF16) return tc::launch_gemm<true, 256, 4, tc::kDown, 0, 128, 16>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s);
   return tc::launch_gemm<false, 256, 4, tc::kDown, kFp32Chunk, 64, 8>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err, s);
 }
@@ -633,6 +791,171 @@ int tc_forward(int dtype, const hffn_layer* L, const void* up_hi, const void* up
   float* act_lo = act_hi + n * H;
   HFFN_TRY(tc_up(dtype, x, up_hi, up_lo, L->b_up, act_hi, act_lo, z, x_split, err, d, H, n, s));
   return tc_down(dtype, act_hi, act_lo, down_hi, down_lo, L->b_down, y, err, d, H, n, s);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// training step on the tensor cores (float32, 3xTF32, chunked accumulation)
+
+namespace tc {
+
+// Fixed-order sums of the per-(token block, column part) partials: the bias gradients (then stored and / or applied
+// by AdamW) and, in block 0 of the loss launch, the loss.
+__global__ void bias_reduce_kernel(const float* __restrict__ partial, int rows, int count, hffn_param p, int adam,
+                                   hffn_adamw_step st) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= count) return;
+  float g = 0.f;
+  for (int j = 0; j < rows; ++j) g += partial[(int64_t)j * count + i];
+  if (p.grad) p.grad[i] = g;
+  if (!adam) return;
+  float v = p.value[i];
+  v -= st.lr_decay * v;
+  const float mi = st.beta1 * p.m[i] + st.one_minus_beta1 * g;
+  const float vi = st.beta2 * p.v[i] + st.one_minus_beta2 * g * g;
+  p.m[i] = mi;
+  p.v[i] = vi;
+  p.value[i] = v - st.step_size * mi / (sqrtf(vi) / st.bias2_sqrt + st.eps);
+}
+
+__global__ void loss_reduce_kernel(const float* __restrict__ partial, int64_t count, double inv, float* loss) {
+  __shared__ double red[256];
+  double acc = 0.0;
+  for (int64_t i = threadIdx.x; i < count; i += blockDim.x) acc += partial[i];
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double sum = 0.0;
+    for (int k = 0; k < (int)blockDim.x; ++k) sum += red[k];
+    *loss = (float)(sum * inv);
+  }
+}
+
+constexpr int kTrainBN = 256, kTrainParts = 2;
+
+struct TrainWork {
+  float *x_hi, *x_lo, *z, *act_hi, *act_lo, *gy_hi, *gy_lo, *gz_hi, *gz_lo, *loss_p, *dn_p, *up_p;
+};
+
+static int64_t train_floats(int64_t d, int64_t H, int64_t n, TrainWork* w, float* base) {
+  const int64_t rows = kTrainParts * ((n + kTrainBN - 1) / kTrainBN);
+  int64_t off = 0;
+  auto take = [&](float** slot, int64_t count) {
+    if (w) *slot = base + off;
+    off += (count + 63) / 64 * 64;   // 256-byte aligned pieces
+  };
+  TrainWork dummy;
+  TrainWork* t = w ? w : &dummy;
+  take(&t->x_hi, n * d);
+  take(&t->x_lo, n * d);
+  take(&t->z, n * H);
+  take(&t->act_hi, n * H);
+  take(&t->act_lo, n * H);
+  take(&t->gy_hi, n * d);
+  take(&t->gy_lo, n * d);
+  take(&t->gz_hi, n * H);
+  take(&t->gz_lo, n * H);
+  take(&t->loss_p, rows * d);
+  take(&t->dn_p, rows * d);
+  take(&t->up_p, rows * H);
+  return off;
+}
+
+}  // namespace tc
+
+int64_t tc_train_workspace(const hffn_layer* L, int64_t n) {
+  return 4 * tc::train_floats(L->d_model, L->d_ff, n, nullptr, nullptr);
+}
+
+int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, const void* down_hi, const void* down_lo,
+                  const float* x, const float* target, float* y, float* gx, const hffn_train_params* P,
+                  const hffn_adamw_step* opt, float* loss, void* work, int* err, int64_t n, int64_t n_total,
+                  cudaStream_t s) {
+  using namespace tc;
+  const int d = L->d_model, H = L->d_ff, nn = (int)n;
+  TrainWork w;
+  train_floats(d, H, n, &w, reinterpret_cast<float*>(work));
+  const int rows = kTrainParts * (int)((n + kTrainBN - 1) / kTrainBN);
+  const int adam = opt != nullptr;
+  const hffn_adamw_step st = opt ? *opt : hffn_adamw_step{};
+  float* dense_up_hi = const_cast<float*>(reinterpret_cast<const float*>(up_hi));
+  float* dense_up_lo = const_cast<float*>(reinterpret_cast<const float*>(up_lo));
+  float* dense_dn_hi = const_cast<float*>(reinterpret_cast<const float*>(down_hi));
+  float* dense_dn_lo = const_cast<float*>(reinterpret_cast<const float*>(down_lo));
+
+  // x -> tf32 hi / lo
+  const int64_t count4 = n * d / 4;
+  split_kernel<<<(int)std::min<int64_t>(std::max<int64_t>(ceil_div(count4, 256), 1), 148 * 8), 256, 0, s>>>(
+      reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(w.x_hi), reinterpret_cast<float4*>(w.x_lo),
+      count4);
+  HFFN_TRY(launch_status("tc_split"));
+  // 1. up: z, act = gelu(z)                                       D[H, n] = W_up[H, d] x[n, d]^T
+  EpilogueArgs e1{};
+  e1.bias = L->b_up;
+  e1.out_hi = w.act_hi;
+  e1.out_lo = w.act_lo;
+  e1.z = w.z;
+  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kUp, kFp32Chunk, 64, 8>(up_hi, up_lo, w.x_hi, w.x_lo, H, nn, d, e1, err,
+                                                                     s)));
+  // 2. down + MSE: y, gy = 2 (y - target) / (n_total d)           D[d, n] = W_down[d, H] act[n, H]^T
+  EpilogueArgs e2{};
+  e2.bias = L->b_down;
+  e2.out_hi = y;
+  e2.target = target;
+  e2.gy_hi = w.gy_hi;
+  e2.gy_lo = w.gy_lo;
+  e2.scale = (float)(2.0 / ((double)n_total * d));
+  e2.loss_partial = w.loss_p;
+  e2.col_partial = w.dn_p;
+  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDownMse, kFp32Chunk, 64, 8>(down_hi, down_lo, w.act_hi, w.act_lo, d, nn,
+                                                                          H, e2, err, s)));
+  // 3. gz = (W_down^T gy) * gelu'(z)                               D[H, n] = W_down^T[H, d] gy[n, d]^T
+  EpilogueArgs e3{};
+  e3.out_hi = w.gz_hi;
+  e3.out_lo = w.gz_lo;
+  e3.z_in = w.z;
+  e3.col_partial = w.up_p;
+  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kGradHidden, kFp32Chunk, 64, 8, true, false>(
+      down_hi, down_lo, w.gy_hi, w.gy_lo, H, nn, d, e3, err, s, H, 0)));
+  // 4. gx = W_up^T gz                                              D[d, n] = W_up^T[d, H] gz[n, H]^T
+  EpilogueArgs e4{};
+  e4.out_hi = gx;
+  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDown, kFp32Chunk, 64, 8, true, false>(up_hi, up_lo, w.gz_hi, w.gz_lo, d,
+                                                                                    nn, H, e4, err, s, d, 0)));
+  // 5. g_down sampled on the output-major support, AdamW, W_down refreshed   D[d, H] = gy^T[d, n] act^T[H, n]^T
+  EpilogueArgs e5{};
+  e5.offsets = L->out_offsets;
+  e5.cols = L->out_hidden;
+  e5.value = P->out_val.value;
+  e5.grad = P->out_val.grad;
+  e5.m = P->out_val.m;
+  e5.v = P->out_val.v;
+  e5.dense_hi = dense_dn_hi;
+  e5.dense_lo = dense_dn_lo;
+  e5.adam = adam;
+  e5.step = st;
+  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kSampled, kFp32Chunk, 64, 8, true, true>(
+      w.gy_hi, w.gy_lo, w.act_hi, w.act_lo, d, H, nn, e5, err, s, d, H)));
+  // 6. g_up sampled on the hidden-major support, AdamW, W_up refreshed        D[H, d] = gz^T[H, n] x^T[d, n]^T
+  EpilogueArgs e6{};
+  e6.offsets = L->up_offsets;
+  e6.cols = L->up_idx;
+  e6.value = P->up_val.value;
+  e6.grad = P->up_val.grad;
+  e6.m = P->up_val.m;
+  e6.v = P->up_val.v;
+  e6.dense_hi = dense_up_hi;
+  e6.dense_lo = dense_up_lo;
+  e6.adam = adam;
+  e6.step = st;
+  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kSampled, kFp32Chunk, 64, 8, true, true>(
+      w.gz_hi, w.gz_lo, w.x_hi, w.x_lo, H, d, nn, e6, err, s, H, d)));
+  // 7. biases and loss
+  bias_reduce_kernel<<<(d + 255) / 256, 256, 0, s>>>(w.dn_p, rows, d, P->b_down, adam, st);
+  HFFN_TRY(launch_status("bias_reduce down"));
+  bias_reduce_kernel<<<(H + 255) / 256, 256, 0, s>>>(w.up_p, rows, H, P->b_up, adam, st);
+  HFFN_TRY(launch_status("bias_reduce up"));
+  loss_reduce_kernel<<<1, 256, 0, s>>>(w.loss_p, (int64_t)rows * d, 1.0 / ((double)n * d), loss);
+  return launch_status("loss_reduce");
 }
 
 int64_t tc_forward_workspace(int dtype, const hffn_layer* L, int64_t n) {

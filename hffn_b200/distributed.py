@@ -159,6 +159,16 @@ class DataParallelTrainer:
         from . import _native as native
         train = self.train
         n = train._check_tokens(target, "target")
+        if train.uses_tensor_cores(index, n):
+            # gradients of the mean over all ranks' tokens (n_total = world n): summed, not averaged
+            train.step_mse_tc(index, x, target, n_total=n * self.world, apply=False)
+            grads = train.gradients(index)
+            for name in ("up_val", "b_up", "out_val", "b_down"):
+                dist.all_reduce(grads[name], op=dist.ReduceOp.SUM, group=self.group)
+            train.apply_adamw(index)
+            self._loss.copy_(train._loss)
+            dist.all_reduce(self._loss, op=dist.ReduceOp.SUM, group=self.group)
+            return self._loss / self.world
         y = train.forward(index, x, train._z)
         gy = train._gy[:n]
         native.check(native.lib.hffn_mse(y.data_ptr(), target.data_ptr(), gy.data_ptr(), train._loss.data_ptr(), n,

@@ -26,7 +26,7 @@ from collections import Counter
 import torch
 
 from . import _native as native
-from .runtime import MAX_TOKENS, HFFNLayer, HFFNRuntime
+from .runtime import MAX_TOKENS, TC, TC_MIN_TOKENS, HFFNLayer, HFFNRuntime
 
 PARAMETERS = ("up_val", "b_up", "out_val", "b_down")
 SUPPORTS = ("in_offsets", "in_pos", "in_hidden", "hid_offsets", "hid_pos", "hid_output")
@@ -54,6 +54,20 @@ def transposed_supports(layer: HFFNLayer) -> dict[str, torch.Tensor]:
             "hid_output": out_owner[by_hidden].to(torch.int16)}
 
 
+def up_slots_ascending(layer: HFFNLayer) -> bool:
+    """Whether the up slots of every neuron are in strictly ascending input order (the tensor-core training step
+    walks each neuron's slots against the columns of its gradient tile)."""
+    idx = layer.up_idx.cpu().long()
+    if idx.numel() < 2:
+        return True
+    step = idx[1:] - idx[:-1]
+    starts = layer.up_offsets.cpu().long()[1:-1]          # a slot that starts a neuron may step down
+    ok = step > 0
+    boundary = torch.zeros(idx.numel(), dtype=torch.bool)
+    boundary[starts[(starts > 0) & (starts < idx.numel())]] = True
+    return bool((ok | boundary[1:]).all())
+
+
 def adamw_scalars(lr: float, betas: tuple[float, float], eps: float, weight_decay: float, k: int) -> native.AdamWStep:
     """The step scalars of update k, in float64 on the host, passed as float32 (``train_runtime.py:195-207``)."""
     beta1, beta2 = betas
@@ -64,13 +78,22 @@ def adamw_scalars(lr: float, betas: tuple[float, float], eps: float, weight_deca
 class HFFNTrainRuntime:
     def __init__(self, runtime: HFFNRuntime, lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.999),
                  eps: float = 1e-8, weight_decay: float = 1e-2, max_tokens: int = PARTIAL_MAX_TOKENS,
-                 store_gradients: bool = True) -> None:
+                 store_gradients: bool = True, tensor_cores: bool | None = None) -> None:
         if runtime.dtype != torch.float32:
             raise ValueError("training runs on a float32 runtime (float32 master weights)")
         self.runtime = runtime
         self.d_model, self.d_ff = runtime.d_model, runtime.d_ff
         self.lr, self.betas, self.eps, self.weight_decay = lr, betas, eps, weight_decay
         self.store_gradients = store_gradients
+        # the MSE step on the tensor cores: None = from TC_MIN_TOKENS tokens when possible, True / False = always / never
+        self.tensor_cores = tensor_cores
+        self._tc_layers = [runtime.tensor_cores and self.d_model % 32 == 0 and self.d_ff % 32 == 0
+                           and up_slots_ascending(layer) for layer in runtime.layers]
+        if tensor_cores and not all(self._tc_layers):
+            raise ValueError("tensor-core training needs dense operands, d_model and d_ff multiples of 32 and ascending "
+                             "up slots per neuron")
+        self._tc_work = None
+        self._tc_tokens = 0
         device = runtime.device
         self._supports, self._grads, self._moments = [], [], []
         self._support_structs, self._param_structs = [], []
@@ -196,11 +219,19 @@ class HFFNTrainRuntime:
         self.runtime.mark_updated(index)
         return gx
 
+    def uses_tensor_cores(self, index: int, n: int) -> bool:
+        if not self._tc_layers[index]:
+            return False
+        return self.tensor_cores if self.tensor_cores is not None else n >= TC_MIN_TOKENS
+
     def step_mse(self, index: int, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
         """One step on the MSE loss ``mean((y - target)^2)``: forward, loss and its gradient
         ``gy = 2 (y - target) / (N d_model)``, fused backward + AdamW. Returns the loss (a 1-element device view,
-        the loss of the parameters before the update)."""
+        the loss of the parameters before the update). From ``TC_MIN_TOKENS`` tokens (``tensor_cores``) the whole
+        step runs on the tensor cores (``hffn_train_step_tc``); gx is then ``self._gx`` and y the runtime's output."""
         n = self._check_tokens(target, "target")
+        if self.uses_tensor_cores(index, n):
+            return self.step_mse_tc(index, x, target)
         y = self.forward(index, x, self._z)
         if n != y.shape[0]:
             raise ValueError("target must have the N of x")
@@ -211,6 +242,41 @@ class HFFNTrainRuntime:
         self._backward(index, gy, self._next_step(index))
         self.runtime.mark_updated(index)
         return self._loss
+
+    def _reserve_tc(self, n: int) -> None:
+        self.reserve(n)
+        if n > self._tc_tokens:
+            size = int(native.lib.hffn_train_step_tc_workspace(self.runtime._structs[0], n))
+            self._tc_work = torch.empty(size, dtype=torch.uint8, device=self.runtime.device)
+            self._tc_tokens = n
+            self.growths += 1
+
+    def step_mse_tc(self, index: int, x: torch.Tensor, target: torch.Tensor, n_total: int | None = None,
+                    apply: bool = True) -> torch.Tensor:
+        """The MSE step on the tensor cores. ``n_total``: tokens of the loss mean (all ranks' for data parallelism).
+        ``apply=False``: gradients stored, nothing updated (the caller exchanges them, then ``apply_adamw``)."""
+        runtime = self.runtime
+        n = self._check_tokens(x, "x")
+        if self._check_tokens(target, "target") != n:
+            raise ValueError("target must have the N of x")
+        self._reserve_tc(n)
+        if runtime._dense_stale[index]:
+            runtime._densify(index)
+        params = self._fused_structs[index] if apply else self._param_structs[index]
+        status = native.lib.hffn_train_step_tc(runtime._structs[index], runtime._dense_structs[index], x.data_ptr(),
+                                               target.data_ptr(), runtime._y.data_ptr(), self._gx.data_ptr(), params,
+                                               self._next_step(index) if apply else None, self._loss.data_ptr(),
+                                               self._tc_work.data_ptr(), runtime._err.data_ptr(), n, n_total or n,
+                                               native.stream_handle(runtime.device))
+        native.check(status, "hffn_train_step_tc")
+        self._saved = None
+        runtime.calls[TC, TC] += 1
+        self.calls[TC, TC] += 1
+        return self._loss
+
+    def apply_adamw(self, index: int) -> None:
+        """AdamW from the stored gradients (after a data-parallel exchange); the dense operands are rebuilt lazily."""
+        self.adamw(index)
 
     # -- read access for the checks (views, no copy) -------------------------------------------------------------
     def parameters(self, index: int) -> dict[str, torch.Tensor]:

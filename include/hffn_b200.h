@@ -177,6 +177,23 @@ int64_t hffn_forward_tc_workspace(int dtype, const hffn_layer* layer, int64_t n)
 int hffn_forward_tc(int dtype, const hffn_layer* layer, const hffn_dense* dense, const void* x, void* y, float* z,
                     void* work, int32_t* err, int64_t n, void* stream);
 
+/* Bytes of the workspace hffn_train_step_tc needs for n tokens. */
+int64_t hffn_train_step_tc_workspace(const hffn_layer* layer, int64_t n);
+
+/* One MSE training step on the tcgen05 tensor cores (float32, 3xTF32): forward, loss, backward and AdamW, the
+ * tensor-core form of HFFNTrainRuntime.step (runtime/gpu/nvidia/ffn/training/train_runtime.py:209-214) with the
+ * training benchmark's MSE loss. Six GEMMs over the dense operands (up; down with the MSE gradient in its epilogue;
+ * W_down^T gy with gelu'; W_up^T gz; gy^T act and gz^T x sampled on the supports). With adamw != NULL every gradient
+ * entry is applied by AdamW in the epilogue that completes it and the dense operands are refreshed in place (so
+ * they stay consistent with the compact values); gradients are stored where params->*.grad != NULL. With
+ * adamw == NULL the gradients are stored and nothing is updated (data parallelism: exchange, then hffn_adamw and
+ * hffn_densify). gy = 2 (y - target) / (n_total d_model); *loss = mean((y - target)^2) over this call's n tokens.
+ * Requires d_model and d_ff multiples of 32 and, for the sampled update, the up slots of each neuron in ascending
+ * input order (the output-major down edges always are). x, target, y, gx token-major [n, d_model]. */
+int hffn_train_step_tc(const hffn_layer* layer, const hffn_dense* dense, const float* x, const float* target,
+                       float* y, float* gx, const hffn_train_params* params, const hffn_adamw_step* adamw,
+                       float* loss, void* work, int32_t* err, int64_t n, int64_t n_total, void* stream);
+
 /* Forward that allocates nothing and needs no workspace from the caller. No counterpart in the reference.
  * Some callers can hand this library only their input and output buffers: a plugin whose host framework owns every
  * device allocation and exposes no allocator, or a caller that must not call cudaMalloc on its path (it can
