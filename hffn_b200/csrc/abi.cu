@@ -26,6 +26,8 @@ int64_t tc_forward_workspace(int dtype, const hffn_layer* L, int64_t n);
 int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const void* b, void* act_hi, void* act_lo,
           float* z, void* x_split, int* err, int d, int H, int64_t n, cudaStream_t s);
 int64_t tc_train_workspace(const hffn_layer* L, int64_t n);
+int tc_gemm_f32(int a_mn, int b_mn, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
+                float* d, int M, int N, int K, int64_t lda, int64_t ldb, int* err, cudaStream_t s);
 int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, const void* down_hi, const void* down_lo,
                   const float* x, const float* target, float* y, float* gx, const hffn_train_params* P,
                   const hffn_adamw_step* opt, float* loss, void* work, int* err, int64_t n, int64_t n_total,
@@ -257,6 +259,18 @@ int hffn_down_tc(int dtype, const void* act_hi, const void* act_lo, const void* 
   HFFN_TRY(bind_stream_device(stream));
   return tc_down(dtype, act_hi, act_lo, w_hi, w_lo, b_down, y, err, d_model, d_ff, n,
                  static_cast<cudaStream_t>(stream));
+}
+
+int hffn_gemm_tc_f32(int a_mn, int b_mn, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
+                     float* d, int32_t m, int32_t n, int32_t k, int64_t lda, int64_t ldb, int32_t* err, void* stream) {
+  HFFN_REQUIRE(a_hi && a_lo && b_hi && b_lo && d && err, "null pointer argument");
+  HFFN_REQUIRE(m >= 1 && n >= 1 && k >= 1, "empty GEMM");
+  HFFN_REQUIRE(k % 4 == 0 && (!a_mn || (m % 32 == 0 && lda >= m && lda % 4 == 0)) &&
+                   (!b_mn || (n % 32 == 0 && ldb >= n && ldb % 4 == 0)),
+               "GEMM shape: K a multiple of 4, MN-major extents multiples of 32");
+  HFFN_REQUIRE(aligned16(a_hi) && aligned16(a_lo) && aligned16(b_hi) && aligned16(b_lo), "operands 16-byte aligned");
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_gemm_f32(a_mn, b_mn, a_hi, a_lo, b_hi, b_lo, d, m, n, k, lda, ldb, err, static_cast<cudaStream_t>(stream));
 }
 
 int64_t hffn_train_step_tc_workspace(const hffn_layer* layer, int64_t n) {

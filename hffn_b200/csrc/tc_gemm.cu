@@ -112,12 +112,14 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
          ((uint64_t)1 << 46) | (layout << 61);
 }
 
-// Shared-memory matrix descriptor of an MN-major operand: blocks of 32 MN elements (128 bytes) x BK K rows written by
-// TMA with the 128-byte swizzle; MN blocks `lbo` bytes apart (leading byte offset), 8-row K groups 1024 bytes apart
-// (stride byte offset), descriptor version 1, layout type 2.
+// Shared-memory matrix descriptor of an MN-major 32-bit (tf32) operand. The only MN-major layout of tf32 operands is the
+// 128-byte swizzle with 32-byte atomicity (layout type 1): atoms of 128 bytes of MN (32 elements) x 4 K rows, the
+// 32-byte granules of a row XORed with the row index mod 4 (TMA's CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B writes it).
+// Blocks of 32 MN elements x BK K rows: MN blocks `lbo` bytes apart (leading byte offset), 4-row K groups 512 bytes
+// apart (stride byte offset), descriptor version 1.
 __device__ __forceinline__ uint64_t smem_desc_mn(uint32_t addr, uint32_t lbo) {
-  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) | ((uint64_t)(512 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)1 << 61);
 }
 
 // Instruction descriptor: fp32 accumulator, A/B format (tf32 = 2, bf16 = 1), A/B major (0 K, 1 MN), N = bn, M = 128.
@@ -676,8 +678,8 @@ static int sm_count() {
   return count;
 }
 
-// [rows, k] K-major operand, or, mn_major, an operand whose element (mn, k) sits at base + k * ld + mn: boxes of 32 MN
-// elements x k_box K rows (128-byte swizzle). Zero fill outside.
+// An MN-major float32 operand whose element (mn, k) sits at base + k * ld + mn: boxes of 32 MN elements x k_box K rows,
+// 128-byte swizzle with 32-byte atomicity (the layout the MMA reads for MN-major tf32). Zero fill outside.
 static int make_map_mn(CUtensorMap* map, const void* base, int64_t mn, int64_t k, int64_t ld, int k_box) {
   auto fn = encode_fn();
   if (fn == nullptr) {
@@ -689,8 +691,8 @@ static int make_map_mn(CUtensorMap* map, const void* base, int64_t mn, int64_t k
   cuuint32_t box[2] = {32, (cuuint32_t)k_box};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d) for an MN-major [%lld, %lld] operand", (int)r, (long long)mn,
               (long long)k);
@@ -956,6 +958,27 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   HFFN_TRY(launch_status("bias_reduce up"));
   loss_reduce_kernel<<<1, 256, 0, s>>>(w.loss_p, (int64_t)rows * d, 1.0 / ((double)n * d), loss);
   return launch_status("loss_reduce");
+}
+
+// D^T [N, M] = (A B^T)^T for the operand layouts of the training GEMMs: A [M, K] K-major or stored [K, M] (MN-major,
+// leading dimension lda), B likewise; float32 3xTF32 hi / lo parts, plain y-store epilogue. A test entry of the GEMM
+// engine itself.
+int tc_gemm_f32(int a_mn, int b_mn, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
+                float* d, int M, int N, int K, int64_t lda, int64_t ldb, int* err, cudaStream_t s) {
+  using namespace tc;
+  EpilogueArgs e{};
+  e.out_hi = d;
+  if (!a_mn && !b_mn)
+    return launch_gemm<false, kTrainBN, 4, kDown, kFp32Chunk, 64, 8, false, false>(a_hi, a_lo, b_hi, b_lo, M, N, K, e,
+                                                                                   err, s, lda, ldb);
+  if (a_mn && !b_mn)
+    return launch_gemm<false, kTrainBN, 4, kDown, kFp32Chunk, 64, 8, true, false>(a_hi, a_lo, b_hi, b_lo, M, N, K, e,
+                                                                                  err, s, lda, ldb);
+  if (!a_mn && b_mn)
+    return launch_gemm<false, kTrainBN, 4, kDown, kFp32Chunk, 64, 8, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K, e,
+                                                                                  err, s, lda, ldb);
+  return launch_gemm<false, kTrainBN, 4, kDown, kFp32Chunk, 64, 8, true, true>(a_hi, a_lo, b_hi, b_lo, M, N, K, e, err,
+                                                                               s, lda, ldb);
 }
 
 int64_t tc_forward_workspace(int dtype, const hffn_layer* L, int64_t n) {

@@ -177,6 +177,12 @@ int64_t hffn_forward_tc_workspace(int dtype, const hffn_layer* layer, int64_t n)
 int hffn_forward_tc(int dtype, const hffn_layer* layer, const hffn_dense* dense, const void* x, void* y, float* z,
                     void* work, int32_t* err, int64_t n, void* stream);
 
+/* The GEMM engine of the tensor-core path alone (a test entry; no reference counterpart): out [n, m] = (A B^T)^T with
+ * A [m, k] (a_mn = 0: K contiguous) or stored [k, m] (a_mn = 1, leading dimension lda), B [n, k] or stored [k, n]
+ * (ldb), float32 operands as tf32 hi / lo parts (3xTF32). */
+int hffn_gemm_tc_f32(int a_mn, int b_mn, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
+                     float* out, int32_t m, int32_t n, int32_t k, int64_t lda, int64_t ldb, int32_t* err, void* stream);
+
 /* Bytes of the workspace hffn_train_step_tc needs for n tokens. */
 int64_t hffn_train_step_tc_workspace(const hffn_layer* layer, int64_t n);
 
