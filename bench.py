@@ -420,9 +420,11 @@ def train_arm(args, workload: dict, rank: int, world: int, local: int, device) -
     kl = HFFNLayer.from_hidden_major(layer.d_model, layer.d_ff, t(layer.b_up), t(layer.up_offsets), t(layer.up_idx),
                                      t(layer.up_val), t(layer.b_down), t(layer.down_offsets), t(layer.down_idx),
                                      t(layer.down_val))
-    runtime = HFFNRuntime([kl], device, tensor_cores=False)
+    runtime = HFFNRuntime([kl], device, tensor_cores=False if args.path == "cuda_cores" else None)
     train = HFFNTrainRuntime(runtime, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-2, max_tokens=n,
-                             store_gradients=world > 1)
+                             store_gradients=world > 1,
+                             tensor_cores={"cuda_cores": False, "tensor_cores": True}.get(args.path))
+    tc = train.uses_tensor_cores(0, n)
     train.reserve(n)
     x_host = t(rank_input(case, n, rank)).pin_memory()
     target_host = t(synth.make_target(case, n) if rank == 0 else rank_input(case, n, rank + 500)).pin_memory()
@@ -472,23 +474,40 @@ def train_arm(args, workload: dict, rank: int, world: int, local: int, device) -
                   + 2 * e * 24)                 # AdamW: p, m, v read and written, both value arrays
     seconds = total_s / args.steps
     achieved = step_bytes / seconds / 1e9
+    if tc:
+        dense_flops = 6 * 2.0 * case.d_model * case.d_ff * n * 3      # six GEMMs, three tf32 passes each
+        roofline = {"bound": "tensor", "kernel": "whole step (six tcgen05 GEMMs)", "achieved": flops / seconds / 1e12,
+                    "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": flops / seconds / 1e12 / pk["bf16_tflops"],
+                    "traffic": None, "algorithmic_flops": flops, "peak_source": pk_source,
+                    "tensor_pipe": {"kind": "tf32 x3 (3xTF32 split)", "executed_tflops": dense_flops / seconds / 1e12,
+                                    "peak_tflops": pk["bf16_tflops"] / 2,
+                                    "peak_note": "tf32 = half the measured bf16 peak (nominal ratio)",
+                                    "frac": dense_flops / seconds / 1e12 / (pk["bf16_tflops"] / 2)},
+                    "hbm": {"achieved_gbs": achieved, "peak_gbs": pk["hbm_gbs"], "frac": achieved / pk["hbm_gbs"],
+                            "algorithmic_bytes": step_bytes},
+                    "fp32_cuda_cores": {"achieved_tflops": flops / seconds / 1e12, "peak_tflops": fp32_peak,
+                                        "frac": flops / seconds / 1e12 / fp32_peak if fp32_peak else None}}
+    else:
+        roofline = {"bound": "hbm", "kernel": "whole step", "achieved": achieved, "peak": pk["hbm_gbs"],
+                    "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                    "algorithmic_bytes": step_bytes, "peak_source": pk_source,
+                    "fp32_cuda_cores": {"achieved_tflops": flops / seconds / 1e12, "peak_tflops": fp32_peak,
+                                        "frac": flops / seconds / 1e12 / fp32_peak if fp32_peak else None}}
     return {
         "metric": "HFFN FFN layer tokens/s (train step, fp32)", "value": n * world * args.steps / total_s,
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * seconds, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{case.name}: d_model {case.d_model}, d_ff {case.d_ff}, support {case.up_degree}, "
-                               f"N {n} tokens per GPU per step, MSE loss, AdamW", "path": "cuda_cores",
+                               f"N {n} tokens per GPU per step, MSE loss, AdamW",
+                   "path": "tensor_cores" if tc else "cuda_cores",
                    "parallelism": f"data parallel x{world}, gradient all-reduce over NCCL" if world > 1 else "single",
                    "l2": "inputs larger than L2 (z and act alone 537 MB)"},
-        "roofline": {"bound": "hbm", "kernel": "whole step", "achieved": achieved, "peak": pk["hbm_gbs"],
-                     "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
-                     "algorithmic_bytes": step_bytes, "peak_source": pk_source,
-                     "fp32_cuda_cores": {"achieved_tflops": flops / seconds / 1e12, "peak_tflops": fp32_peak,
-                                         "frac": flops / seconds / 1e12 / fp32_peak if fp32_peak else None}},
+        "roofline": roofline,
         "e2e": {"value": n * world * args.steps / e2e_s, "unit": "tokens/s",
                 "h2d_bytes_per_step": 2 * x_host.numel() * 4, "d2h_bytes_per_step": loss_host.numel() * 8},
-        "gpu_launches": None, "device_errors": runtime.device_errors(), "clocks": clocks.summary(),
+        "gpu_launches": (10 if tc else 8) * args.steps, "device_errors": runtime.device_errors(),
+        "clocks": clocks.summary(),
         "loss_last": float(loss_host),
     }
 
