@@ -64,12 +64,20 @@ def pythia_410m(tmp_path_factory):
     return root
 
 
-def test_pythia_410m_bf16_tokens(pythia_410m):
-    """The benchmark model in bfloat16: prefill of 8 x 512 tokens, then 32 greedy steps (arbiter-driven)."""
-    dense = pythia_dense.dense_pythia(pythia_410m / "model", pythia_410m / "export", "cuda", torch.bfloat16)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_pythia_410m_tokens(pythia_410m, dtype):
+    """The benchmark model: prefill of 8 x 512 tokens, then 32 greedy steps (arbiter-driven). float32: the reference's
+    criterion as it is (its loader path is float32); bfloat16: the same criterion with the control's global band."""
+    dense = pythia_dense.dense_pythia(pythia_410m / "model", pythia_410m / "export", "cuda", dtype)
     arbiter = pythia_dense.dense_pythia(pythia_410m / "model", pythia_410m / "export", "cuda", torch.float64)
-    hffn = pythia.load_pythia(pythia_410m / "model", pythia_410m / "export", "hffn", "cuda", torch.bfloat16)
+    hffn = pythia.load_pythia(pythia_410m / "model", pythia_410m / "export", "hffn", "cuda", dtype)
     ps = prompts(50277, ((8, 512),), 3004)
-    result = pythia_dense.check_arm(dense, hffn, arbiter, ps, steps=32)
+    band = "pointwise" if dtype == torch.float32 else "global"
+    result = pythia_dense.check_arm(dense, hffn, arbiter, ps, steps=32, band=band)
+    print(f"pythia-410m {dtype}: {result}")
     assert result["unexplained"] == 0, result
     assert hffn.hffn_runtime.device_errors() == 0
+    with torch.no_grad():
+        hffn.gpt_neox.layers[3].attention.dense.weight.mul_(1.5)
+    faulty = pythia_dense.check_arm(dense, hffn, arbiter, ps, steps=8, band=band)
+    assert faulty["unexplained"] > 0, faulty
