@@ -37,6 +37,8 @@ WORKLOADS = {
     "fwd_bf16": {"case": "c2_1024_4096_k512", "n": 4096, "dtype": "bf16"},
     "train": {"case": "c3_2048_8192_k1638", "n": 8192, "dtype": "fp32"},
     "train_small": {"case": "c3_2048_8192_k1638", "n": 1024, "dtype": "fp32"},
+    "pythia410m": {"case": "c4_1024_4096_k512", "n": 8 * 512, "dtype": "bf16", "batch": 8, "prompt": 512,
+                   "decode": 128},
 }
 CLOCK_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
                "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -223,6 +225,8 @@ def gpu_arm(args, workload: dict) -> dict | None:
     rank, world, local, device = setup_dist(torch)
     if args.workload.startswith("train"):
         return train_arm(args, workload, rank, world, local, device)
+    if args.workload == "pythia410m":
+        return pythia_arm(args, workload, rank, world, local, device)
     case = synth.CASES[workload["case"]]
     n = workload["n"]
     dtype = torch.float32 if workload["dtype"] == "fp32" else torch.bfloat16
@@ -510,6 +514,61 @@ def train_arm(args, workload: dict, rank: int, world: int, local: int, device) -
         "clocks": clocks.summary(),
         "loss_last": float(loss_host),
     }
+
+
+def pythia_arm(args, workload: dict, rank: int, world: int, local: int, device) -> dict | None:
+    """The Pythia-410M architecture (random init, 50 % HFFN FFNs, bfloat16): prefill of batch x prompt tokens, then
+    greedy decode steps with the KV cache; the HFFN arm and the dense arm (the model's own MLP with the same weights
+    on the support) timed back to back on the same prompts."""
+    import tempfile
+
+    import torch
+
+    from hffn_b200 import pythia
+    root = Path(tempfile.gettempdir()) / "hffn_bench_pythia410m"
+    if not (root / "model" / "model.safetensors").exists():
+        pythia.make_random_pythia(root / "model", root / "export", pythia.PYTHIA_410M, support=512, seed=3004)
+    b, t, steps = workload["batch"], workload["prompt"], workload["decode"]
+    g = torch.Generator().manual_seed(3004)
+    prompt = torch.randint(0, 50277, (b, t), generator=g).to(device)
+    stream = torch.cuda.current_stream(device)
+    results = {}
+    for arm in ("hffn", "dense"):
+        model = pythia.load_pythia(root / "model", root / "export", arm, device, torch.bfloat16)
+
+        @torch.inference_mode()
+        def run():
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            e[0].record(stream)
+            out = model(input_ids=prompt, use_cache=True)
+            e[1].record(stream)
+            cache, token = out.past_key_values, out.logits[:, -1:].argmax(-1)
+            for _ in range(steps):
+                out = model(input_ids=token, past_key_values=cache, use_cache=True)
+                cache, token = out.past_key_values, out.logits[:, -1:].argmax(-1)
+            e[2].record(stream)
+            e[2].synchronize()
+            return e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2])
+
+        for _ in range(args.warmup):
+            run()
+        prefill, decode = zip(*[run() for _ in range(args.steps)])
+        results[arm] = {"prefill_ms": statistics.median(prefill), "decode_ms": statistics.median(decode)}
+        if arm == "hffn":
+            results[arm]["device_errors"] = model.hffn_runtime.device_errors()
+            results[arm]["ffn_calls"] = {f"{u}/{d}": c for (u, d), c in model.hffn_runtime.calls.items()}
+        del model
+        torch.cuda.empty_cache()
+    h, d = results["hffn"], results["dense"]
+    tokens = b * t + b * steps
+    return {"metric": "Pythia-410M (50 % HFFN FFNs, bf16) tokens/s: prefill 8 x 512 + 128 greedy decode steps",
+            "value": tokens / ((h["prefill_ms"] + h["decode_ms"]) / 1e3), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random init, uniform token ids)",
+            "config": {"workload": "pythia-410m architecture, 24 layers, d_model 1024, d_ff 4096, 512-of-1024 supports"},
+            "prefill_tokens_per_s": {"hffn": b * t / (h["prefill_ms"] / 1e3), "dense": b * t / (d["prefill_ms"] / 1e3)},
+            "decode_tokens_per_s": {"hffn": b * steps / (h["decode_ms"] / 1e3), "dense": b * steps / (d["decode_ms"] / 1e3)},
+            "arms_ms": results}
 
 
 def main() -> int:

@@ -5,7 +5,7 @@ model.py:11-28``).
 ``load_pythia(model_dir, export_dir, ffn, device, dtype)`` builds the GPT-NeoX model of ``model_dir/config.json``,
 loads every non-FFN tensor of ``model_dir/model.safetensors`` and reads the compact FFNs of ``export_dir``
 (``hffn_training_compact_g4_v2``). ``ffn="hffn"``: every ``block.mlp`` is an ``HFFNMLP`` that hands its activations to
-one shared ``HFFNRuntime`` (no dense FFN weight is ever allocated); ``ffn="dense"``: the model's own MLP with its
+one shared ``PreparedRuntime`` (decode-sized calls prepared once; no dense FFN weight is ever allocated); ``ffn="dense"``: the model's own MLP with its
 weights set from the export on the support and zero elsewhere (the control arm of the checks). Embeddings,
 attention (PyTorch SDPA), LayerNorm, KV cache and head stay PyTorch in both arms. The HFFN arm exposes its runtime
 as ``model.hffn_runtime``. ``dtype`` float32 (the reference's only type) or bfloat16.
@@ -112,9 +112,9 @@ def load_pythia(model_dir: str | Path, export_dir: str | Path, ffn: str, device:
         for block, layer in zip(blocks, layers):
             set_dense_mlp(block.mlp, layer)
     else:
-        from .runtime import HFFNRuntime
-        runtime = HFFNRuntime([export.kernel_layer(layer) for layer in layers], device, dtype,
-                              tensor_cores=tensor_cores)
+        from .runtime import PreparedRuntime
+        runtime = PreparedRuntime([export.kernel_layer(layer) for layer in layers], device, dtype,
+                                  tensor_cores=tensor_cores)
         for index, block in enumerate(blocks):
             block.mlp = HFFNMLP(runtime, index)
     model = model.to(device=device, dtype=dtype).eval().requires_grad_(False)

@@ -257,3 +257,46 @@ class HFFNRuntime:
                                          native.stream_handle(self.device))
         native.check(status, "hffn_forward")
         return up, down
+
+
+class PreparedRuntime(HFFNRuntime):
+    """``HFFNRuntime`` whose small-batch calls (the decode steps) skip the per-call resolution: the drop-in of the
+    reference's ``runtime/gpu/nvidia/llm/inference/hffn_pythia_cuda/prepared_runtime.py:34-82``.
+
+    A call with N <= ``PREPARED_MAX_TOKENS`` tokens and no forced mode looks up a prepared entry of (layer, N): the
+    layer's struct, the kernel mode codes and the device pointers of the runtime's ``act`` and ``y`` buffers, resolved
+    once; the call then checks ``x`` and issues one ``hffn_forward``. ``_reserve`` (buffers moved) and ``force`` drop
+    every entry. Every other call is ``HFFNRuntime.forward``. The kernels allocate nothing and run on the caller's
+    current stream, so a prepared call can be captured in a CUDA graph (after one call outside the capture).
+    """
+
+    PREPARED_MAX_TOKENS = 8
+
+    def _reserve(self, n: int) -> None:
+        super()._reserve(n)
+        self._prepared: dict = {}
+
+    def force(self, up, down) -> None:
+        super().force(up, down)
+        self._prepared = {}
+
+    def forward(self, index: int, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        n = x.shape[0] if x.dim() == 2 else 0
+        if out is not None or self.forced_up or self.forced_down or not 1 <= n <= self.PREPARED_MAX_TOKENS:
+            return super().forward(index, x, out)
+        entry = self._prepared.get((index, n))
+        if entry is None:
+            self._check_input(x)
+            if n > self._tokens:
+                self._reserve(n)
+            up, down = self.modes(n)
+            entry = (self._structs[index], native.UP_CODES[up], native.DOWN_CODES[down], self._act.data_ptr(),
+                     self._y.data_ptr(), (up, down))
+            self._prepared[(index, n)] = entry
+        elif x.dtype != self.dtype or x.shape[1] != self.d_model or x.device != self._y.device or not x.is_contiguous():
+            raise ValueError(f"expected a contiguous {self.dtype} [N, d_model] tensor on the runtime's device")
+        struct, up_code, down_code, act, y, modes = entry
+        native.check(native.lib.hffn_forward(self._code, struct, x.data_ptr(), y, act, None, n, up_code, down_code,
+                                             native.stream_handle(self.device)), "hffn_forward")
+        self.calls[modes] += 1
+        return self._y[:n]

@@ -130,3 +130,32 @@ def test_device_layout_validation():
     native.check(native.lib.hffn_validate_layout(layer_struct(bad, runtime.d_model, runtime.d_ff), flag.data_ptr(),
                                                  stream), "validate")
     assert int(flag) == 1
+
+
+def test_prepared_runtime_and_cuda_graph():
+    """The decode fast path gives the bits of the plain runtime, and a prepared call replays inside a CUDA graph."""
+    from hffn_b200.runtime import PreparedRuntime
+    case = synth.TEST_CASES["homog_512_2048"]
+    layer = synth.make_layer(case)
+    plain = runtime_for(layer)
+    prepared = PreparedRuntime([kernel_layer(layer)], "cuda")
+    for n in (1, 4, 8, 9):
+        x = torch.from_numpy(synth.make_input(case, n)).cuda()
+        expected = plain.forward(0, x).clone()
+        assert torch.equal(prepared.forward(0, x).clone(), expected)
+        assert torch.equal(prepared.forward(0, x).clone(), expected)      # second call: the prepared entry
+    x = torch.from_numpy(synth.make_input(case, 4)).cuda()
+    static_x = x.clone()
+    prepared.forward(0, static_x)
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            y_graph = prepared.forward(0, static_x)
+    torch.cuda.current_stream().wait_stream(stream)
+    x2 = torch.from_numpy(synth.make_input(case, 7)[:4]).cuda()
+    static_x.copy_(x2)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y_graph, plain.forward(0, x2))
