@@ -55,12 +55,18 @@ inline int launch_status(const char* what) {
   return HFFN_OK;
 }
 
-// Make the device of `stream` current for the launches of one call (a null stream keeps the current device).
+// Make the device of `stream` current for the launches of one call (a null stream keeps the current device). A stream
+// being captured into a CUDA graph is left as it is: the capture runs on the current device, and device queries and
+// switches are not permitted during a capture.
 inline int bind_stream_device(void* stream) {
   if (stream == nullptr) return HFFN_OK;
-  int device = -1;
-  cudaError_t e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &device);
-  if (e == cudaSuccess) e = cudaSetDevice(device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &capture) == cudaSuccess && capture != cudaStreamCaptureStatusNone) return HFFN_OK;
+  int device = -1, current = -1;
+  cudaError_t e = cudaStreamGetDevice(s, &device);
+  if (e == cudaSuccess) e = cudaGetDevice(&current);
+  if (e == cudaSuccess && device != current) e = cudaSetDevice(device);
   if (e != cudaSuccess) {
     set_error("stream device: %s", cudaGetErrorString(e));
     return HFFN_ERR_CUDA;
