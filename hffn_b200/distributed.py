@@ -79,6 +79,10 @@ class ShardedFFN:
         # two ranks (the exchange is a few percent of the compute), up to four at eight.
         self.segments = segments or max(1, min(4, self.world // 2))
         self._buffers: dict = {}
+        # The reduce-scatters run on a second communicator of the same ranks, so that they proceed concurrently with
+        # the gathers (the other NVLink direction) instead of queueing behind them on one NCCL stream.
+        ranks = [dist.get_global_rank(group, k) if group is not None else k for k in range(self.world)]
+        self.scatter_group = dist.new_group(ranks=ranks) if self.world > 1 else group
         self._ranks = [dist.get_global_rank(group, k) if group is not None else k for k in range(self.world)]
 
     def forward_replicated(self, x: torch.Tensor) -> torch.Tensor:
@@ -122,11 +126,11 @@ class ShardedFFN:
 
     def _reduce_scatter(self, out: torch.Tensor, partial: torch.Tensor):
         if dist.get_backend(self.group) == "gloo":      # gloo has no reduce-scatter: all-reduce and keep the slice
-            dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
+            dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.scatter_group)
             m = out.shape[0]
             out.copy_(partial[self.rank * m:(self.rank + 1) * m])
             return None
-        return dist.reduce_scatter_tensor(out, partial, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+        return dist.reduce_scatter_tensor(out, partial, op=dist.ReduceOp.SUM, group=self.scatter_group, async_op=True)
 
 
 def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, tensor_cores=None, group=None):
