@@ -241,7 +241,8 @@ def gpu_arm(args, workload: dict) -> dict | None:
         runtime, shard, (lo, hi) = HFFNRuntime([kl], device, dtype, tensor_cores=tensor_cores), None, (0, case.d_ff)
     else:
         runtime, shard, (lo, hi) = sharded_runtime(case.d_model, canonical(layer, torch), device, dtype,
-                                                   tensor_cores=tensor_cores)
+                                                   tensor_cores=tensor_cores, segments=args.segments,
+                                                   comm_sms=args.comm_sms)
     if args.path == "tensor_cores":
         runtime.force("tc", "tc")
     d, f_local = case.d_model, hi - lo
@@ -389,7 +390,9 @@ def gpu_arm(args, workload: dict) -> dict | None:
         "dtype": "f32" if elem == 4 else "bf16", "data": "synthetic",
         "config": {"workload": f"{case.name}: d_model {d}, d_ff {case.d_ff}, support {case.up_degree}, "
                                f"N {n} tokens per GPU per step", "modes": [up, down],
-                   "parallelism": f"neuron-sharded x{world} (broadcast / reduce over NCCL)" if world > 1 else "single",
+                   "parallelism": f"neuron-sharded x{world} (all-gather / reduce-scatter pipeline over NCCL, "
+                                  f"{shard.segments} segments, {shard.comm_sms} SMs left to NCCL)" if world > 1
+                   else "single",
                    "l2": "flushed between steps (512 MiB write)"},
         "roofline": roofline,
         "fp32_gemm_peak_tflops": fp32_peak,
@@ -581,6 +584,8 @@ def main() -> int:
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--ref-tokens", type=int, default=512)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--segments", type=int, default=None, help="sharded forward: pipeline segments per step")
+    parser.add_argument("--comm-sms", type=int, default=16, help="sharded forward: SMs left to the collectives")
     parser.add_argument("--path", choices=("auto", "cuda_cores", "tensor_cores"), default="auto",
                         help="forward kernels: the runtime policy, the CUDA-core gather kernels, or the tcgen05 path")
     args = parser.parse_args()

@@ -26,6 +26,7 @@ int64_t tc_forward_workspace(int dtype, const hffn_layer* L, int64_t n);
 int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const void* b, void* act_hi, void* act_lo,
           float* z, void* x_split, int* err, int d, int H, int64_t n, cudaStream_t s);
 int64_t tc_train_workspace(const hffn_layer* L, int64_t n);
+void tc_set_max_ctas(int max_ctas);
 int tc_gemm_f32(int a_mn, int b_mn, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
                 float* d, int M, int N, int K, int64_t lda, int64_t ldb, int* err, cudaStream_t s);
 int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, const void* down_hi, const void* down_lo,
@@ -259,6 +260,12 @@ int hffn_down_tc(int dtype, const void* act_hi, const void* act_lo, const void* 
   HFFN_TRY(bind_stream_device(stream));
   return tc_down(dtype, act_hi, act_lo, w_hi, w_lo, b_down, y, err, d_model, d_ff, n,
                  static_cast<cudaStream_t>(stream));
+}
+
+int hffn_set_tc_max_ctas(int32_t max_ctas) {
+  HFFN_REQUIRE(max_ctas >= 0, "negative CTA cap");
+  tc_set_max_ctas(max_ctas);
+  return HFFN_OK;
 }
 
 int hffn_gemm_tc_f32(int a_mn, int b_mn, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,

@@ -24,6 +24,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <climits>
 
 #include "common.cuh"
@@ -667,6 +668,10 @@ static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k,
   return HFFN_OK;
 }
 
+// CTA cap of the persistent GEMMs (0: one CTA per SM). Leaving SMs free lets collectives (NCCL kernels) run
+// alongside a GEMM instead of after it.
+static std::atomic<int> g_max_ctas{0};
+
 static int sm_count() {
   static int count = 0;
   if (count == 0) {
@@ -675,7 +680,8 @@ static int sm_count() {
     cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
     if (count <= 0) count = 148;
   }
-  return count;
+  const int cap = g_max_ctas.load();
+  return cap > 0 && cap < count ? cap : count;
 }
 
 // An MN-major float32 operand whose element (mn, k) sits at base + k * ld + mn: boxes of 32 MN elements x k_box K rows,
@@ -980,6 +986,8 @@ int tc_gemm_f32(int a_mn, int b_mn, const float* a_hi, const float* a_lo, const 
   return launch_gemm<false, kTrainBN, 4, kDown, kFp32Chunk, 64, 8, true, true>(a_hi, a_lo, b_hi, b_lo, M, N, K, e, err,
                                                                                s, lda, ldb);
 }
+
+void tc_set_max_ctas(int max_ctas) { tc::g_max_ctas.store(max_ctas > 0 ? max_ctas : 0); }
 
 int64_t tc_forward_workspace(int dtype, const hffn_layer* L, int64_t n) {
   if (dtype == HFFN_BF16) return n * L->d_ff * 2;

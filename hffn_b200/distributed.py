@@ -69,7 +69,7 @@ class ShardedFFN:
     process group."""
 
     def __init__(self, local_forward: Callable[[torch.Tensor, torch.Tensor], None], d_model: int, group=None,
-                 segments: int | None = None) -> None:
+                 segments: int | None = None, comm_sms: int = 16) -> None:
         self.local_forward = local_forward
         self.d_model = d_model
         self.group = group
@@ -78,6 +78,8 @@ class ShardedFFN:
         # The exchange grows with the world size while a segment's GEMMs shrink with the segment count: one segment at
         # two ranks (the exchange is a few percent of the compute), up to four at eight.
         self.segments = segments or max(1, min(4, self.world // 2))
+        self.comm_sms = comm_sms
+        self._cuda = False
         self._buffers: dict = {}
         # The reduce-scatters run on a second communicator of the same ranks, so that they proceed concurrently with
         # the gathers (the other NVLink direction) instead of queueing behind them on one NCCL stream.
@@ -91,6 +93,13 @@ class ShardedFFN:
         self.local_forward(x, y)
         dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
         return y
+
+    def _limit_ctas(self, on: bool) -> None:
+        """While the pipeline runs, the persistent tensor-core GEMMs leave ``comm_sms`` SMs to the NCCL kernels."""
+        if self.comm_sms and x_is_cuda(self):
+            from . import _native as native
+            count = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+            native.lib.hffn_set_tc_max_ctas(count - self.comm_sms if on else 0)
 
     def forward(self, x_local: torch.Tensor, segments: int | None = None) -> torch.Tensor:
         """``y`` of this rank's own batch ``x_local`` (every rank passes a batch of the same shape).
@@ -109,6 +118,9 @@ class ShardedFFN:
                                    torch.empty(self.world * (bounds[s + 1] - bounds[s]), d, dtype=x_local.dtype,
                                                device=x_local.device)) for s in range(segments)]
         buffers = self._buffers[key]
+        self._cuda = x_local.is_cuda
+        if segments > 1:
+            self._limit_ctas(True)
         gathers = []
         for s in range(segments):
             part = x_local[bounds[s]:bounds[s + 1]]
@@ -122,6 +134,8 @@ class ShardedFFN:
         for work in scatters:
             if work is not None:
                 work.wait()
+        if segments > 1:
+            self._limit_ctas(False)
         return out
 
     def _reduce_scatter(self, out: torch.Tensor, partial: torch.Tensor):
@@ -133,7 +147,12 @@ class ShardedFFN:
         return dist.reduce_scatter_tensor(out, partial, op=dist.ReduceOp.SUM, group=self.scatter_group, async_op=True)
 
 
-def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, tensor_cores=None, group=None):
+def x_is_cuda(ffn: "ShardedFFN") -> bool:
+    return ffn._cuda
+
+
+def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, tensor_cores=None, group=None,
+                    segments: int | None = None, comm_sms: int = 16):
     """The rank's ``HFFNRuntime`` over its neuron shard and the ``ShardedFFN`` around it."""
     from .runtime import HFFNLayer, HFFNRuntime
     rank, world = dist.get_rank(group), dist.get_world_size(group)
@@ -146,7 +165,9 @@ def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, ten
                                         shard["up_idx"], shard["up_val"], shard["b_down"], shard["down_offsets"],
                                         shard["down_idx"], shard["down_val"])
     runtime = HFFNRuntime([layer], device, dtype, tensor_cores=tensor_cores)
-    return runtime, ShardedFFN(lambda x, out: runtime.forward(0, x, out=out), d_model, group), (lo, hi)
+    ffn = ShardedFFN(lambda x, out: runtime.forward(0, x, out=out), d_model, group, segments=segments,
+                     comm_sms=comm_sms)
+    return runtime, ffn, (lo, hi)
 
 
 class DataParallelTrainer:

@@ -177,6 +177,11 @@ int64_t hffn_forward_tc_workspace(int dtype, const hffn_layer* layer, int64_t n)
 int hffn_forward_tc(int dtype, const hffn_layer* layer, const hffn_dense* dense, const void* x, void* y, float* z,
                     void* work, int32_t* err, int64_t n, void* stream);
 
+/* Cap on the CTAs of the persistent tensor-core GEMMs, process-wide (0: one per SM, the default). A tuning knob with
+ * no reference counterpart: the neuron-sharded forward leaves a few SMs to the NCCL kernels so that its collectives
+ * run alongside the GEMMs. */
+int hffn_set_tc_max_ctas(int32_t max_ctas);
+
 /* The GEMM engine of the tensor-core path alone (a test entry; no reference counterpart): out [n, m] = (A B^T)^T with
  * A [m, k] (a_mn = 0: K contiguous) or stored [k, m] (a_mn = 1, leading dimension lda), B [n, k] or stored [k, n]
  * (ldb), float32 operands as tf32 hi / lo parts (3xTF32). */
