@@ -585,7 +585,7 @@ def main() -> int:
     parser.add_argument("--ref-tokens", type=int, default=512)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--segments", type=int, default=None, help="sharded forward: pipeline segments per step")
-    parser.add_argument("--comm-sms", type=int, default=16, help="sharded forward: SMs left to the collectives")
+    parser.add_argument("--comm-sms", type=int, default=0, help="sharded forward: SMs left to the collectives")
     parser.add_argument("--path", choices=("auto", "cuda_cores", "tensor_cores"), default="auto",
                         help="forward kernels: the runtime policy, the CUDA-core gather kernels, or the tcgen05 path")
     args = parser.parse_args()
