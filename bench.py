@@ -242,7 +242,7 @@ def gpu_arm(args, workload: dict) -> dict | None:
     else:
         runtime, shard, (lo, hi) = sharded_runtime(case.d_model, canonical(layer, torch), device, dtype,
                                                    tensor_cores=tensor_cores, segments=args.segments,
-                                                   comm_sms=args.comm_sms)
+                                                   comm_sms=args.comm_sms, transport=args.transport)
     if args.path == "tensor_cores":
         runtime.force("tc", "tc")
     d, f_local = case.d_model, hi - lo
@@ -390,9 +390,11 @@ def gpu_arm(args, workload: dict) -> dict | None:
         "dtype": "f32" if elem == 4 else "bf16", "data": "synthetic",
         "config": {"workload": f"{case.name}: d_model {d}, d_ff {case.d_ff}, support {case.up_degree}, "
                                f"N {n} tokens per GPU per step", "modes": [up, down],
-                   "parallelism": f"neuron-sharded x{world} (all-gather / reduce-scatter pipeline over NCCL, "
-                                  f"{shard.segments} segments, {shard.comm_sms} SMs left to NCCL)" if world > 1
-                   else "single",
+                   "parallelism": "single" if world == 1 else
+                   f"neuron-sharded x{world} (peer memory: copy-engine pulls of the batches, partial outputs stored "
+                   f"into the owners' slots by the down GEMM)" if args.transport == "peer" else
+                   f"neuron-sharded x{world} (all-gather / reduce-scatter pipeline over NCCL, "
+                   f"{shard.segments} segments, {shard.comm_sms} SMs left to NCCL)",
                    "l2": "flushed between steps (512 MiB write)"},
         "roofline": roofline,
         "fp32_gemm_peak_tflops": fp32_peak,
@@ -586,6 +588,8 @@ def main() -> int:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--segments", type=int, default=None, help="sharded forward: pipeline segments per step")
     parser.add_argument("--comm-sms", type=int, default=0, help="sharded forward: SMs left to the collectives")
+    parser.add_argument("--transport", choices=("nccl", "peer"), default="nccl",
+                        help="sharded forward: NCCL collectives or NVLink peer memory (tensor cores)")
     parser.add_argument("--path", choices=("auto", "cuda_cores", "tensor_cores"), default="auto",
                         help="forward kernels: the runtime policy, the CUDA-core gather kernels, or the tcgen05 path")
     args = parser.parse_args()

@@ -27,6 +27,10 @@ int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const vo
           float* z, void* x_split, int* err, int d, int H, int64_t n, cudaStream_t s);
 int64_t tc_train_workspace(const hffn_layer* L, int64_t n);
 void tc_set_max_ctas(int max_ctas);
+int tc_down_peer(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo, const void* b,
+                 void* const* peers, int world, int64_t tokens_per_owner, int* err, int d, int H, int64_t n,
+                 cudaStream_t s);
+int tc_sum_slots(int dtype, const void* slots, int count, int64_t elems, void* out, cudaStream_t s);
 int tc_gemm_f32(int a_mn, int b_mn, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
                 float* d, int M, int N, int K, int64_t lda, int64_t ldb, int* err, cudaStream_t s);
 int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, const void* down_hi, const void* down_lo,
@@ -260,6 +264,31 @@ int hffn_down_tc(int dtype, const void* act_hi, const void* act_lo, const void* 
   HFFN_TRY(bind_stream_device(stream));
   return tc_down(dtype, act_hi, act_lo, w_hi, w_lo, b_down, y, err, d_model, d_ff, n,
                  static_cast<cudaStream_t>(stream));
+}
+
+int hffn_down_tc_peer(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo,
+                      const void* b_down, const uint64_t* peer_y, int32_t world, int64_t tokens_per_owner,
+                      int32_t* err, int32_t d_model, int32_t d_ff, int64_t n, void* stream) {
+  HFFN_TRY(check_tc(dtype, d_model, d_ff, n));
+  const bool f32 = dtype == HFFN_F32;
+  HFFN_REQUIRE(act_hi && w_hi && b_down && peer_y && err && (!f32 || (act_lo && w_lo)), "null pointer argument");
+  HFFN_REQUIRE(world >= 1 && world <= 8, "world %d outside [1, 8]", world);
+  HFFN_REQUIRE(tokens_per_owner >= 1 && n == (int64_t)world * tokens_per_owner, "n must be world x tokens_per_owner");
+  void* peers[8] = {};
+  for (int p = 0; p < world; ++p) {
+    HFFN_REQUIRE(peer_y[p] != 0, "null peer buffer %d", p);
+    peers[p] = reinterpret_cast<void*>(peer_y[p]);
+  }
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_down_peer(dtype, act_hi, act_lo, w_hi, w_lo, b_down, peers, world, tokens_per_owner, err, d_model, d_ff,
+                      n, static_cast<cudaStream_t>(stream));
+}
+
+int hffn_sum_slots(int dtype, const void* slots, int32_t count, int64_t elems, void* out, void* stream) {
+  HFFN_REQUIRE(dtype == HFFN_F32 || dtype == HFFN_BF16, "unknown dtype %d", dtype);
+  HFFN_REQUIRE(slots && out && count >= 1 && elems >= 0, "bad argument");
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_sum_slots(dtype, slots, count, elems, out, static_cast<cudaStream_t>(stream));
 }
 
 int hffn_set_tc_max_ctas(int32_t max_ctas) {

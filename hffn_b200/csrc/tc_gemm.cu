@@ -42,7 +42,11 @@ constexpr uint64_t kWaitNs = 2000000000ull;
 // kGradHidden: gz = acc * gelu'(z) as tf32 hi/lo, per-thread partial sums of gz per neuron. kSampled: the weight
 // gradient sampled at the support entries of each row (CSR, columns ascending), stored and / or applied by AdamW, the
 // dense operand refreshed with the new value.
-enum Epilogue { kUp = 0, kDown = 1, kDownMse = 2, kGradHidden = 3, kSampled = 4 };
+// kDownPeer: as kDown, the value of token t stored into the buffer of the rank that owns t (peer memory over NVLink):
+// peers[t / tokens_per_owner] + (t % tokens_per_owner) * M + row.
+enum Epilogue { kUp = 0, kDown = 1, kDownMse = 2, kGradHidden = 3, kSampled = 4, kDownPeer = 5 };
+
+constexpr int kMaxPeers = 8;
 
 // error codes written to the kernel's error flag
 constexpr int kErrTimeoutProducer = 101, kErrTimeoutMma = 102, kErrTimeoutEpilogue = 103;
@@ -199,6 +203,10 @@ struct EpilogueArgs {
   float* dense_lo;
   int adam;              // apply AdamW
   hffn_adamw_step step;
+  // kDownPeer
+  void* peers[kMaxPeers];
+  int64_t tokens_per_owner;
+  int64_t rows;          // M
 };
 
 // One value of the output tile: bias added, then (up) GELU and the stores of act (float32: tf32 hi and lo parts) and
@@ -220,6 +228,13 @@ __device__ __forceinline__ float2 emit_one(const EpilogueArgs* e, int64_t at, fl
   } else if constexpr (EPI == kDown) {
     if constexpr (kBf16) reinterpret_cast<__nv_bfloat16*>(e->out_hi)[at] = __float2bfloat16_rn(s);
     else reinterpret_cast<float*>(e->out_hi)[at] = s;
+    return make_float2(0.f, 0.f);
+  } else if constexpr (EPI == kDownPeer) {
+    const int64_t t = at / e->rows, row = at - t * e->rows;
+    const int64_t owner = t / e->tokens_per_owner, local = t - owner * e->tokens_per_owner;
+    const int64_t dst = local * e->rows + row;
+    if constexpr (kBf16) reinterpret_cast<__nv_bfloat16*>(e->peers[owner])[dst] = __float2bfloat16_rn(s);
+    else reinterpret_cast<float*>(e->peers[owner])[dst] = s;
     return make_float2(0.f, 0.f);
   } else if constexpr (EPI == kDownMse) {
     reinterpret_cast<float*>(e->out_hi)[at] = s;
@@ -985,6 +1000,43 @@ int tc_gemm_f32(int a_mn, int b_mn, const float* a_hi, const float* a_lo, const 
                                                                                   err, s, lda, ldb);
   return launch_gemm<false, kTrainBN, 4, kDown, kFp32Chunk, 64, 8, true, true>(a_hi, a_lo, b_hi, b_lo, M, N, K, e, err,
                                                                                s, lda, ldb);
+}
+
+// down with the outputs routed to their owners' buffers (the neuron-sharded forward's reduction target).
+int tc_down_peer(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo, const void* b,
+                 void* const* peers, int world, int64_t tokens_per_owner, int* err, int d, int H, int64_t n,
+                 cudaStream_t s) {
+  tc::EpilogueArgs dn{};
+  dn.bias = b;
+  for (int p = 0; p < world && p < tc::kMaxPeers; ++p) dn.peers[p] = peers[p];
+  dn.tokens_per_owner = tokens_per_owner;
+  dn.rows = d;
+  const int nn = (int)n;
+  if (dtype == HFFN_BF16)
+    return tc::launch_gemm<true, 256, 4, tc::kDownPeer, 0, 128, 16>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s);
+  return tc::launch_gemm<false, 256, 4, tc::kDownPeer, kFp32Chunk, 64, 8>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err,
+                                                                          s);
+}
+
+// out[i] = slots[0][i] + slots[1][i] + ... in slot order (float32 accumulation).
+template <typename T>
+__global__ void sum_slots_kernel(const T* __restrict__ slots, int count, int64_t elems, T* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < elems; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = to_f(slots[i]);
+    for (int k = 1; k < count; ++k) acc += to_f(slots[(int64_t)k * elems + i]);
+    out[i] = from_f<T>(acc);
+  }
+}
+
+int tc_sum_slots(int dtype, const void* slots, int count, int64_t elems, void* out, cudaStream_t s) {
+  const int blocks = (int)std::min<int64_t>(std::max<int64_t>(ceil_div(elems, 256), 1), 148 * 16);
+  if (dtype == HFFN_BF16)
+    sum_slots_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(slots), count, elems,
+                                                          reinterpret_cast<__nv_bfloat16*>(out));
+  else
+    sum_slots_kernel<float><<<blocks, 256, 0, s>>>(reinterpret_cast<const float*>(slots), count, elems,
+                                                  reinterpret_cast<float*>(out));
+  return launch_status("sum_slots");
 }
 
 void tc_set_max_ctas(int max_ctas) { tc::g_max_ctas.store(max_ctas > 0 ? max_ctas : 0); }

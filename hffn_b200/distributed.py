@@ -20,6 +20,7 @@ Every rank calls the same collectives in the same order, in warm-up and in timin
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
@@ -153,8 +154,12 @@ def x_is_cuda(ffn: "ShardedFFN") -> bool:
 
 
 def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, tensor_cores=None, group=None,
-                    segments: int | None = None, comm_sms: int = 0):
-    """The rank's ``HFFNRuntime`` over its neuron shard and the ``ShardedFFN`` around it."""
+                    segments: int | None = None, comm_sms: int = 0, transport: str = "nccl"):
+    """The rank's ``HFFNRuntime`` over its neuron shard and the sharded forward around it: ``transport="nccl"`` a
+    ``ShardedFFN`` (collective kernels), ``"peer"`` a ``PeerShardedFFN`` (NVLink peer memory, tensor cores only;
+    ``forward`` only)."""
+    if transport not in ("nccl", "peer"):
+        raise ValueError("transport must be 'nccl' or 'peer'")
     from .runtime import HFFNLayer, HFFNRuntime
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     bounds = neuron_partition(arrays, world)
@@ -166,6 +171,8 @@ def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, ten
                                         shard["up_idx"], shard["up_val"], shard["b_down"], shard["down_offsets"],
                                         shard["down_idx"], shard["down_val"])
     runtime = HFFNRuntime([layer], device, dtype, tensor_cores=tensor_cores)
+    if transport == "peer":
+        return runtime, PeerShardedFFN(runtime, d_model, group), (lo, hi)
     ffn = ShardedFFN(lambda x, out: runtime.forward(0, x, out=out), d_model, group, segments=segments,
                      comm_sms=comm_sms)
     return runtime, ffn, (lo, hi)
@@ -209,3 +216,114 @@ class DataParallelTrainer:
         self._loss.copy_(train._loss)
         dist.all_reduce(self._loss, op=dist.ReduceOp.SUM, group=self.group)
         return self._loss / self.world
+
+
+class PeerShardedFFN:
+    """The neuron-sharded forward with its exchange over NVLink peer memory instead of collective kernels.
+
+    Buffers in symmetric memory (``torch.distributed._symmetric_memory``): each rank's staged batch ``x_in [n, d]`` and
+    its receive slots ``slots [world, n, d]`` (slot p: the partial output that rank p computed for this rank's tokens).
+    A step: stage x; barrier (a 1-element NCCL all-reduce: every rank's x is staged); the other ranks' batches are
+    pulled into local memory by copy-engine copies on a side stream (no SM is used) while the rank's shard runs on its
+    own batch; then on the pulled batches in one call. The down GEMM's epilogue (``hffn_down_tc_peer``) stores each
+    token's partial output straight into the owner's slot over NVLink, so the reduction's transfer overlaps the GEMM
+    tile by tile; barrier (every partial has landed); each rank sums its slots in rank order (``hffn_sum_slots``).
+    Requires the tensor-core runtime; every rank passes batches of the same shape.
+    """
+
+    def __init__(self, runtime, d_model: int, group=None) -> None:
+        if not runtime.tensor_cores:
+            raise ValueError("the peer-memory sharded forward runs on the tensor-core path")
+        self.runtime = runtime
+        self.d_model = d_model
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        if self.world > 8:
+            raise ValueError("at most 8 ranks (one box)")
+        self._state: dict = {}
+
+    def _setup(self, n: int, dtype: torch.dtype, device) -> dict:
+        import os
+
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import _native as native
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")   # plain peer mappings: no multicast object
+        d, w, r = self.d_model, self.world, self.rank
+        elem = torch.empty(0, dtype=dtype).element_size()
+        x_in = symm_mem.empty(n, d, dtype=dtype, device=device)
+        hx = symm_mem.rendezvous(x_in, self.group)
+        slots = symm_mem.empty(w, n, d, dtype=dtype, device=device)
+        hs = symm_mem.rendezvous(slots, self.group)
+        order = [(r + j) % w for j in range(w)]                       # rotated: own batch first
+        peers_x = [hx.get_buffer(p, (n, d), dtype) for p in order]
+        targets = [int(hs.buffer_ptrs[p]) + r * n * d * elem for p in order]
+        runtime = self.runtime
+        m = max(1, w - 1) * n
+        work = torch.empty(int(native.lib.hffn_forward_tc_workspace(runtime._code, runtime._structs[0], m)),
+                           dtype=torch.uint8, device=device)
+        return {"x_in": x_in, "hx": hx, "slots": slots, "hs": hs, "peers_x": peers_x,
+                "x_all": torch.empty(max(1, w - 1) * n, d, dtype=dtype, device=device),
+                "own": (ctypes.c_uint64 * 1)(targets[0]),
+                "rest": (ctypes.c_uint64 * max(1, w - 1))(*targets[1:]) if w > 1 else None,
+                "work": work, "flag": torch.zeros(1, device=device), "copy": torch.cuda.Stream(device)}
+
+    def _barrier(self, state: dict) -> None:
+        dist.all_reduce(state["flag"], op=dist.ReduceOp.SUM, group=self.group)
+
+    def _run(self, state: dict, x_ptr: int, m: int, targets, count: int, n: int, stream) -> None:
+        from . import _native as native
+        runtime = self.runtime
+        dense = runtime._dense[0]
+        ptr = lambda v: None if v is None else v.data_ptr()  # noqa: E731
+        d, f = self.d_model, runtime.d_ff
+        work = state["work"].data_ptr()
+        if runtime.dtype == torch.float32:
+            x_split, act_hi = work, work + 2 * m * d * 4
+            act_lo = act_hi + m * f * 4
+        else:
+            x_split, act_hi, act_lo = None, work, None
+        struct = runtime._structs[0]
+        native.check(native.lib.hffn_up_tc(runtime._code, x_ptr, ptr(dense["up_hi"]), ptr(dense["up_lo"]), struct.b_up,
+                                           act_hi, act_lo, None, x_split, runtime._err.data_ptr(), d, f, m, stream),
+                     "hffn_up_tc")
+        native.check(native.lib.hffn_down_tc_peer(runtime._code, act_hi, act_lo, ptr(dense["down_hi"]),
+                                                  ptr(dense["down_lo"]), struct.b_down, targets, count, n,
+                                                  runtime._err.data_ptr(), d, f, m, stream), "hffn_down_tc_peer")
+        runtime.calls["tc", "tc"] += 1
+
+    def forward(self, x_local: torch.Tensor) -> torch.Tensor:
+        from . import _native as native
+        runtime = self.runtime
+        n, d = x_local.shape[0], self.d_model
+        runtime._check_input(x_local)
+        key = (n, x_local.dtype)
+        if key not in self._state:
+            self._state[key] = self._setup(n, x_local.dtype, x_local.device)
+        state = self._state[key]
+        if runtime._dense_stale[0]:
+            runtime._densify(0)
+        compute = torch.cuda.current_stream(x_local.device)
+        handle = compute.cuda_stream
+        state["x_in"].copy_(x_local)
+        self._barrier(state)                                   # every rank's batch is staged
+        staged = torch.cuda.Event()
+        staged.record(compute)
+        copy = state["copy"]
+        copy.wait_event(staged)
+        pulled = torch.cuda.Event()
+        with torch.cuda.stream(copy):
+            for j in range(1, self.world):
+                state["x_all"][(j - 1) * n:j * n].copy_(state["peers_x"][j], non_blocking=True)
+            pulled.record(copy)
+        # the own batch first, overlapping the pulls; partial outputs land in the owners' slots
+        self._run(state, x_local.data_ptr(), n, state["own"], 1, n, handle)
+        if self.world > 1:
+            compute.wait_event(pulled)
+            self._run(state, state["x_all"].data_ptr(), (self.world - 1) * n, state["rest"], self.world - 1, n, handle)
+        self._barrier(state)                                   # every partial has landed in its owner's slots
+        out = torch.empty(n, d, dtype=x_local.dtype, device=x_local.device)
+        native.check(native.lib.hffn_sum_slots(runtime._code, state["slots"].data_ptr(), self.world, n * d,
+                                               out.data_ptr(), handle), "hffn_sum_slots")
+        return out

@@ -177,6 +177,19 @@ int64_t hffn_forward_tc_workspace(int dtype, const hffn_layer* layer, int64_t n)
 int hffn_forward_tc(int dtype, const hffn_layer* layer, const hffn_dense* dense, const void* x, void* y, float* z,
                     void* work, int32_t* err, int64_t n, void* stream);
 
+/* The tensor-core down projection of a rank's neuron shard, fused with the reduction's transfer: the partial output of
+ * token t is stored directly into the receive buffer of the rank that owns t (peer memory over NVLink, plain stores,
+ * no collective call): peer_y[t / tokens_per_owner] + (t % tokens_per_owner) * d_model. n = world x tokens_per_owner;
+ * peer_y: `world` device addresses (host array). Replaces the reduce-scatter of the partial outputs (no reference
+ * counterpart: the reference has no multi-GPU path). */
+int hffn_down_tc_peer(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo,
+                      const void* b_down, const uint64_t* peer_y, int32_t world, int64_t tokens_per_owner,
+                      int32_t* err, int32_t d_model, int32_t d_ff, int64_t n, void* stream);
+
+/* out[i] = slots[0][i] + ... + slots[count - 1][i] in slot order (float32 accumulation): the owner's sum of the partial
+ * outputs its peers stored. */
+int hffn_sum_slots(int dtype, const void* slots, int32_t count, int64_t elems, void* out, void* stream);
+
 /* Cap on the CTAs of the persistent tensor-core GEMMs, process-wide (0: one per SM, the default). A tuning knob with
  * no reference counterpart: the neuron-sharded forward leaves a few SMs to the NCCL kernels so that its collectives
  * run alongside the GEMMs. */

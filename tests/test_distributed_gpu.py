@@ -1,8 +1,9 @@
 """GPU, NCCL, 2 ranks (skipped with fewer than 2 GPUs): the neuron-sharded forward and the data-parallel training
 step against one GPU.
 
-Sharded forward (both the replicated and the per-rank-batch forms, tensor cores and CUDA cores) equals the single-GPU
-runtime's output within the forward tolerance (the partial sums are added in another order). The data-parallel MSE
+Sharded forward (the replicated and the per-rank-batch forms, tensor cores and CUDA cores, and the peer-memory form
+on tensor cores) equals the single-GPU runtime's output within the forward tolerance (the partial sums are added in
+another order). The data-parallel MSE
 step of two ranks gives the gradients (all-reduced mean) and the loss of a single-GPU step on the concatenation of
 their batches within float32 tolerance (the update itself is AdamW of those gradients, tested on one GPU)."""
 import os
@@ -64,6 +65,18 @@ def _worker(rank: int, world: int, port: int, results) -> None:
             out[f"sharded_tc{int(tensor_cores)}"] = max(rel_rep, rel_own)
             out[f"errors_tc{int(tensor_cores)}"] = runtime.device_errors()
 
+        # the peer-memory form (tensor cores): two batch sizes, each run twice (buffers reused across steps)
+        runtime, peer, _ = sharded_runtime(layer.d_model, arrays, device, tensor_cores=True, transport="peer")
+        worst = 0.0
+        for n_own in (260, 1000):
+            x_own = torch.from_numpy(synth.make_input(case, n_own + rank)[:n_own]).to(device)
+            expected = full.forward(0, x_own).double()
+            for _ in range(2):
+                y_peer = peer.forward(x_own)
+                worst = max(worst, float(((y_peer.double() - expected).abs() / expected.abs().clamp(min=1)).max()))
+        out["sharded_peer"] = worst
+        out["errors_peer"] = runtime.device_errors()
+
         # data-parallel training: 2 x 64 tokens against one GPU on the 128 concatenated tokens
         n = 64
         xs = [synth.make_input(case, 128)[k * n:(k + 1) * n] for k in range(world)]
@@ -104,4 +117,5 @@ def test_two_ranks():
         r = results[rank]
         assert r["sharded_tc1"] <= 1e-5 and r["sharded_tc0"] <= 1e-5, r
         assert r["errors_tc1"] == 0 and r["errors_tc0"] == 0, r
+        assert r["sharded_peer"] <= 1e-5 and r["errors_peer"] == 0, r
         assert r["dp_param_rel"] <= 1e-5 and r["dp_loss_rel"] <= 1e-5, r
