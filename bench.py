@@ -242,7 +242,8 @@ def gpu_arm(args, workload: dict) -> dict | None:
     else:
         runtime, shard, (lo, hi) = sharded_runtime(case.d_model, canonical(layer, torch), device, dtype,
                                                    tensor_cores=tensor_cores, segments=args.segments,
-                                                   comm_sms=args.comm_sms, transport=args.transport)
+                                                   comm_sms=args.comm_sms, transport=args.transport,
+                                                   peers_per_chunk=args.peers_per_chunk, push=args.push)
     if args.path == "tensor_cores":
         runtime.force("tc", "tc")
     d, f_local = case.d_model, hi - lo
@@ -391,8 +392,9 @@ def gpu_arm(args, workload: dict) -> dict | None:
         "config": {"workload": f"{case.name}: d_model {d}, d_ff {case.d_ff}, support {case.up_degree}, "
                                f"N {n} tokens per GPU per step", "modes": [up, down],
                    "parallelism": "single" if world == 1 else
-                   f"neuron-sharded x{world} (peer memory: copy-engine pulls of the batches, partial outputs stored "
-                   f"into the owners' slots by the down GEMM)" if args.transport == "peer" else
+                   f"neuron-sharded x{world} (NVLink peer memory: copy-engine pulls of the batches, partial outputs "
+                   f"pushed into the owners' slots by {'the down GEMM epilogue' if args.push == 'store' else 'copy engines'}"
+                   f", {shard.peers_per_chunk} peers per chunk)" if args.transport == "peer" else
                    f"neuron-sharded x{world} (all-gather / reduce-scatter pipeline over NCCL, "
                    f"{shard.segments} segments, {shard.comm_sms} SMs left to NCCL)",
                    "l2": "flushed between steps (512 MiB write)"},
@@ -590,6 +592,9 @@ def main() -> int:
     parser.add_argument("--comm-sms", type=int, default=0, help="sharded forward: SMs left to the collectives")
     parser.add_argument("--transport", choices=("nccl", "peer"), default="nccl",
                         help="sharded forward: NCCL collectives or NVLink peer memory (tensor cores)")
+    parser.add_argument("--peers-per-chunk", type=int, default=None, help="peer sharded forward: batches per chunk")
+    parser.add_argument("--push", choices=("copy", "store"), default="copy",
+                        help="peer sharded forward: partial outputs pushed by copy engines or by the GEMM epilogue")
     parser.add_argument("--path", choices=("auto", "cuda_cores", "tensor_cores"), default="auto",
                         help="forward kernels: the runtime policy, the CUDA-core gather kernels, or the tcgen05 path")
     args = parser.parse_args()

@@ -68,6 +68,7 @@ SIGNATURES = {
     "hffn_up_tc": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I64, _P]),
     "hffn_down_tc": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I64, _P]),
     "hffn_set_tc_max_ctas": (ctypes.c_int, [_I32]),
+    "hffn_set_tc_tile_tokens": (ctypes.c_int, [_I32]),
     "hffn_down_tc_peer": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, ctypes.POINTER(ctypes.c_uint64), _I32, _I64,
                                          _P, _I32, _I32, _I64, _P]),
     "hffn_sum_slots": (ctypes.c_int, [ctypes.c_int, _P, _I32, _I64, _P, _P]),

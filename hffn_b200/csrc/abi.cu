@@ -27,6 +27,7 @@ int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const vo
           float* z, void* x_split, int* err, int d, int H, int64_t n, cudaStream_t s);
 int64_t tc_train_workspace(const hffn_layer* L, int64_t n);
 void tc_set_max_ctas(int max_ctas);
+void tc_set_tile_tokens(int tokens);
 int tc_down_peer(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo, const void* b,
                  void* const* peers, int world, int64_t tokens_per_owner, int* err, int d, int H, int64_t n,
                  cudaStream_t s);
@@ -294,6 +295,13 @@ int hffn_sum_slots(int dtype, const void* slots, int32_t count, int64_t elems, v
 int hffn_set_tc_max_ctas(int32_t max_ctas) {
   HFFN_REQUIRE(max_ctas >= 0, "negative CTA cap");
   tc_set_max_ctas(max_ctas);
+  return HFFN_OK;
+}
+
+int hffn_set_tc_tile_tokens(int32_t tokens) {
+  HFFN_REQUIRE(tokens == 0 || tokens == 64 || tokens == 128 || tokens == 256, "tile tokens %d not in {0, 64, 128, 256}",
+               tokens);
+  tc_set_tile_tokens(tokens);
   return HFFN_OK;
 }
 

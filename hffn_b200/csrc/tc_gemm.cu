@@ -755,6 +755,47 @@ static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, con
   return launch_status("tc_gemm");
 }
 
+// Token width of the forward GEMMs' tiles. The grid is persistent (one CTA per SM, tiles dealt round-robin), so a
+// GEMM costs about ceil(tiles / SMs) rounds of one tile each, and a tile's time is about proportional to its width:
+// the width among 256, 128, 64 with the fewest rounds x width wins (ties: the wider tile, which loads fewer operand
+// bytes per MMA). A nonzero g_tile_tokens forces the width.
+static std::atomic<int> g_tile_tokens{0};
+
+static int pick_tile_tokens(int M, int N) {
+  const int forced = g_tile_tokens.load();
+  if (forced == 64 || forced == 128 || forced == 256) return forced;
+  const int64_t sms = sm_count(), rows = (M + BM - 1) / BM;
+  int best = 256;
+  int64_t best_cost = INT64_MAX;
+  for (int bn = 256; bn >= 64; bn /= 2) {
+    const int64_t tiles = rows * ((N + bn - 1) / bn);
+    const int64_t cost = (tiles + sms - 1) / sms * bn;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+// One forward GEMM at the tile width pick_tile_tokens chooses (float32: 64-byte rows, 8 epilogue warps; bfloat16:
+// 128-byte rows, 16 epilogue warps, 8 at width 64 where 16 warps would split 64 columns too finely).
+template <bool kBf16, int EPI>
+static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N,
+                               int K, const EpilogueArgs& epi, int* err, cudaStream_t s) {
+  constexpr int kChunk = kBf16 ? 0 : 4;
+  constexpr int kRow = kBf16 ? 128 : 64;
+  constexpr int kWarps = kBf16 ? 16 : 8;
+  switch (pick_tile_tokens(M, N)) {
+    case 64:
+      return launch_gemm<kBf16, 64, 6, EPI, kChunk, kRow, 8>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi, err, s);
+    case 128:
+      return launch_gemm<kBf16, 128, 5, EPI, kChunk, kRow, kWarps>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi, err, s);
+    default:
+      return launch_gemm<kBf16, 256, 4, EPI, kChunk, kRow, kWarps>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi, err, s);
+  }
+}
+
 }  // namespace tc
 
 // Tile shapes: float32 (3xTF32) 128 x 256 tiles, stages of 16 K values (64-byte rows, 48 KB: A hi/lo + B hi/lo), 4
@@ -772,7 +813,7 @@ int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const vo
     tc::EpilogueArgs up{};
     up.bias = b;
     up.out_hi = act_hi;
-    return tc::launch_gemm<true, 256, 4, tc::kUp, 0, 128, 16>(w_hi, nullptr, x, nullptr, H, nn, d, up, err, s);
+    return tc::launch_forward_gemm<true, tc::kUp>(w_hi, nullptr, x, nullptr, H, nn, d, up, err, s);
   }
   float* x_hi = reinterpret_cast<float*>(x_split);
   float* x_lo = x_hi + (int64_t)n * d;
@@ -786,7 +827,7 @@ int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const vo
   up.out_hi = act_hi;
   up.out_lo = act_lo;
   up.z = z;
-  return tc::launch_gemm<false, 256, 4, tc::kUp, kFp32Chunk, 64, 8>(w_hi, w_lo, x_hi, x_lo, H, nn, d, up, err, s);
+  return tc::launch_forward_gemm<false, tc::kUp>(w_hi, w_lo, x_hi, x_lo, H, nn, d, up, err, s);
 }
 
 // down: act [n, H] token-major -> y [n, d].
@@ -796,8 +837,9 @@ int tc_down(int dtype, const void* act_hi, const void* act_lo, const void* w_hi,
   tc::EpilogueArgs dn{};
   dn.bias = b;
   dn.out_hi = y;
-  if (dtype == HFFN_BF16) return tc::launch_gemm<true, 256, 4, tc::kDown, 0, 128, 16>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s);
-  return tc::launch_gemm<false, 256, 4, tc::kDown, kFp32Chunk, 64, 8>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err, s);
+  if (dtype == HFFN_BF16)
+    return tc::launch_forward_gemm<true, tc::kDown>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s);
+  return tc::launch_forward_gemm<false, tc::kDown>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err, s);
 }
 
 // Workspace of the whole forward: fp32 [x_hi, x_lo (n d each), act_hi, act_lo (n H each)] floats; bf16 act [n, H].
@@ -1013,9 +1055,8 @@ int tc_down_peer(int dtype, const void* act_hi, const void* act_lo, const void* 
   dn.rows = d;
   const int nn = (int)n;
   if (dtype == HFFN_BF16)
-    return tc::launch_gemm<true, 256, 4, tc::kDownPeer, 0, 128, 16>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s);
-  return tc::launch_gemm<false, 256, 4, tc::kDownPeer, kFp32Chunk, 64, 8>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err,
-                                                                          s);
+    return tc::launch_forward_gemm<true, tc::kDownPeer>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s);
+  return tc::launch_forward_gemm<false, tc::kDownPeer>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err, s);
 }
 
 // out[i] = slots[0][i] + slots[1][i] + ... in slot order (float32 accumulation).
@@ -1040,6 +1081,8 @@ int tc_sum_slots(int dtype, const void* slots, int count, int64_t elems, void* o
 }
 
 void tc_set_max_ctas(int max_ctas) { tc::g_max_ctas.store(max_ctas > 0 ? max_ctas : 0); }
+
+void tc_set_tile_tokens(int tokens) { tc::g_tile_tokens.store(tokens); }
 
 int64_t tc_forward_workspace(int dtype, const hffn_layer* L, int64_t n) {
   if (dtype == HFFN_BF16) return n * L->d_ff * 2;

@@ -154,7 +154,8 @@ def x_is_cuda(ffn: "ShardedFFN") -> bool:
 
 
 def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, tensor_cores=None, group=None,
-                    segments: int | None = None, comm_sms: int = 0, transport: str = "nccl"):
+                    segments: int | None = None, comm_sms: int = 0, transport: str = "nccl",
+                    peers_per_chunk: int | None = None, push: str = "copy"):
     """The rank's ``HFFNRuntime`` over its neuron shard and the sharded forward around it: ``transport="nccl"`` a
     ``ShardedFFN`` (collective kernels), ``"peer"`` a ``PeerShardedFFN`` (NVLink peer memory, tensor cores only;
     ``forward`` only)."""
@@ -172,7 +173,7 @@ def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, ten
                                         shard["down_idx"], shard["down_val"])
     runtime = HFFNRuntime([layer], device, dtype, tensor_cores=tensor_cores)
     if transport == "peer":
-        return runtime, PeerShardedFFN(runtime, d_model, group), (lo, hi)
+        return runtime, PeerShardedFFN(runtime, d_model, group, peers_per_chunk=peers_per_chunk, push=push), (lo, hi)
     ffn = ShardedFFN(lambda x, out: runtime.forward(0, x, out=out), d_model, group, segments=segments,
                      comm_sms=comm_sms)
     return runtime, ffn, (lo, hi)
@@ -221,19 +222,30 @@ class DataParallelTrainer:
 class PeerShardedFFN:
     """The neuron-sharded forward with its exchange over NVLink peer memory instead of collective kernels.
 
-    Buffers in symmetric memory (``torch.distributed._symmetric_memory``): each rank's staged batch ``x_in [n, d]`` and
-    its receive slots ``slots [world, n, d]`` (slot p: the partial output that rank p computed for this rank's tokens).
-    A step: stage x; barrier (a 1-element NCCL all-reduce: every rank's x is staged); the other ranks' batches are
-    pulled into local memory by copy-engine copies on a side stream (no SM is used) while the rank's shard runs on its
-    own batch; then on the pulled batches in one call. The down GEMM's epilogue (``hffn_down_tc_peer``) stores each
-    token's partial output straight into the owner's slot over NVLink, so the reduction's transfer overlaps the GEMM
-    tile by tile; barrier (every partial has landed); each rank sums its slots in rank order (``hffn_sum_slots``).
-    Requires the tensor-core runtime; every rank passes batches of the same shape.
+    Buffers in symmetric memory (``torch.distributed._symmetric_memory``, plain peer mappings): each rank's staged
+    batch ``x_in [n, d]`` and its receive slots ``slots [world, n, d]`` (slot p: the partial output that rank p computed
+    for this rank's tokens). A step:
+
+    1. stage x into ``x_in``; barrier (a 1-element NCCL all-reduce): every rank's batch is staged;
+    2. the other ranks' batches are pulled into local memory by copy-engine copies, one stream per peer (no SM);
+    3. the rank's shard runs on its own batch first (overlapping the pulls), its partial output going straight to its
+       own slot; then on the pulled batches in groups of ``peers_per_chunk`` owners, each group once its pulls have
+       landed. A group's partial outputs reach their owners' slots either from the down GEMM's epilogue (``push=
+       "store"``: ``hffn_down_tc_peer`` stores over NVLink tile by tile) or by copy-engine copies from a local buffer
+       overlapping the next group's GEMMs (``push="copy"``);
+    4. barrier: every partial has landed; each rank sums its slots in rank order (``hffn_sum_slots``).
+
+    The summation order of a token's output is fixed (slot order), whatever the timing. Requires the tensor-core
+    runtime; every rank passes batches of the same shape. No collective kernel runs beside the GEMMs, and no load
+    with multicast is issued.
     """
 
-    def __init__(self, runtime, d_model: int, group=None) -> None:
+    def __init__(self, runtime, d_model: int, group=None, peers_per_chunk: int | None = None,
+                 push: str = "copy") -> None:
         if not runtime.tensor_cores:
             raise ValueError("the peer-memory sharded forward runs on the tensor-core path")
+        if push not in ("store", "copy"):
+            raise ValueError("push must be 'store' or 'copy'")
         self.runtime = runtime
         self.d_model = d_model
         self.group = group if group is not None else dist.group.WORLD
@@ -241,7 +253,15 @@ class PeerShardedFFN:
         self.world = dist.get_world_size(self.group)
         if self.world > 8:
             raise ValueError("at most 8 ranks (one box)")
+        self.peers_per_chunk = max(1, peers_per_chunk or 2)
+        self.push = push
         self._state: dict = {}
+
+    def _chunks(self) -> list[list[int]]:
+        """Positions 1 .. world - 1 (rotated peer order: position j is rank (rank + j) % world) in groups."""
+        rest = list(range(1, self.world))
+        k = self.peers_per_chunk
+        return [rest[i:i + k] for i in range(0, len(rest), k)]
 
     def _setup(self, n: int, dtype: torch.dtype, device) -> dict:
         import os
@@ -257,25 +277,37 @@ class PeerShardedFFN:
         slots = symm_mem.empty(w, n, d, dtype=dtype, device=device)
         hs = symm_mem.rendezvous(slots, self.group)
         order = [(r + j) % w for j in range(w)]                       # rotated: own batch first
-        peers_x = [hx.get_buffer(p, (n, d), dtype) for p in order]
-        targets = [int(hs.buffer_ptrs[p]) + r * n * d * elem for p in order]
+        chunks = self._chunks()
         runtime = self.runtime
-        m = max(1, w - 1) * n
+        m = max([n] + [len(c) * n for c in chunks])
         work = torch.empty(int(native.lib.hffn_forward_tc_workspace(runtime._code, runtime._structs[0], m)),
                            dtype=torch.uint8, device=device)
-        return {"x_in": x_in, "hx": hx, "slots": slots, "hs": hs, "peers_x": peers_x,
-                "x_all": torch.empty(max(1, w - 1) * n, d, dtype=dtype, device=device),
-                "own": (ctypes.c_uint64 * 1)(targets[0]),
-                "rest": (ctypes.c_uint64 * max(1, w - 1))(*targets[1:]) if w > 1 else None,
-                "work": work, "flag": torch.zeros(1, device=device), "copy": torch.cuda.Stream(device)}
+        targets = [int(hs.buffer_ptrs[p]) + r * n * d * elem for p in order]
+        rest = max(1, w - 1) * n
+        return {
+            "x_in": x_in, "hx": hx, "slots": slots, "hs": hs, "work": work,
+            "peers_x": [hx.get_buffer(p, (n, d), dtype) for p in order],
+            "peer_slot": [hs.get_buffer(p, (w, n, d), dtype)[r] for p in order],
+            "x_all": torch.empty(rest, d, dtype=dtype, device=device),
+            "y_part": torch.empty(rest, d, dtype=dtype, device=device) if self.push == "copy" else None,
+            "chunks": chunks,
+            "targets": [(ctypes.c_uint64 * len(c))(*(targets[j] for j in c)) for c in chunks],
+            "flag": torch.zeros(1, device=device),
+            "streams": [torch.cuda.Stream(device) for _ in range(w)],
+            "pulled": [torch.cuda.Event() for _ in range(w)],
+            "computed": [torch.cuda.Event() for _ in range(len(chunks))],
+            "pushed": [torch.cuda.Event() for _ in range(w)],
+            "staged": torch.cuda.Event()}
 
     def _barrier(self, state: dict) -> None:
         dist.all_reduce(state["flag"], op=dist.ReduceOp.SUM, group=self.group)
 
-    def _run(self, state: dict, x_ptr: int, m: int, targets, count: int, n: int, stream) -> None:
+    def _run(self, state: dict, x_ptr: int, m: int, stream, y_ptr=None, targets=None, count: int = 0) -> None:
+        """The shard's up GEMM over ``m`` tokens at ``x_ptr``, then its down GEMM into ``y_ptr`` (local) or, with
+        ``targets``, into the ``count`` owners' slots (``m = count n``)."""
         from . import _native as native
         runtime = self.runtime
-        dense = runtime._dense[0]
+        dense, struct = runtime._dense[0], runtime._structs[0]
         ptr = lambda v: None if v is None else v.data_ptr()  # noqa: E731
         d, f = self.d_model, runtime.d_ff
         work = state["work"].data_ptr()
@@ -284,13 +316,17 @@ class PeerShardedFFN:
             act_lo = act_hi + m * f * 4
         else:
             x_split, act_hi, act_lo = None, work, None
-        struct = runtime._structs[0]
+        err = runtime._err.data_ptr()
         native.check(native.lib.hffn_up_tc(runtime._code, x_ptr, ptr(dense["up_hi"]), ptr(dense["up_lo"]), struct.b_up,
-                                           act_hi, act_lo, None, x_split, runtime._err.data_ptr(), d, f, m, stream),
-                     "hffn_up_tc")
-        native.check(native.lib.hffn_down_tc_peer(runtime._code, act_hi, act_lo, ptr(dense["down_hi"]),
-                                                  ptr(dense["down_lo"]), struct.b_down, targets, count, n,
-                                                  runtime._err.data_ptr(), d, f, m, stream), "hffn_down_tc_peer")
+                                           act_hi, act_lo, None, x_split, err, d, f, m, stream), "hffn_up_tc")
+        if targets is None:
+            native.check(native.lib.hffn_down_tc(runtime._code, act_hi, act_lo, ptr(dense["down_hi"]),
+                                                 ptr(dense["down_lo"]), struct.b_down, y_ptr, err, d, f, m, stream),
+                         "hffn_down_tc")
+        else:
+            native.check(native.lib.hffn_down_tc_peer(runtime._code, act_hi, act_lo, ptr(dense["down_hi"]),
+                                                      ptr(dense["down_lo"]), struct.b_down, targets, count, m // count,
+                                                      err, d, f, m, stream), "hffn_down_tc_peer")
         runtime.calls["tc", "tc"] += 1
 
     def forward(self, x_local: torch.Tensor) -> torch.Tensor:
@@ -306,22 +342,36 @@ class PeerShardedFFN:
             runtime._densify(0)
         compute = torch.cuda.current_stream(x_local.device)
         handle = compute.cuda_stream
+        streams, pulled, pushed = state["streams"], state["pulled"], state["pushed"]
         state["x_in"].copy_(x_local)
         self._barrier(state)                                   # every rank's batch is staged
-        staged = torch.cuda.Event()
-        staged.record(compute)
-        copy = state["copy"]
-        copy.wait_event(staged)
-        pulled = torch.cuda.Event()
-        with torch.cuda.stream(copy):
-            for j in range(1, self.world):
+        state["staged"].record(compute)
+        for j in range(1, self.world):                         # copy-engine pulls, one stream per peer
+            streams[j].wait_event(state["staged"])
+            with torch.cuda.stream(streams[j]):
                 state["x_all"][(j - 1) * n:j * n].copy_(state["peers_x"][j], non_blocking=True)
-            pulled.record(copy)
-        # the own batch first, overlapping the pulls; partial outputs land in the owners' slots
-        self._run(state, x_local.data_ptr(), n, state["own"], 1, n, handle)
-        if self.world > 1:
-            compute.wait_event(pulled)
-            self._run(state, state["x_all"].data_ptr(), (self.world - 1) * n, state["rest"], self.world - 1, n, handle)
+                pulled[j].record(streams[j])
+        # the own batch first, overlapping the pulls: its partial output goes to this rank's own slot
+        self._run(state, x_local.data_ptr(), n, handle, y_ptr=state["slots"][self.rank].data_ptr())
+        for c, chunk in enumerate(state["chunks"]):
+            for j in chunk:
+                compute.wait_event(pulled[j])
+            first = chunk[0] - 1
+            x_ptr = state["x_all"][first * n:].data_ptr()
+            m = len(chunk) * n
+            if self.push == "store":
+                self._run(state, x_ptr, m, handle, targets=state["targets"][c], count=len(chunk))
+                continue
+            self._run(state, x_ptr, m, handle, y_ptr=state["y_part"][first * n:].data_ptr())
+            state["computed"][c].record(compute)
+            for j in chunk:                                    # copy-engine pushes into the owners' slots
+                streams[j].wait_event(state["computed"][c])
+                with torch.cuda.stream(streams[j]):
+                    state["peer_slot"][j].copy_(state["y_part"][(j - 1) * n:j * n], non_blocking=True)
+                    pushed[j].record(streams[j])
+        if self.push == "copy":
+            for j in range(1, self.world):
+                compute.wait_event(pushed[j])
         self._barrier(state)                                   # every partial has landed in its owner's slots
         out = torch.empty(n, d, dtype=x_local.dtype, device=x_local.device)
         native.check(native.lib.hffn_sum_slots(runtime._code, state["slots"].data_ptr(), self.world, n * d,

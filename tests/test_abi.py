@@ -59,3 +59,13 @@ def test_native_errors_map_to_python_exceptions():
         n.check(n.HFFN_ERR_ARGUMENT, "x")
     with pytest.raises(n.NativeError):
         n.check(n.HFFN_ERR_CUDA, "x")
+
+
+def test_tuning_knobs_check_their_arguments():
+    from hffn_b200 import _native as n
+    assert n.lib.hffn_set_tc_tile_tokens(96) == n.HFFN_ERR_ARGUMENT
+    assert b"tile tokens" in n.lib.hffn_last_error()
+    assert n.lib.hffn_set_tc_max_ctas(-1) == n.HFFN_ERR_ARGUMENT
+    for tokens in (64, 128, 256, 0):
+        assert n.lib.hffn_set_tc_tile_tokens(tokens) == n.HFFN_OK
+    assert n.lib.hffn_set_tc_max_ctas(0) == n.HFFN_OK

@@ -97,3 +97,25 @@ def test_dense_operands_follow_optimizer_steps():
     assert not torch.equal(before, after_tc)
     assert float((after_tc - after_cuda_cores).abs().max()) <= 2e-5
     assert runtime.device_errors() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("width", [64, 128, 256])
+def test_forced_tile_widths(width, dtype):
+    """Every token width of the forward GEMMs' tiles (forced process-wide, then back to the automatic choice) on ragged
+    token counts, irregular supports."""
+    from hffn_b200 import _native as native
+    case = synth.TEST_CASES["irreg_512_2048"]
+    layer = synth.make_layer(case)
+    runtime = tc_runtime(layer, dtype)
+    try:
+        native.check(native.lib.hffn_set_tc_tile_tokens(width), "hffn_set_tc_tile_tokens")
+        for n in (1, 65, 200, 777):
+            x = synth.make_input(case, n)
+            y = runtime.forward(0, torch.from_numpy(x).cuda().to(dtype)).float().cpu().numpy()
+            rel = relative(y, forward64.forward(layer, x))
+            assert rel <= (1e-5 if dtype == torch.float32 else 2e-2), (width, n, rel)
+    finally:
+        native.check(native.lib.hffn_set_tc_tile_tokens(0), "hffn_set_tc_tile_tokens")
+    assert runtime.device_errors() == 0
+
