@@ -755,30 +755,18 @@ static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, con
   return launch_status("tc_gemm");
 }
 
-// Token width of the forward GEMMs' tiles. The grid is persistent (one CTA per SM, tiles dealt round-robin), so a
-// GEMM costs about ceil(tiles / SMs) rounds of one tile each, and a tile's time is about proportional to its width:
-// the width among 256, 128, 64 with the fewest rounds x width wins (ties: the wider tile, which loads fewer operand
-// bytes per MMA). A nonzero g_tile_tokens forces the width.
+// Token width of the forward GEMMs' tiles: 256 unless g_tile_tokens forces 128 or 64. Measured on B200 over the
+// layer shapes of the single-GPU and neuron-sharded forwards (float32 and bfloat16, one call or token chunks), the
+// 256-wide tile was fastest in every case: a narrower tile reloads the whole 128 x K weight tile per token block, which
+// costs more than the rounds it saves on the persistent grid.
 static std::atomic<int> g_tile_tokens{0};
 
-static int pick_tile_tokens(int M, int N) {
+static int pick_tile_tokens() {
   const int forced = g_tile_tokens.load();
-  if (forced == 64 || forced == 128 || forced == 256) return forced;
-  const int64_t sms = sm_count(), rows = (M + BM - 1) / BM;
-  int best = 256;
-  int64_t best_cost = INT64_MAX;
-  for (int bn = 256; bn >= 64; bn /= 2) {
-    const int64_t tiles = rows * ((N + bn - 1) / bn);
-    const int64_t cost = (tiles + sms - 1) / sms * bn;
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = bn;
-    }
-  }
-  return best;
+  return forced == 64 || forced == 128 ? forced : 256;
 }
 
-// One forward GEMM at the tile width pick_tile_tokens chooses (float32: 64-byte rows, 8 epilogue warps; bfloat16:
+// One forward GEMM at the tile width pick_tile_tokens gives (float32: 64-byte rows, 8 epilogue warps; bfloat16:
 // 128-byte rows, 16 epilogue warps, 8 at width 64 where 16 warps would split 64 columns too finely).
 template <bool kBf16, int EPI>
 static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N,
@@ -786,7 +774,7 @@ static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b
   constexpr int kChunk = kBf16 ? 0 : 4;
   constexpr int kRow = kBf16 ? 128 : 64;
   constexpr int kWarps = kBf16 ? 16 : 8;
-  switch (pick_tile_tokens(M, N)) {
+  switch (pick_tile_tokens()) {
     case 64:
       return launch_gemm<kBf16, 64, 6, EPI, kChunk, kRow, 8>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi, err, s);
     case 128:

@@ -195,9 +195,8 @@ int hffn_sum_slots(int dtype, const void* slots, int32_t count, int64_t elems, v
  * run alongside the GEMMs. */
 int hffn_set_tc_max_ctas(int32_t max_ctas);
 
-/* Token width of the forward GEMMs' tiles, process-wide: 0 (the default) picks per GEMM among 256, 128 and 64 the
- * width with the fewest tile rounds x width on the persistent grid; 64, 128 or 256 force it. A tuning knob with no
- * reference counterpart. */
+/* Token width of the forward GEMMs' tiles, process-wide: 0 (the default) or 256, or 128 or 64. A tuning knob with no
+ * reference counterpart (256 measured fastest on the forward shapes). */
 int hffn_set_tc_tile_tokens(int32_t tokens);
 
 /* The GEMM engine of the tensor-core path alone (a test entry; no reference counterpart): out [n, m] = (A B^T)^T with
