@@ -766,14 +766,16 @@ static int pick_tile_tokens() {
   return forced == 64 || forced == 128 ? forced : 256;
 }
 
-// One forward GEMM at the tile width pick_tile_tokens gives (float32: 64-byte rows, 8 epilogue warps; bfloat16:
-// 128-byte rows, 16 epilogue warps, 8 at width 64 where 16 warps would split 64 columns too finely).
+// One forward GEMM at the tile width pick_tile_tokens gives (float32: 64-byte rows; bfloat16: 128-byte rows; 8
+// epilogue warps at width 64, where 16 would split 64 columns too finely).
 template <bool kBf16, int EPI>
 static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N,
                                int K, const EpilogueArgs& epi, int* err, cudaStream_t s) {
   constexpr int kChunk = kBf16 ? 0 : 4;
   constexpr int kRow = kBf16 ? 128 : 64;
-  constexpr int kWarps = kBf16 ? 16 : 8;
+  // float32 up: 16 warps (its tail epilogue, GELU and the tf32 split of 128 x 256 values, would otherwise stall the
+  // MMAs; measured 0.212 ms against 0.238 ms with 8 at C2); float32 down: 8 (16 measured slower)
+  constexpr int kWarps = kBf16 || EPI == kUp ? 16 : 8;
   switch (pick_tile_tokens()) {
     case 64:
       return launch_gemm<kBf16, 64, 6, EPI, kChunk, kRow, 8>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi, err, s);
@@ -787,8 +789,8 @@ static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b
 }  // namespace tc
 
 // Tile shapes: float32 (3xTF32) 128 x 256 tiles, stages of 16 K values (64-byte rows, 48 KB: A hi/lo + B hi/lo), 4
-// stages, 8 epilogue warps; bfloat16 128 x 256 tiles, stages of 64 K values (128-byte rows, 48 KB), 4 stages,
-// 16 epilogue warps.
+// stages, 16 epilogue warps for up and 8 for down; bfloat16 128 x 256 tiles, stages of 64 K values (128-byte rows,
+// 48 KB), 4 stages, 16 epilogue warps.
 // float32 accumulation: the tensor cores' fp32 accumulation in TMEM is not round-to-nearest at every add (measured
 // here: results biased toward zero by ~1e-5 relative over ~400 MMAs), so the K loop runs in chunks of kFp32Chunk
 // k-blocks (64 K values, 24 MMAs) into fresh accumulators whose values the epilogue adds in float32 registers.
