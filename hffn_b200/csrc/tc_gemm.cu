@@ -12,8 +12,9 @@
 // ~2^-22 relative, is dropped), with fp32 accumulation in TMEM: products carry ~2^-21 relative error instead of tf32's
 // 2^-11. The conversions are the PTX instruction cvt.rna.tf32.f32.
 //
-// float32 accumulation runs in K chunks of 64 (24 MMAs) into fresh TMEM accumulators that the epilogue adds into
-// float32 registers with round-to-nearest: the accumulation bias of the tensor core stays bounded by one chunk.
+// float32 accumulation runs in K chunks (128 values, 48 MMAs, in the forward; 64 values, 24 MMAs, in the training
+// step) into fresh TMEM accumulators that the epilogue adds into float32 registers with round-to-nearest: the
+// accumulation bias of the tensor core stays bounded by one chunk.
 //
 // Kernel shape: persistent, one CTA per SM, 6 warps: warp 0 issues the TMA loads (one elected thread), warp 1 owns
 // the TMEM allocation and issues the MMAs (one elected thread), warps 2-9 run the epilogue (one TMEM lane = one
@@ -254,12 +255,13 @@ __device__ __forceinline__ float2 emit_one(const EpilogueArgs* e, int64_t at, fl
 }
 
 // Four values of one output row (tokens t0 .. t0 + 3 at `stride` apart, `count` of them valid): bias added, then
-// the epilogue's stores; returns the partial sums it contributes (loss, column sum). Out of line: the epilogue calls
-// it once per 4 values (an inlined copy per value of an unrolled tile overflows the instruction cache); the four
-// values are independent, so their chains interleave.
+// the epilogue's stores; returns the partial sums it contributes (loss, column sum). The four values are independent,
+// so their chains interleave. emit4 is out of line (the epilogue calls it once per 4 values: with 128 values per
+// thread an inlined copy per value overflows the instruction cache); emit4_inline is the same code inlined, for
+// epilogues of at most 64 values per thread (measured faster there: no call, no registers saved around it).
 template <bool kBf16, int EPI>
-__device__ __noinline__ float2 emit4(const EpilogueArgs* e, int64_t at, int64_t stride, int count, float bias,
-                                     float v0, float v1, float v2, float v3) {
+__device__ __forceinline__ float2 emit4_inline(const EpilogueArgs* e, int64_t at, int64_t stride, int count,
+                                               float bias, float v0, float v1, float v2, float v3) {
   float2 acc = make_float2(0.f, 0.f), r;
   if (count >= 4) {
     r = emit_one<kBf16, EPI>(e, at, v0 + bias); acc.x += r.x; acc.y += r.y;
@@ -272,6 +274,20 @@ __device__ __noinline__ float2 emit4(const EpilogueArgs* e, int64_t at, int64_t 
   if (count > 1) { r = emit_one<kBf16, EPI>(e, at + stride, v1 + bias); acc.x += r.x; acc.y += r.y; }
   if (count > 2) { r = emit_one<kBf16, EPI>(e, at + 2 * stride, v2 + bias); acc.x += r.x; acc.y += r.y; }
   return acc;
+}
+
+template <bool kBf16, int EPI>
+__device__ __noinline__ float2 emit4(const EpilogueArgs* e, int64_t at, int64_t stride, int count, float bias,
+                                     float v0, float v1, float v2, float v3) {
+  return emit4_inline<kBf16, EPI>(e, at, stride, count, bias, v0, v1, v2, v3);
+}
+
+// emit4 or emit4_inline by the number of values per epilogue thread.
+template <bool kBf16, int EPI, int HALF>
+__device__ __forceinline__ float2 emit4_at(const EpilogueArgs* e, int64_t at, int64_t stride, int count, float bias,
+                                           float v0, float v1, float v2, float v3) {
+  if constexpr (HALF <= 64) return emit4_inline<kBf16, EPI>(e, at, stride, count, bias, v0, v1, v2, v3);
+  else return emit4<kBf16, EPI>(e, at, stride, count, bias, v0, v1, v2, v3);
 }
 
 // One support entry q of row `row`, column `col`, gradient g: stored and / or applied by AdamW (PyTorch's fused order),
@@ -552,7 +568,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
 #pragma unroll
           for (int i = 0; i < HALF; i += 4)
             if (n0 + i < N) {
-              const float2 r = emit4<kBf16, EPI>(e, (int64_t)(n0 + i) * M + row, M, N - (n0 + i), bias, sum[i],
+              const float2 r = emit4_at<kBf16, EPI, HALF>(e, (int64_t)(n0 + i) * M + row, M, N - (n0 + i), bias, sum[i],
                                                  sum[i + 1], sum[i + 2], sum[i + 3]);
               partial.x += r.x;
               partial.y += r.y;
@@ -572,7 +588,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
             for (int j = 0; j < 32; j += 4) {
               const int t = n0 + c * 32 + j;
               if (t < N) {
-                const float2 r = emit4<kBf16, EPI>(e, (int64_t)t * M + row, M, N - t, bias, v[j], v[j + 1],
+                const float2 r = emit4_at<kBf16, EPI, HALF>(e, (int64_t)t * M + row, M, N - t, bias, v[j], v[j + 1],
                                                    v[j + 2], v[j + 3]);
                 partial.x += r.x;
                 partial.y += r.y;
@@ -766,12 +782,16 @@ static int pick_tile_tokens() {
   return forced == 64 || forced == 128 ? forced : 256;
 }
 
+// float32 forward GEMMs: K chunks of 128 values (48 MMAs; 64 in the training step): the accumulation error stays well
+// inside the float32 bar (tested) and the epilogue drains TMEM half as often (measured 8 % faster at C2).
+constexpr int kFp32ForwardChunk = 8;
+
 // One forward GEMM at the tile width pick_tile_tokens gives (float32: 64-byte rows; bfloat16: 128-byte rows; 8
 // epilogue warps at width 64, where 16 would split 64 columns too finely).
 template <bool kBf16, int EPI>
 static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N,
                                int K, const EpilogueArgs& epi, int* err, cudaStream_t s) {
-  constexpr int kChunk = kBf16 ? 0 : 4;
+  constexpr int kChunk = kBf16 ? 0 : kFp32ForwardChunk;
   constexpr int kRow = kBf16 ? 128 : 64;
   // float32 up: 16 warps (its tail epilogue, GELU and the tf32 split of 128 x 256 values, would otherwise stall the
   // MMAs; measured 0.212 ms against 0.238 ms with 8 at C2); float32 down: 8 (16 measured slower)
