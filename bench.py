@@ -497,8 +497,7 @@ def train_arm(args, workload: dict, rank: int, world: int, local: int, device) -
         b.record(stream)
         b.synchronize()
         e2e_ms.append(a.elapsed_time(b))
-    total_s, e2e_s, e2e_flushed_s = max_over_ranks(torch, [sum(step_ms) / 1e3, sum(e2e_ms) / 1e3,
-                                                          e2e_flushed_ms / 1e3], world, device)
+    total_s, e2e_s = max_over_ranks(torch, [sum(step_ms) / 1e3, sum(e2e_ms) / 1e3], world, device)
     pk, pk_source = peaks()
     fp32_peak = fp32_gemm_peak(torch) if rank == 0 else None
     if world > 1:

@@ -12,9 +12,8 @@
 // ~2^-22 relative, is dropped), with fp32 accumulation in TMEM: products carry ~2^-21 relative error instead of tf32's
 // 2^-11. The conversions are the PTX instruction cvt.rna.tf32.f32.
 //
-// float32 accumulation runs in K chunks (128 values, 48 MMAs, in the forward; 64 values, 24 MMAs, in the training
-// step) into fresh TMEM accumulators that the epilogue adds into float32 registers with round-to-nearest: the
-// accumulation bias of the tensor core stays bounded by one chunk.
+// float32 accumulation runs in K chunks of 128 values (48 MMAs) into fresh TMEM accumulators that the epilogue adds
+// into float32 registers with round-to-nearest: the accumulation bias of the tensor core stays bounded by one chunk.
 //
 // Kernel shape: persistent, one CTA per SM, 6 warps: warp 0 issues the TMA loads (one elected thread), warp 1 owns
 // the TMEM allocation and issues the MMAs (one elected thread), warps 2-9 run the epilogue (one TMEM lane = one
@@ -782,16 +781,19 @@ static int pick_tile_tokens() {
   return forced == 64 || forced == 128 ? forced : 256;
 }
 
-// float32 forward GEMMs: K chunks of 128 values (48 MMAs; 64 in the training step): the accumulation error stays well
-// inside the float32 bar (tested) and the epilogue drains TMEM half as often (measured 8 % faster at C2).
-constexpr int kFp32ForwardChunk = 8;
+// float32 accumulation: the tensor cores' fp32 accumulation in TMEM is not round-to-nearest at every add (measured
+// here: results biased toward zero by ~1e-5 relative over ~400 MMAs), so the K loop runs in chunks of kFp32Chunk
+// k-blocks (128 K values, 48 MMAs) into fresh accumulators whose values the epilogue adds in float32 registers. 128
+// values measured faster than 64 (8 % on the C2 forward, 2.5 % on the C3 training step), the error well inside the
+// float32 bar.
+constexpr int kFp32Chunk = 8;
 
 // One forward GEMM at the tile width pick_tile_tokens gives (float32: 64-byte rows; bfloat16: 128-byte rows; 8
 // epilogue warps at width 64, where 16 would split 64 columns too finely).
 template <bool kBf16, int EPI>
 static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N,
                                int K, const EpilogueArgs& epi, int* err, cudaStream_t s) {
-  constexpr int kChunk = kBf16 ? 0 : kFp32ForwardChunk;
+  constexpr int kChunk = kBf16 ? 0 : kFp32Chunk;
   constexpr int kRow = kBf16 ? 128 : 64;
   // float32 up: 16 warps (its tail epilogue, GELU and the tf32 split of 128 x 256 values, would otherwise stall the
   // MMAs; measured 0.212 ms against 0.238 ms with 8 at C2); float32 down: 8 (16 measured slower)
@@ -811,10 +813,6 @@ static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b
 // Tile shapes: float32 (3xTF32) 128 x 256 tiles, stages of 16 K values (64-byte rows, 48 KB: A hi/lo + B hi/lo), 4
 // stages, 16 epilogue warps for up and 8 for down; bfloat16 128 x 256 tiles, stages of 64 K values (128-byte rows,
 // 48 KB), 4 stages, 16 epilogue warps.
-// float32 accumulation: the tensor cores' fp32 accumulation in TMEM is not round-to-nearest at every add (measured
-// here: results biased toward zero by ~1e-5 relative over ~400 MMAs), so the K loop runs in chunks of kFp32Chunk
-// k-blocks (64 K values, 24 MMAs) into fresh accumulators whose values the epilogue adds in float32 registers.
-constexpr int kFp32Chunk = 4;
 // up: x [n, d] -> act [n, H] token-major (fp32: the split x_hi / x_lo [n, d] go to x_split, act as hi / lo parts).
 int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const void* b, void* act_hi, void* act_lo,
           float* z, void* x_split, int* err, int d, int H, int64_t n, cudaStream_t s) {
