@@ -192,9 +192,17 @@ struct EpilogueArgs {
   float* col_partial;    // kDownMse / kGradHidden: [num_n * parts, M] partial sums of gy / gz per row
   // kGradHidden
   const float* z_in;     // [N, M] pre-activations of the forward
-  // kSampled: support of each row (offsets [M + 1], ascending columns), compact values / gradient / moments
-  const int32_t* offsets;
-  const int16_t* cols;
+  // kUp / kDownMse / kGradHidden (float32), optional: feature-major copies [M, t_ld] of the tf32 hi / lo outputs
+  // (act, gy, gz), the K-major operands of the sampled weight-gradient GEMMs (t_ld: a multiple of 4 >= N)
+  float* t_hi;
+  float* t_lo;
+  int64_t t_ld;
+  // kSampled: the support of each row as a bitmask over the N columns (32-column words, mask_ld words per row) and,
+  // per word, the compact index of the row's first support entry at or after the word's first column; compact
+  // values / gradient / moments
+  const uint32_t* mask;
+  const int32_t* first;
+  int64_t mask_ld;
   float* value;
   float* grad;           // NULL: not stored
   float* m;
@@ -213,16 +221,17 @@ struct EpilogueArgs {
 // of z, or (down) the store of y. Out of line: the epilogue calls it once per value, and an inlined copy per value
 // of an unrolled tile overflows the instruction cache.
 template <bool kBf16, int EPI>
-__device__ __forceinline__ float2 emit_one(const EpilogueArgs* e, int64_t at, float s) {
+__device__ __forceinline__ float2 emit_one(const EpilogueArgs* e, int64_t at, float s, float& hi, float& lo) {
   if constexpr (EPI == kUp) {
     if (!kBf16 && e->z) e->z[at] = s;
     const float h = gelu(s);
     if constexpr (kBf16) {
       reinterpret_cast<__nv_bfloat16*>(e->out_hi)[at] = __float2bfloat16_rn(h);
     } else {
-      const float hi = tf32_rna(h);
+      hi = tf32_rna(h);
+      lo = tf32_rna(h - hi);
       reinterpret_cast<float*>(e->out_hi)[at] = hi;
-      reinterpret_cast<float*>(e->out_lo)[at] = tf32_rna(h - hi);
+      reinterpret_cast<float*>(e->out_lo)[at] = lo;
     }
     return make_float2(0.f, 0.f);
   } else if constexpr (EPI == kDown) {
@@ -240,53 +249,72 @@ __device__ __forceinline__ float2 emit_one(const EpilogueArgs* e, int64_t at, fl
     reinterpret_cast<float*>(e->out_hi)[at] = s;
     const float diff = s - e->target[at];
     const float g = e->scale * diff;
-    const float hi = tf32_rna(g);
+    hi = tf32_rna(g);
+    lo = tf32_rna(g - hi);
     e->gy_hi[at] = hi;
-    e->gy_lo[at] = tf32_rna(g - hi);
+    e->gy_lo[at] = lo;
     return make_float2(diff * diff, g);
   } else {   // kGradHidden
     const float g = s * gelu_grad(e->z_in[at]);
-    const float hi = tf32_rna(g);
+    hi = tf32_rna(g);
+    lo = tf32_rna(g - hi);
     reinterpret_cast<float*>(e->out_hi)[at] = hi;
-    reinterpret_cast<float*>(e->out_lo)[at] = tf32_rna(g - hi);
+    reinterpret_cast<float*>(e->out_lo)[at] = lo;
     return make_float2(0.f, g);
   }
 }
 
-// Four values of one output row (tokens t0 .. t0 + 3 at `stride` apart, `count` of them valid): bias added, then
-// the epilogue's stores; returns the partial sums it contributes (loss, column sum). The four values are independent,
-// so their chains interleave. emit4 is out of line (the epilogue calls it once per 4 values: with 128 values per
-// thread an inlined copy per value overflows the instruction cache); emit4_inline is the same code inlined, for
-// epilogues of at most 64 values per thread (measured faster there: no call, no registers saved around it).
+// Four values of one output row `row`, tokens t0 .. t0 + 3 (t0 a multiple of 4; those below N valid): bias added,
+// then the epilogue's stores, and (when the epilogue has them) the feature-major copies as one 16-byte store each;
+// returns the partial sums it contributes (loss, column sum). The four values are independent, so their chains
+// interleave. emit4 is out of line (the epilogue calls it once per 4 values: with 128 values per thread an inlined
+// copy per value overflows the instruction cache); emit4_inline is the same code inlined, for epilogues of at most
+// 64 values per thread (measured faster there: no call, no registers saved around it).
 template <bool kBf16, int EPI>
-__device__ __forceinline__ float2 emit4_inline(const EpilogueArgs* e, int64_t at, int64_t stride, int count,
-                                               float bias, float v0, float v1, float v2, float v3) {
-  float2 acc = make_float2(0.f, 0.f), r;
-  if (count >= 4) {
-    r = emit_one<kBf16, EPI>(e, at, v0 + bias); acc.x += r.x; acc.y += r.y;
-    r = emit_one<kBf16, EPI>(e, at + stride, v1 + bias); acc.x += r.x; acc.y += r.y;
-    r = emit_one<kBf16, EPI>(e, at + 2 * stride, v2 + bias); acc.x += r.x; acc.y += r.y;
-    r = emit_one<kBf16, EPI>(e, at + 3 * stride, v3 + bias); acc.x += r.x; acc.y += r.y;
-    return acc;
+__device__ __forceinline__ float2 emit4_inline(const EpilogueArgs* e, int row, int t0, int M, int N, float bias,
+                                               float v0, float v1, float v2, float v3) {
+  const int64_t at = (int64_t)t0 * M + row;
+  const int count = N - t0;
+  const float v[4] = {v0, v1, v2, v3};
+  float h[4] = {0.f, 0.f, 0.f, 0.f}, l[4] = {0.f, 0.f, 0.f, 0.f};
+  float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (count >= 4 || j < count) {
+      const float2 r = emit_one<kBf16, EPI>(e, at + (int64_t)j * M, v[j] + bias, h[j], l[j]);
+      acc.x += r.x;
+      acc.y += r.y;
+    }
+  if constexpr (!kBf16 && (EPI == kUp || EPI == kDownMse || EPI == kGradHidden)) {
+    if (e->t_hi != nullptr) {
+      float* th = e->t_hi + (int64_t)row * e->t_ld + t0;
+      float* tl = e->t_lo + (int64_t)row * e->t_ld + t0;
+      if (count >= 4) {
+        *reinterpret_cast<float4*>(th) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4*>(tl) = make_float4(l[0], l[1], l[2], l[3]);
+      } else {
+        for (int j = 0; j < count; ++j) {
+          th[j] = h[j];
+          tl[j] = l[j];
+        }
+      }
+    }
   }
-  if (count > 0) { r = emit_one<kBf16, EPI>(e, at, v0 + bias); acc.x += r.x; acc.y += r.y; }
-  if (count > 1) { r = emit_one<kBf16, EPI>(e, at + stride, v1 + bias); acc.x += r.x; acc.y += r.y; }
-  if (count > 2) { r = emit_one<kBf16, EPI>(e, at + 2 * stride, v2 + bias); acc.x += r.x; acc.y += r.y; }
   return acc;
 }
 
 template <bool kBf16, int EPI>
-__device__ __noinline__ float2 emit4(const EpilogueArgs* e, int64_t at, int64_t stride, int count, float bias,
-                                     float v0, float v1, float v2, float v3) {
-  return emit4_inline<kBf16, EPI>(e, at, stride, count, bias, v0, v1, v2, v3);
+__device__ __noinline__ float2 emit4(const EpilogueArgs* e, int row, int t0, int M, int N, float bias, float v0,
+                                     float v1, float v2, float v3) {
+  return emit4_inline<kBf16, EPI>(e, row, t0, M, N, bias, v0, v1, v2, v3);
 }
 
 // emit4 or emit4_inline by the number of values per epilogue thread.
 template <bool kBf16, int EPI, int HALF>
-__device__ __forceinline__ float2 emit4_at(const EpilogueArgs* e, int64_t at, int64_t stride, int count, float bias,
-                                           float v0, float v1, float v2, float v3) {
-  if constexpr (HALF <= 64) return emit4_inline<kBf16, EPI>(e, at, stride, count, bias, v0, v1, v2, v3);
-  else return emit4<kBf16, EPI>(e, at, stride, count, bias, v0, v1, v2, v3);
+__device__ __forceinline__ float2 emit4_at(const EpilogueArgs* e, int row, int t0, int M, int N, float bias, float v0,
+                                           float v1, float v2, float v3) {
+  if constexpr (HALF <= 64) return emit4_inline<kBf16, EPI>(e, row, t0, M, N, bias, v0, v1, v2, v3);
+  else return emit4<kBf16, EPI>(e, row, t0, M, N, bias, v0, v1, v2, v3);
 }
 
 // One support entry q of row `row`, column `col`, gradient g: stored and / or applied by AdamW (PyTorch's fused order),
@@ -378,46 +406,57 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t armed = 0;   // bit s: stage s has been armed at least once
-      uint32_t armed_parity = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, kWaitNs)) {
-            ok = false;
-            break;
-          }
-          mbar_expect_tx(&full[stage], L::kStageBytes);
-          armed |= 1u << stage;
-          armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
-          uint8_t* a = a_base + stage * L::kParts * L::kA;
-          uint8_t* b = b_base + stage * L::kParts * L::kB;
-          const int kc = kb * k_elems;
-          // K-major: one box (K extent x rows); MN-major: one box (32 MN x K extent) per 32-element MN block
-          auto load = [&](uint8_t* dst, const CUtensorMap* map, int mn0, int rows, bool mn_major) {
-            if (!mn_major) {
-              tma_load_2d(dst, map, &full[stage], kc, mn0);
-            } else {
-              for (int blk = 0; blk < rows / 32; ++blk)
-                tma_load_2d(dst + blk * (k_elems * 128), map, &full[stage], mn0 + 32 * blk, kc);
-            }
-          };
-          load(a, &map_a_hi, m0, BM, A_MN);
-          load(b, &map_b_hi, n0, BN, B_MN);
-          if (!kBf16) {
-            load(a + L::kA, &map_a_lo, m0, BM, A_MN);
-            load(b + L::kB, &map_b_lo, n0, BN, B_MN);
-          }
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
+    // Lane 0 waits for a free stage and arms its barrier; then the stage's boxes are issued one per lane (an MN-major
+    // operand takes one box per 32-element MN block: up to 24 boxes a stage, which one thread issues too slowly to
+    // keep the MMAs fed).
+    constexpr int kBoxA = A_MN ? BM / 32 : 1, kBoxB = B_MN ? BN / 32 : 1;
+    constexpr int kBoxes = (kBoxA + kBoxB) * (kBf16 ? 1 : 2);
+    static_assert(kBoxes <= 32, "one box per lane");
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t armed = 0;   // bit s: stage s has been armed at least once
+    uint32_t armed_parity = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      const int m0 = (tile % num_m) * BM, n0 = (tile / num_m) * BN;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        int got = 1;
+        if (lane == 0) {
+          got = mbar_wait(&empty[stage], phase ^ 1, abort_flag, kWaitNs) ? 1 : 0;
+          if (got) {
+            mbar_expect_tx(&full[stage], L::kStageBytes);
+            armed |= 1u << stage;
+            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
           }
         }
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        __syncwarp();
+        if (lane < kBoxes) {
+          const int kc = kb * k_elems;
+          int box = lane;
+          const bool lo = !kBf16 && box >= kBoxA + kBoxB;
+          if (lo) box -= kBoxA + kBoxB;
+          const bool is_a = box < kBoxA;
+          const int blk = is_a ? box : box - kBoxA;
+          const bool mn = is_a ? A_MN : B_MN;
+          const CUtensorMap* map = is_a ? (lo ? &map_a_lo : &map_a_hi) : (lo ? &map_b_lo : &map_b_hi);
+          uint8_t* dst = is_a ? a_base + stage * L::kParts * L::kA + (lo ? L::kA : 0)
+                              : b_base + stage * L::kParts * L::kB + (lo ? L::kB : 0);
+          // K-major: one box (K extent x rows); MN-major: one box (32 MN x K extent) per 32-element MN block
+          if (!mn) tma_load_2d(dst, map, &full[stage], kc, is_a ? m0 : n0);
+          else tma_load_2d(dst + blk * (k_elems * 128), map, &full[stage], (is_a ? m0 : n0) + 32 * blk, kc);
+        }
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
       }
+    }
+    if (lane == 0) {
       if (!ok) {
         atomicCAS(err, 0, kErrTimeoutProducer);
         *abort_flag = 1;
@@ -542,24 +581,21 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
         }
         if (!ok) break;
         if constexpr (EPI == kSampled) {
-          // the support entries of this row within columns [n0, n0 + HALF), ascending: binary search, then a walk
+          // the support entries of this row within columns [n0, n0 + HALF): the row's bitmask words for these
+          // columns and the compact index of the first of them (independent loads, no search)
           if (row < M) {
-            const int q_begin = e->offsets[row], q_end = e->offsets[row + 1];
-            int lo = q_begin, hi = q_end;
-            while (lo < hi) {
-              const int mid = (lo + hi) >> 1;
-              if ((int)e->cols[mid] < n0) lo = mid + 1;
-              else hi = mid;
-            }
-            int q = lo;
-            int next = q < q_end ? (int)e->cols[q] : INT_MAX;
+            static_assert(HALF % 32 == 0, "whole mask words");
+            const int64_t word0 = (int64_t)row * e->mask_ld + (n0 >> 5);
+            uint32_t bits[HALF / 32];
+#pragma unroll
+            for (int c = 0; c < HALF / 32; ++c) bits[c] = e->mask[word0 + c];
+            int q = e->first[word0];
             const int64_t dense_row = (int64_t)row * N;
 #pragma unroll
             for (int i = 0; i < HALF; ++i) {
-              if (next == n0 + i) {
+              if ((bits[i >> 5] >> (i & 31)) & 1u) {
                 sampled_entry(e, q, dense_row + n0 + i, sum[i]);
                 ++q;
-                next = q < q_end ? (int)e->cols[q] : INT_MAX;
               }
             }
           }
@@ -567,8 +603,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
 #pragma unroll
           for (int i = 0; i < HALF; i += 4)
             if (n0 + i < N) {
-              const float2 r = emit4_at<kBf16, EPI, HALF>(e, (int64_t)(n0 + i) * M + row, M, N - (n0 + i), bias, sum[i],
-                                                 sum[i + 1], sum[i + 2], sum[i + 3]);
+              const float2 r = emit4_at<kBf16, EPI, HALF>(e, row, n0 + i, M, N, bias, sum[i], sum[i + 1], sum[i + 2],
+                                                          sum[i + 3]);
               partial.x += r.x;
               partial.y += r.y;
             }
@@ -587,8 +623,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
             for (int j = 0; j < 32; j += 4) {
               const int t = n0 + c * 32 + j;
               if (t < N) {
-                const float2 r = emit4_at<kBf16, EPI, HALF>(e, (int64_t)t * M + row, M, N - t, bias, v[j], v[j + 1],
-                                                   v[j + 2], v[j + 3]);
+                const float2 r = emit4_at<kBf16, EPI, HALF>(e, row, t, M, N, bias, v[j], v[j + 1], v[j + 2],
+                                                            v[j + 3]);
                 partial.x += r.x;
                 partial.y += r.y;
               }
@@ -659,6 +695,69 @@ __global__ void split_kernel(const float4* __restrict__ x, float4* __restrict__ 
   }
 }
 
+// x [n, d] -> feature-major tf32 parts x_hi^T, x_lo^T [d, ld] (ld >= n): 32 x 32 tiles through shared memory, reads
+// and writes coalesced.
+__global__ void split_transpose_kernel(const float* __restrict__ x, int64_t n, int d, float* __restrict__ hi,
+                                       float* __restrict__ lo, int64_t ld) {
+  __shared__ float tile[32][33];
+  const int64_t t0 = (int64_t)blockIdx.x * 32;
+  const int f0 = blockIdx.y * 32;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int64_t t = t0 + r;
+    const int f = f0 + threadIdx.x;
+    tile[r][threadIdx.x] = t < n && f < d ? x[t * d + f] : 0.f;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int f = f0 + r;
+    const int64_t t = t0 + threadIdx.x;
+    if (f < d && t < n) {
+      const float v = tile[threadIdx.x][r];
+      const float h = tf32_rna(v);
+      hi[(int64_t)f * ld + t] = h;
+      lo[(int64_t)f * ld + t] = tf32_rna(v - h);
+    }
+  }
+}
+
+// The support of each row (CSR: offsets [rows + 1], columns) as a bitmask over 32-column words (ld words per row,
+// zero past the last column) and, per word, the compact index of the row's first entry at or after the word's first
+// column. One warp per row, the row's mask assembled in shared memory (ld <= kMaxMaskWords).
+constexpr int kMaskWarps = 4, kMaxMaskWords = 1024;
+__global__ void support_tables_kernel(const int32_t* __restrict__ off, const int16_t* __restrict__ cols, int rows,
+                                      int ld, uint32_t* __restrict__ mask, int32_t* __restrict__ first) {
+  extern __shared__ uint32_t words[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kMaskWarps + warp;
+  if (row >= rows) return;
+  uint32_t* w = words + warp * ld;
+  for (int k = lane; k < ld; k += 32) w[k] = 0u;
+  __syncwarp();
+  const int begin = off[row], end = off[row + 1];
+  for (int q = begin + lane; q < end; q += 32) {
+    const int c = cols[q];
+    atomicOr(&w[c >> 5], 1u << (c & 31));
+  }
+  __syncwarp();
+  int base = begin;
+  for (int k0 = 0; k0 < ld; k0 += 32) {
+    const int k = k0 + lane;
+    const uint32_t word = k < ld ? w[k] : 0u;
+    const int count = __popc(word);
+    int inclusive = count;
+#pragma unroll
+    for (int step = 1; step < 32; step <<= 1) {
+      const int other = __shfl_up_sync(0xffffffffu, inclusive, step);
+      if (lane >= step) inclusive += other;
+    }
+    if (k < ld) {
+      mask[(int64_t)row * ld + k] = word;
+      first[(int64_t)row * ld + k] = base + inclusive - count;
+    }
+    base += __shfl_sync(0xffffffffu, inclusive, 31);
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // host side
 
@@ -676,7 +775,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // [rows, k] K-major operand, box = (128 bytes of K) x box_rows, 128-byte swizzle, zero fill outside.
 static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, bool bf16, int box_rows,
-                    int row_bytes) {
+                    int row_bytes, int64_t ld = 0) {
   auto fn = encode_fn();
   if (fn == nullptr) {
     set_error("cuTensorMapEncodeTiled unavailable");
@@ -684,7 +783,7 @@ static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k,
   }
   const int elem = bf16 ? 2 : 4;
   cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(k * elem)};
+  cuuint64_t strides[1] = {(cuuint64_t)((ld > 0 ? ld : k) * elem)};
   cuuint32_t box[2] = {(cuuint32_t)(row_bytes / elem), (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
@@ -747,7 +846,7 @@ static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, con
   constexpr int k_box = RB / 4;
   CUtensorMap ma_hi, ma_lo, mb_hi, mb_lo;
   auto map = [&](CUtensorMap* m, const void* base, int rows, int box_rows, bool mn, int64_t ld) {
-    return mn ? make_map_mn(m, base, rows, K, ld, k_box) : make_map(m, base, rows, K, kBf16, box_rows, RB);
+    return mn ? make_map_mn(m, base, rows, K, ld, k_box) : make_map(m, base, rows, K, kBf16, box_rows, RB, ld);
   };
   HFFN_TRY(map(&ma_hi, a_hi, M, BM, A_MN, lda));
   HFFN_TRY(map(&mb_hi, b_hi, N, BN, B_MN, ldb));
@@ -903,14 +1002,26 @@ __global__ void loss_reduce_kernel(const float* __restrict__ partial, int64_t co
   }
 }
 
-constexpr int kTrainBN = 256, kTrainParts = 2;
+// Training GEMMs: 256-token tiles. The per-(token block, column part) partial sums of the down + MSE GEMM (8
+// epilogue warps: 2 column parts) and of the gelu' GEMM (16 warps: 4 column parts, its tail epilogue being the
+// heavier) are reduced in a fixed order afterwards.
+constexpr int kTrainBN = 256, kTrainPartsDown = 2, kTrainPartsUp = 4;
 
+// The training step's workspace: token-major operands [n, features], their feature-major copies [features, t_ld]
+// (the K-major operands of the two weight-gradient GEMMs), the partial sums, and the support tables of both
+// supports (bitmask words and first indices, mask_ld words per row: whole 256-column tiles).
 struct TrainWork {
   float *x_hi, *x_lo, *z, *act_hi, *act_lo, *gy_hi, *gy_lo, *gz_hi, *gz_lo, *loss_p, *dn_p, *up_p;
+  float *xt_hi, *xt_lo, *actt_hi, *actt_lo, *gyt_hi, *gyt_lo, *gzt_hi, *gzt_lo;
+  uint32_t *dn_mask, *up_mask;
+  int32_t *dn_first, *up_first;
+  int64_t t_ld, dn_ld, up_ld;
 };
 
+static int64_t mask_words(int64_t cols) { return (cols + kTrainBN - 1) / kTrainBN * (kTrainBN / 32); }
+
 static int64_t train_floats(int64_t d, int64_t H, int64_t n, TrainWork* w, float* base) {
-  const int64_t rows = kTrainParts * ((n + kTrainBN - 1) / kTrainBN);
+  const int64_t blocks = (n + kTrainBN - 1) / kTrainBN;
   int64_t off = 0;
   auto take = [&](float** slot, int64_t count) {
     if (w) *slot = base + off;
@@ -927,10 +1038,43 @@ static int64_t train_floats(int64_t d, int64_t H, int64_t n, TrainWork* w, float
   take(&t->gy_lo, n * d);
   take(&t->gz_hi, n * H);
   take(&t->gz_lo, n * H);
-  take(&t->loss_p, rows * d);
-  take(&t->dn_p, rows * d);
-  take(&t->up_p, rows * H);
+  take(&t->loss_p, kTrainPartsDown * blocks * d);
+  take(&t->dn_p, kTrainPartsDown * blocks * d);
+  take(&t->up_p, kTrainPartsUp * blocks * H);
+  t->t_ld = (n + 3) / 4 * 4;
+  take(&t->xt_hi, d * t->t_ld);
+  take(&t->xt_lo, d * t->t_ld);
+  take(&t->actt_hi, H * t->t_ld);
+  take(&t->actt_lo, H * t->t_ld);
+  take(&t->gyt_hi, d * t->t_ld);
+  take(&t->gyt_lo, d * t->t_ld);
+  take(&t->gzt_hi, H * t->t_ld);
+  take(&t->gzt_lo, H * t->t_ld);
+  // down support: rows d (outputs) over H columns; up support: rows H (neurons) over d columns
+  t->dn_ld = mask_words(H);
+  t->up_ld = mask_words(d);
+  float* tables[4];
+  take(&tables[0], d * t->dn_ld);
+  take(&tables[1], d * t->dn_ld);
+  take(&tables[2], H * t->up_ld);
+  take(&tables[3], H * t->up_ld);
+  t->dn_mask = reinterpret_cast<uint32_t*>(tables[0]);
+  t->dn_first = reinterpret_cast<int32_t*>(tables[1]);
+  t->up_mask = reinterpret_cast<uint32_t*>(tables[2]);
+  t->up_first = reinterpret_cast<int32_t*>(tables[3]);
   return off;
+}
+
+static int build_support_tables(const int32_t* off, const int16_t* cols, int rows, int64_t ld, uint32_t* mask,
+                                int32_t* first, cudaStream_t s) {
+  if (ld > kMaxMaskWords) {
+    set_error("support tables: %lld mask words per row above %d", (long long)ld, kMaxMaskWords);
+    return HFFN_ERR_ARGUMENT;
+  }
+  const size_t smem = (size_t)kMaskWarps * ld * sizeof(uint32_t);
+  support_tables_kernel<<<(rows + kMaskWarps - 1) / kMaskWarps, 32 * kMaskWarps, smem, s>>>(off, cols, rows, (int)ld,
+                                                                                            mask, first);
+  return launch_status("support tables");
 }
 
 }  // namespace tc
@@ -947,7 +1091,8 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   const int d = L->d_model, H = L->d_ff, nn = (int)n;
   TrainWork w;
   train_floats(d, H, n, &w, reinterpret_cast<float*>(work));
-  const int rows = kTrainParts * (int)((n + kTrainBN - 1) / kTrainBN);
+  const int blocks = (int)((n + kTrainBN - 1) / kTrainBN);
+  const int rows_dn = kTrainPartsDown * blocks, rows_up = kTrainPartsUp * blocks;
   const int adam = opt != nullptr;
   const hffn_adamw_step st = opt ? *opt : hffn_adamw_step{};
   float* dense_up_hi = const_cast<float*>(reinterpret_cast<const float*>(up_hi));
@@ -961,15 +1106,23 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
       reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(w.x_hi), reinterpret_cast<float4*>(w.x_lo),
       count4);
   HFFN_TRY(launch_status("tc_split"));
-  // 1. up: z, act = gelu(z)                                       D[H, n] = W_up[H, d] x[n, d]^T
+  split_transpose_kernel<<<dim3((unsigned)ceil_div(n, 32), (unsigned)ceil_div(d, 32)), dim3(32, 8), 0, s>>>(
+      x, n, d, w.xt_hi, w.xt_lo, w.t_ld);
+  HFFN_TRY(launch_status("tc_split_transpose"));
+  HFFN_TRY(build_support_tables(L->out_offsets, L->out_hidden, d, w.dn_ld, w.dn_mask, w.dn_first, s));
+  HFFN_TRY(build_support_tables(L->up_offsets, L->up_idx, H, w.up_ld, w.up_mask, w.up_first, s));
+  // 1. up: z, act = gelu(z) (+ act^T)                             D[H, n] = W_up[H, d] x[n, d]^T
   EpilogueArgs e1{};
   e1.bias = L->b_up;
   e1.out_hi = w.act_hi;
   e1.out_lo = w.act_lo;
   e1.z = w.z;
+  e1.t_hi = w.actt_hi;
+  e1.t_lo = w.actt_lo;
+  e1.t_ld = w.t_ld;
   HFFN_TRY((launch_gemm<false, kTrainBN, 4, kUp, kFp32Chunk, 64, 8>(up_hi, up_lo, w.x_hi, w.x_lo, H, nn, d, e1, err,
                                                                      s)));
-  // 2. down + MSE: y, gy = 2 (y - target) / (n_total d)           D[d, n] = W_down[d, H] act[n, H]^T
+  // 2. down + MSE: y, gy = 2 (y - target) / (n_total d) (+ gy^T)  D[d, n] = W_down[d, H] act[n, H]^T
   EpilogueArgs e2{};
   e2.bias = L->b_down;
   e2.out_hi = y;
@@ -979,15 +1132,21 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   e2.scale = (float)(2.0 / ((double)n_total * d));
   e2.loss_partial = w.loss_p;
   e2.col_partial = w.dn_p;
+  e2.t_hi = w.gyt_hi;
+  e2.t_lo = w.gyt_lo;
+  e2.t_ld = w.t_ld;
   HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDownMse, kFp32Chunk, 64, 8>(down_hi, down_lo, w.act_hi, w.act_lo, d, nn,
                                                                           H, e2, err, s)));
-  // 3. gz = (W_down^T gy) * gelu'(z)                               D[H, n] = W_down^T[H, d] gy[n, d]^T
+  // 3. gz = (W_down^T gy) * gelu'(z) (+ gz^T)                      D[H, n] = W_down^T[H, d] gy[n, d]^T
   EpilogueArgs e3{};
   e3.out_hi = w.gz_hi;
   e3.out_lo = w.gz_lo;
   e3.z_in = w.z;
   e3.col_partial = w.up_p;
-  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kGradHidden, kFp32Chunk, 64, 8, true, false>(
+  e3.t_hi = w.gzt_hi;
+  e3.t_lo = w.gzt_lo;
+  e3.t_ld = w.t_ld;
+  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kGradHidden, kFp32Chunk, 64, 16, true, false>(
       down_hi, down_lo, w.gy_hi, w.gy_lo, H, nn, d, e3, err, s, H, 0)));
   // 4. gx = W_up^T gz                                              D[d, n] = W_up^T[d, H] gz[n, H]^T
   EpilogueArgs e4{};
@@ -995,9 +1154,11 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDown, kFp32Chunk, 64, 8, true, false>(up_hi, up_lo, w.gz_hi, w.gz_lo, d,
                                                                                     nn, H, e4, err, s, d, 0)));
   // 5. g_down sampled on the output-major support, AdamW, W_down refreshed   D[d, H] = gy^T[d, n] act^T[H, n]^T
+  //    (both operands K-major: the feature-major copies)
   EpilogueArgs e5{};
-  e5.offsets = L->out_offsets;
-  e5.cols = L->out_hidden;
+  e5.mask = w.dn_mask;
+  e5.first = w.dn_first;
+  e5.mask_ld = w.dn_ld;
   e5.value = P->out_val.value;
   e5.grad = P->out_val.grad;
   e5.m = P->out_val.m;
@@ -1006,12 +1167,13 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   e5.dense_lo = dense_dn_lo;
   e5.adam = adam;
   e5.step = st;
-  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kSampled, kFp32Chunk, 64, 8, true, true>(
-      w.gy_hi, w.gy_lo, w.act_hi, w.act_lo, d, H, nn, e5, err, s, d, H)));
+  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kSampled, kFp32Chunk, 64, 8, false, false>(
+      w.gyt_hi, w.gyt_lo, w.actt_hi, w.actt_lo, d, H, nn, e5, err, s, w.t_ld, w.t_ld)));
   // 6. g_up sampled on the hidden-major support, AdamW, W_up refreshed        D[H, d] = gz^T[H, n] x^T[d, n]^T
   EpilogueArgs e6{};
-  e6.offsets = L->up_offsets;
-  e6.cols = L->up_idx;
+  e6.mask = w.up_mask;
+  e6.first = w.up_first;
+  e6.mask_ld = w.up_ld;
   e6.value = P->up_val.value;
   e6.grad = P->up_val.grad;
   e6.m = P->up_val.m;
@@ -1020,14 +1182,14 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   e6.dense_lo = dense_up_lo;
   e6.adam = adam;
   e6.step = st;
-  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kSampled, kFp32Chunk, 64, 8, true, true>(
-      w.gz_hi, w.gz_lo, w.x_hi, w.x_lo, H, d, nn, e6, err, s, H, d)));
+  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kSampled, kFp32Chunk, 64, 8, false, false>(
+      w.gzt_hi, w.gzt_lo, w.xt_hi, w.xt_lo, H, d, nn, e6, err, s, w.t_ld, w.t_ld)));
   // 7. biases and loss
-  bias_reduce_kernel<<<(d + 255) / 256, 256, 0, s>>>(w.dn_p, rows, d, P->b_down, adam, st);
+  bias_reduce_kernel<<<(d + 255) / 256, 256, 0, s>>>(w.dn_p, rows_dn, d, P->b_down, adam, st);
   HFFN_TRY(launch_status("bias_reduce down"));
-  bias_reduce_kernel<<<(H + 255) / 256, 256, 0, s>>>(w.up_p, rows, H, P->b_up, adam, st);
+  bias_reduce_kernel<<<(H + 255) / 256, 256, 0, s>>>(w.up_p, rows_up, H, P->b_up, adam, st);
   HFFN_TRY(launch_status("bias_reduce up"));
-  loss_reduce_kernel<<<1, 256, 0, s>>>(w.loss_p, (int64_t)rows * d, 1.0 / ((double)n * d), loss);
+  loss_reduce_kernel<<<1, 256, 0, s>>>(w.loss_p, (int64_t)rows_dn * d, 1.0 / ((double)n * d), loss);
   return launch_status("loss_reduce");
 }
 
