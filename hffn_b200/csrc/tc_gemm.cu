@@ -44,7 +44,8 @@ constexpr uint64_t kWaitNs = 2000000000ull;
 // dense operand refreshed with the new value.
 // kDownPeer: as kDown, the value of token t stored into the buffer of the rank that owns t (peer memory over NVLink):
 // peers[t / tokens_per_owner] + (t % tokens_per_owner) * M + row.
-enum Epilogue { kUp = 0, kDown = 1, kDownMse = 2, kGradHidden = 3, kSampled = 4, kDownPeer = 5 };
+// kUpT: kUp of the training step, which also stores act^T (the feature-major copy).
+enum Epilogue { kUp = 0, kDown = 1, kDownMse = 2, kGradHidden = 3, kSampled = 4, kDownPeer = 5, kUpT = 6 };
 
 constexpr int kMaxPeers = 8;
 
@@ -192,8 +193,8 @@ struct EpilogueArgs {
   float* col_partial;    // kDownMse / kGradHidden: [num_n * parts, M] partial sums of gy / gz per row
   // kGradHidden
   const float* z_in;     // [N, M] pre-activations of the forward
-  // kUp / kDownMse / kGradHidden (float32), optional: feature-major copies [M, t_ld] of the tf32 hi / lo outputs
-  // (act, gy, gz), the K-major operands of the sampled weight-gradient GEMMs (t_ld: a multiple of 4 >= N)
+  // kUpT / kDownMse / kGradHidden (float32): feature-major copies [M, t_ld] of the tf32 hi / lo outputs (act, gy,
+  // gz), the K-major operands of the sampled weight-gradient GEMMs (t_ld: a multiple of 4 >= N)
   float* t_hi;
   float* t_lo;
   int64_t t_ld;
@@ -222,7 +223,7 @@ struct EpilogueArgs {
 // of an unrolled tile overflows the instruction cache.
 template <bool kBf16, int EPI>
 __device__ __forceinline__ float2 emit_one(const EpilogueArgs* e, int64_t at, float s, float& hi, float& lo) {
-  if constexpr (EPI == kUp) {
+  if constexpr (EPI == kUp || EPI == kUpT) {
     if (!kBf16 && e->z) e->z[at] = s;
     const float h = gelu(s);
     if constexpr (kBf16) {
@@ -264,15 +265,35 @@ __device__ __forceinline__ float2 emit_one(const EpilogueArgs* e, int64_t at, fl
   }
 }
 
-// Four values of one output row `row`, tokens t0 .. t0 + 3 (t0 a multiple of 4; those below N valid): bias added,
-// then the epilogue's stores, and (when the epilogue has them) the feature-major copies as one 16-byte store each;
-// returns the partial sums it contributes (loss, column sum). The four values are independent, so their chains
-// interleave. emit4 is out of line (the epilogue calls it once per 4 values: with 128 values per thread an inlined
-// copy per value overflows the instruction cache); emit4_inline is the same code inlined, for epilogues of at most
-// 64 values per thread (measured faster there: no call, no registers saved around it).
+// Four values of one output row (tokens t0 .. t0 + 3 at `stride` apart, `count` of them valid): bias added, then
+// the epilogue's stores; returns the partial sums it contributes (loss, column sum). The four values are independent,
+// so their chains interleave. Out of line (emit4) where a thread holds 128 values (an inlined copy per value of the
+// unrolled tile overflows the instruction cache), inlined (emit4_inline) where it holds at most 64 (measured faster:
+// no call, no registers saved around it).
 template <bool kBf16, int EPI>
-__device__ __forceinline__ float2 emit4_inline(const EpilogueArgs* e, int row, int t0, int M, int N, float bias,
-                                               float v0, float v1, float v2, float v3) {
+__device__ __forceinline__ float2 emit4_inline(const EpilogueArgs* e, int64_t at, int64_t stride, int count,
+                                               float bias, float v0, float v1, float v2, float v3) {
+  float2 acc = make_float2(0.f, 0.f), r;
+  float hi, lo;
+  if (count >= 4) {
+    r = emit_one<kBf16, EPI>(e, at, v0 + bias, hi, lo); acc.x += r.x; acc.y += r.y;
+    r = emit_one<kBf16, EPI>(e, at + stride, v1 + bias, hi, lo); acc.x += r.x; acc.y += r.y;
+    r = emit_one<kBf16, EPI>(e, at + 2 * stride, v2 + bias, hi, lo); acc.x += r.x; acc.y += r.y;
+    r = emit_one<kBf16, EPI>(e, at + 3 * stride, v3 + bias, hi, lo); acc.x += r.x; acc.y += r.y;
+    return acc;
+  }
+  if (count > 0) { r = emit_one<kBf16, EPI>(e, at, v0 + bias, hi, lo); acc.x += r.x; acc.y += r.y; }
+  if (count > 1) { r = emit_one<kBf16, EPI>(e, at + stride, v1 + bias, hi, lo); acc.x += r.x; acc.y += r.y; }
+  if (count > 2) { r = emit_one<kBf16, EPI>(e, at + 2 * stride, v2 + bias, hi, lo); acc.x += r.x; acc.y += r.y; }
+  return acc;
+}
+
+// The same for the training epilogues that also store feature-major copies (kUpT, kDownMse, kGradHidden): the four
+// values of row `row`, tokens t0 .. t0 + 3 (t0 a multiple of 4), and their tf32 hi / lo parts into the copies as one
+// 16-byte store each.
+template <bool kBf16, int EPI>
+__device__ __forceinline__ float2 emit4t_inline(const EpilogueArgs* e, int row, int t0, int M, int N, float bias,
+                                                float v0, float v1, float v2, float v3) {
   const int64_t at = (int64_t)t0 * M + row;
   const int count = N - t0;
   const float v[4] = {v0, v1, v2, v3};
@@ -285,36 +306,46 @@ __device__ __forceinline__ float2 emit4_inline(const EpilogueArgs* e, int row, i
       acc.x += r.x;
       acc.y += r.y;
     }
-  if constexpr (!kBf16 && (EPI == kUp || EPI == kDownMse || EPI == kGradHidden)) {
-    if (e->t_hi != nullptr) {
-      float* th = e->t_hi + (int64_t)row * e->t_ld + t0;
-      float* tl = e->t_lo + (int64_t)row * e->t_ld + t0;
-      if (count >= 4) {
-        *reinterpret_cast<float4*>(th) = make_float4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<float4*>(tl) = make_float4(l[0], l[1], l[2], l[3]);
-      } else {
-        for (int j = 0; j < count; ++j) {
-          th[j] = h[j];
-          tl[j] = l[j];
-        }
-      }
+  float* th = e->t_hi + (int64_t)row * e->t_ld + t0;
+  float* tl = e->t_lo + (int64_t)row * e->t_ld + t0;
+  if (count >= 4) {
+    *reinterpret_cast<float4*>(th) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(tl) = make_float4(l[0], l[1], l[2], l[3]);
+  } else {
+    for (int j = 0; j < count; ++j) {
+      th[j] = h[j];
+      tl[j] = l[j];
     }
   }
   return acc;
 }
 
 template <bool kBf16, int EPI>
-__device__ __noinline__ float2 emit4(const EpilogueArgs* e, int row, int t0, int M, int N, float bias, float v0,
-                                     float v1, float v2, float v3) {
-  return emit4_inline<kBf16, EPI>(e, row, t0, M, N, bias, v0, v1, v2, v3);
+__device__ __noinline__ float2 emit4(const EpilogueArgs* e, int64_t at, int64_t stride, int count, float bias,
+                                     float v0, float v1, float v2, float v3) {
+  return emit4_inline<kBf16, EPI>(e, at, stride, count, bias, v0, v1, v2, v3);
 }
 
-// emit4 or emit4_inline by the number of values per epilogue thread.
+template <bool kBf16, int EPI>
+__device__ __noinline__ float2 emit4t(const EpilogueArgs* e, int row, int t0, int M, int N, float bias, float v0,
+                                      float v1, float v2, float v3) {
+  return emit4t_inline<kBf16, EPI>(e, row, t0, M, N, bias, v0, v1, v2, v3);
+}
+
+// The emitter of an epilogue: with or without the feature-major copies, out of line or inlined by the number of
+// values per epilogue thread.
 template <bool kBf16, int EPI, int HALF>
 __device__ __forceinline__ float2 emit4_at(const EpilogueArgs* e, int row, int t0, int M, int N, float bias, float v0,
                                            float v1, float v2, float v3) {
-  if constexpr (HALF <= 64) return emit4_inline<kBf16, EPI>(e, row, t0, M, N, bias, v0, v1, v2, v3);
-  else return emit4<kBf16, EPI>(e, row, t0, M, N, bias, v0, v1, v2, v3);
+  constexpr bool kCopies = !kBf16 && (EPI == kUpT || EPI == kDownMse || EPI == kGradHidden);
+  if constexpr (kCopies) {
+    if constexpr (HALF <= 64) return emit4t_inline<kBf16, EPI>(e, row, t0, M, N, bias, v0, v1, v2, v3);
+    else return emit4t<kBf16, EPI>(e, row, t0, M, N, bias, v0, v1, v2, v3);
+  } else {
+    const int64_t at = (int64_t)t0 * M + row;
+    if constexpr (HALF <= 64) return emit4_inline<kBf16, EPI>(e, at, M, N - t0, bias, v0, v1, v2, v3);
+    else return emit4<kBf16, EPI>(e, at, M, N - t0, bias, v0, v1, v2, v3);
+  }
 }
 
 // One support entry q of row `row`, column `col`, gradient g: stored and / or applied by AdamW (PyTorch's fused order),
@@ -1120,7 +1151,7 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   e1.t_hi = w.actt_hi;
   e1.t_lo = w.actt_lo;
   e1.t_ld = w.t_ld;
-  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kUp, kFp32Chunk, 64, 8>(up_hi, up_lo, w.x_hi, w.x_lo, H, nn, d, e1, err,
+  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kUpT, kFp32Chunk, 64, 8>(up_hi, up_lo, w.x_hi, w.x_lo, H, nn, d, e1, err,
                                                                      s)));
   // 2. down + MSE: y, gy = 2 (y - target) / (n_total d) (+ gy^T)  D[d, n] = W_down[d, H] act[n, H]^T
   EpilogueArgs e2{};
