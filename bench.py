@@ -242,8 +242,7 @@ def gpu_arm(args, workload: dict) -> dict | None:
     else:
         runtime, shard, (lo, hi) = sharded_runtime(case.d_model, canonical(layer, torch), device, dtype,
                                                    tensor_cores=tensor_cores, segments=args.segments,
-                                                   comm_sms=args.comm_sms, transport=args.transport,
-                                                   peers_per_chunk=args.peers_per_chunk, push=args.push)
+                                                   comm_sms=args.comm_sms, transport=args.transport, push=args.push)
     if args.path == "tensor_cores":
         runtime.force("tc", "tc")
     d, f_local = case.d_model, hi - lo
@@ -308,7 +307,20 @@ def gpu_arm(args, workload: dict) -> dict | None:
             marks[2].record(stream)
         torch.cuda.synchronize(device)
         step_events = None
-        if world > 1:
+        if world > 1 and args.transport == "peer":
+            # the sharded steps as one pipelined stream of batches (forward_many): batch k's gathers and batch
+            # k - 2's deliveries run on the copy engines during batch k - 1's GEMMs; each step's working set
+            # (gathered batches, activations, partial outputs) exceeds L2, which is not flushed inside the stream
+            shard.forward_many([x] * args.warmup)
+            dist.barrier()
+            torch.cuda.synchronize(device)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            shard.forward_many([x] * args.steps)
+            b.record(stream)
+            torch.cuda.synchronize(device)
+            step_ms_pipelined = a.elapsed_time(b) / args.steps
+        elif world > 1:
             # the sharded step: broadcast / compute / reduce pipeline over the ranks' batches
             for _ in range(args.warmup):
                 flush.zero_()
@@ -327,6 +339,8 @@ def gpu_arm(args, workload: dict) -> dict | None:
     up_ms = [e[0].elapsed_time(e[1]) for e in kernel_events]
     down_ms = [e[1].elapsed_time(e[2]) for e in kernel_events]
     step_ms = [e[0].elapsed_time(e[2]) for e in (step_events or kernel_events)]
+    if world > 1 and args.transport == "peer":
+        step_ms = [step_ms_pipelined] * args.steps
 
     # end to end through the public API: every step copies its batch from pinned host memory to the device, runs the
     # forward and copies the output back to pinned host memory; HostPipeline overlaps step k's kernels with the copy
@@ -414,9 +428,10 @@ def gpu_arm(args, workload: dict) -> dict | None:
         "config": {"workload": f"{case.name}: d_model {d}, d_ff {case.d_ff}, support {case.up_degree}, "
                                f"N {n} tokens per GPU per step", "modes": [up, down],
                    "parallelism": "single" if world == 1 else
-                   f"neuron-sharded x{world} (NVLink peer memory: copy-engine pulls of the batches, partial outputs "
-                   f"pushed into the owners' slots by {'the down GEMM epilogue' if args.push == 'store' else 'copy engines'}"
-                   f", {shard.peers_per_chunk} peers per chunk)" if args.transport == "peer" else
+                   f"neuron-sharded x{world} (NVLink peer memory, pipelined over batches: copy-engine gathers, "
+                   f"partial outputs delivered into the owners' slots by "
+                   f"{'the down GEMM epilogue' if args.push == 'store' else 'copy engines'})" if args.transport == "peer"
+                   else
                    f"neuron-sharded x{world} (all-gather / reduce-scatter pipeline over NCCL, "
                    f"{shard.segments} segments, {shard.comm_sms} SMs left to NCCL)",
                    "l2": "flushed between steps (512 MiB write)"},
@@ -619,7 +634,6 @@ def main() -> int:
     parser.add_argument("--comm-sms", type=int, default=0, help="sharded forward: SMs left to the collectives")
     parser.add_argument("--transport", choices=("nccl", "peer"), default="nccl",
                         help="sharded forward: NCCL collectives or NVLink peer memory (tensor cores)")
-    parser.add_argument("--peers-per-chunk", type=int, default=None, help="peer sharded forward: batches per chunk")
     parser.add_argument("--push", choices=("copy", "store"), default="copy",
                         help="peer sharded forward: partial outputs pushed by copy engines or by the GEMM epilogue")
     parser.add_argument("--path", choices=("auto", "cuda_cores", "tensor_cores"), default="auto",

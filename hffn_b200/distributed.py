@@ -154,11 +154,10 @@ def x_is_cuda(ffn: "ShardedFFN") -> bool:
 
 
 def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, tensor_cores=None, group=None,
-                    segments: int | None = None, comm_sms: int = 0, transport: str = "nccl",
-                    peers_per_chunk: int | None = None, push: str = "copy"):
+                    segments: int | None = None, comm_sms: int = 0, transport: str = "nccl", push: str = "copy"):
     """The rank's ``HFFNRuntime`` over its neuron shard and the sharded forward around it: ``transport="nccl"`` a
-    ``ShardedFFN`` (collective kernels), ``"peer"`` a ``PeerShardedFFN`` (NVLink peer memory, tensor cores only;
-    ``forward`` only)."""
+    ``ShardedFFN`` (collective kernels), ``"peer"`` a ``PeerShardedFFN`` (NVLink peer memory and copy engines,
+    pipelined over batches, tensor cores only, ``push`` its delivery mode)."""
     if transport not in ("nccl", "peer"):
         raise ValueError("transport must be 'nccl' or 'peer'")
     from .runtime import HFFNLayer, HFFNRuntime
@@ -173,7 +172,251 @@ def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, ten
                                         shard["down_idx"], shard["down_val"])
     runtime = HFFNRuntime([layer], device, dtype, tensor_cores=tensor_cores)
     if transport == "peer":
-        return runtime, PeerShardedFFN(runtime, d_model, group, peers_per_chunk=peers_per_chunk, push=push), (lo, hi)
+        return runtime, PeerShardedFFN(runtime, d_model, group, push=push), (lo, hi)
+    ffn = ShardedFFN(lambda x, out: runtime.forward(0, x, out=out), d_model, group, segments=segments,
+                     comm_sms=comm_sms)
+    return runtime, ffn, (lo, hi)
+
+
+class DataParallelTrainer:
+    """Data-parallel MSE training step over an ``HFFNTrainRuntime`` replica per rank."""
+
+    def __init__(self, train, group=None) -> None:
+        self.train = train
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self._loss = torch.zeros(1, dtype=torch.float64, device=train.runtime.device)
+
+    def step_mse(self, index: int, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+        """One step on this rank's tokens; returns the mean loss over all ranks' tokens (before the update)."""
+        from . import _native as native
+        train = self.train
+        n = train._check_tokens(target, "target")
+        if train.uses_tensor_cores(index, n):
+            # gradients of the mean over all ranks' tokens (n_total = world n): summed, not averaged
+            train.step_mse_tc(index, x, target, n_total=n * self.world, apply=False)
+            grads = train.gradients(index)
+            for name in ("up_val", "b_up", "out_val", "b_down"):
+                dist.all_reduce(grads[name], op=dist.ReduceOp.SUM, group=self.group)
+            train.apply_adamw(index)
+            self._loss.copy_(train._loss)
+            dist.all_reduce(self._loss, op=dist.ReduceOp.SUM, group=self.group)
+            return self._loss / self.world
+        y = train.forward(index, x, train._z)
+        gy = train._gy[:n]
+        native.check(native.lib.hffn_mse(y.data_ptr(), target.data_ptr(), gy.data_ptr(), train._loss.data_ptr(), n,
+                                         train.d_model, train._work.data_ptr(),
+                                         native.stream_handle(train.runtime.device)), "hffn_mse")
+        train.backward(index, gy)
+        grads = train.gradients(index)
+        for name in ("up_val", "b_up", "out_val", "b_down"):
+            dist.all_reduce(grads[name], op=dist.ReduceOp.SUM, group=self.group)
+            grads[name].mul_(1.0 / self.world)
+        train.adamw(index)
+        self._loss.copy_(train._loss)
+        dist.all_reduce(self._loss, op=dist.ReduceOp.SUM, group=self.group)
+        return self._loss / self.world
+
+
+class PeerShardedFFN:
+    """The neuron-sharded forward over a stream of batches, its exchange through NVLink peer memory and copy engines
+    instead of collective kernels, pipelined across batches.
+
+    Every rank holds its neuron shard and hands in one batch [n, d] per step (all ranks the same n). Batch k of rank
+    r goes through: staging into this rank's symmetric gather buffer; copy-engine pulls into every other rank (one
+    stream per peer, no SM); on each rank, one call of its shard (up, down on the tensor cores) over all ranks'
+    batches; the partial outputs of the tokens of rank p delivered into rank p's receive slot for r, by copy-engine
+    pushes from a local buffer (``push="copy"``) or by the down GEMM's epilogue storing straight into the peer's slot
+    over NVLink (``push="store"``, ``hffn_down_tc_peer``); each rank sums its slots in rank order
+    (``hffn_sum_slots``: a fixed summation order, whatever the timing).
+
+    Iteration k of ``forward_many`` stages batch k, waits for the pulls of batch k - 1 and the deliveries of batch
+    k - 3, passes one barrier (a 1-element NCCL all-reduce), starts the pulls of batch k, runs the shard over batch
+    k - 1, starts the delivery of its partial outputs and sums the slots of batch k - 3. So the pulls of one batch and
+    the deliveries of another run on the copy engines while the GEMMs of a third run on the SMs. Gather buffers and
+    partial outputs are double-buffered, receive slots triple-buffered; the barrier orders every reuse (a buffer is
+    rewritten only after every rank has passed the barrier that follows its last reader). Buffers live in symmetric
+    memory (``torch.distributed._symmetric_memory``, plain peer mappings, no multicast object); no collective kernel
+    runs beside the GEMMs and no load with multicast is issued. Requires the tensor-core runtime.
+    """
+
+    SLOTS = 3
+
+    def __init__(self, runtime, d_model: int, group=None, push: str = "copy") -> None:
+        if not runtime.tensor_cores:
+            raise ValueError("the peer-memory sharded forward runs on the tensor-core path")
+        if push not in ("store", "copy"):
+            raise ValueError("push must be 'store' or 'copy'")
+        self.runtime = runtime
+        self.d_model = d_model
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        if self.world > 8:
+            raise ValueError("at most 8 ranks (one box)")
+        self.push = push
+        self._state: dict = {}
+
+    def _setup(self, n: int, dtype: torch.dtype, device) -> dict:
+        import os
+
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import _native as native
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")   # plain peer mappings: no multicast object
+        d, w, r = self.d_model, self.world, self.rank
+        elem = torch.empty(0, dtype=dtype).element_size()
+        order = [(r + j) % w for j in range(w)]        # position j of a gathered batch: the tokens of rank order[j]
+        gather, gather_peer = [], []
+        for _ in range(2):
+            buf = symm_mem.empty(w * n, d, dtype=dtype, device=device)
+            handle = symm_mem.rendezvous(buf, self.group)
+            gather.append((buf, handle))
+            gather_peer.append([handle.get_buffer(p, (w * n, d), dtype)[:n] for p in order])
+        slots, slot_peer, slot_ptrs = [], [], []
+        for _ in range(self.SLOTS):
+            buf = symm_mem.empty(w, n, d, dtype=dtype, device=device)
+            handle = symm_mem.rendezvous(buf, self.group)
+            slots.append((buf, handle))
+            slot_peer.append([handle.get_buffer(p, (w, n, d), dtype)[r] for p in order])
+            slot_ptrs.append((ctypes.c_uint64 * w)(*(int(handle.buffer_ptrs[p]) + r * n * d * elem for p in order)))
+        runtime = self.runtime
+        m = w * n
+        work = torch.empty(int(native.lib.hffn_forward_tc_workspace(runtime._code, runtime._structs[0], m)),
+                           dtype=torch.uint8, device=device)
+        return {
+            "gather": gather, "gather_peer": gather_peer, "slots": slots, "slot_peer": slot_peer,
+            "slot_ptrs": slot_ptrs, "work": work,
+            "partial": [torch.empty(m, d, dtype=dtype, device=device) for _ in range(2)] if self.push == "copy" else None,
+            "flag": torch.zeros(1, device=device),
+            "pull_streams": [torch.cuda.Stream(device) for _ in range(w)],
+            "push_streams": [torch.cuda.Stream(device) for _ in range(w)],
+            "pulled": [[torch.cuda.Event() for _ in range(w)] for _ in range(2)],
+            "delivered": [[torch.cuda.Event() for _ in range(w)] for _ in range(self.SLOTS)],
+            "barrier_done": torch.cuda.Event(), "computed": torch.cuda.Event()}
+
+    def _barrier(self, state: dict) -> None:
+        dist.all_reduce(state["flag"], op=dist.ReduceOp.SUM, group=self.group)
+
+    def _run(self, state: dict, x_ptr: int, m: int, stream, y_ptr=None, targets=None) -> None:
+        """The shard's up GEMM over ``m`` tokens at ``x_ptr``, then its down GEMM into ``y_ptr`` or, with ``targets``
+        (one per rank, rotated order), into the owners' receive slots."""
+        from . import _native as native
+        runtime = self.runtime
+        dense, struct = runtime._dense[0], runtime._structs[0]
+        ptr = lambda v: None if v is None else v.data_ptr()  # noqa: E731
+        d, f = self.d_model, runtime.d_ff
+        work = state["work"].data_ptr()
+        if runtime.dtype == torch.float32:
+            x_split, act_hi = work, work + 2 * m * d * 4
+            act_lo = act_hi + m * f * 4
+        else:
+            x_split, act_hi, act_lo = None, work, None
+        err = runtime._err.data_ptr()
+        native.check(native.lib.hffn_up_tc(runtime._code, x_ptr, ptr(dense["up_hi"]), ptr(dense["up_lo"]), struct.b_up,
+                                           act_hi, act_lo, None, x_split, err, d, f, m, stream), "hffn_up_tc")
+        if targets is None:
+            native.check(native.lib.hffn_down_tc(runtime._code, act_hi, act_lo, ptr(dense["down_hi"]),
+                                                 ptr(dense["down_lo"]), struct.b_down, y_ptr, err, d, f, m, stream),
+                         "hffn_down_tc")
+        else:
+            native.check(native.lib.hffn_down_tc_peer(runtime._code, act_hi, act_lo, ptr(dense["down_hi"]),
+                                                      ptr(dense["down_lo"]), struct.b_down, targets, self.world,
+                                                      m // self.world, err, d, f, m, stream), "hffn_down_tc_peer")
+        runtime.calls["tc", "tc"] += 1
+
+    def forward(self, x_local: torch.Tensor) -> torch.Tensor:
+        """One batch: ``forward_many([x_local])[0]``."""
+        return self.forward_many([x_local])[0]
+
+    def forward_many(self, xs: list[torch.Tensor], outs: list[torch.Tensor] | None = None) -> list[torch.Tensor]:
+        """The layer's output for each batch of ``xs`` (this rank's tokens), every rank calling with the same number
+        of batches of the same shape. ``outs``: contiguous [n, d] tensors to write (else allocated)."""
+        from . import _native as native
+        runtime = self.runtime
+        if not xs:
+            return []
+        n, d, w = xs[0].shape[0], self.d_model, self.world
+        for x in xs:
+            runtime._check_input(x)
+            if x.shape[0] != n:
+                raise ValueError("every batch of one call has the same token count")
+        if outs is None:
+            outs = [torch.empty(n, d, dtype=xs[0].dtype, device=xs[0].device) for _ in xs]
+        elif len(outs) != len(xs) or any(o.shape != (n, d) or o.dtype != xs[0].dtype or not o.is_contiguous()
+                                         for o in outs):
+            raise ValueError("outs: one contiguous [n, d] tensor of the input dtype per batch")
+        key = (n, xs[0].dtype)
+        if key not in self._state:
+            self._state[key] = self._setup(n, xs[0].dtype, xs[0].device)
+        st = self._state[key]
+        if runtime._dense_stale[0]:
+            runtime._densify(0)
+        compute = torch.cuda.current_stream(xs[0].device)
+        handle = compute.cuda_stream
+        count = len(xs)
+        for k in range(count + 3):
+            g = k % 2
+            if k < count:                                           # stage batch k
+                st["gather"][g][0][:n].copy_(xs[k])
+            if 1 <= k <= count:                                     # pulls of batch k - 1 landed
+                for j in range(1, w):
+                    compute.wait_event(st["pulled"][(k - 1) % 2][j])
+            if 3 <= k:                                              # deliveries of batch k - 3 started here
+                for j in range(w):
+                    compute.wait_event(st["delivered"][(k - 3) % self.SLOTS][j])
+            self._barrier(st)
+            st["barrier_done"].record(compute)
+            if k < count:                                           # pulls of batch k (copy engines)
+                for j in range(1, w):
+                    stream = st["pull_streams"][j]
+                    stream.wait_event(st["barrier_done"])
+                    with torch.cuda.stream(stream):
+                        st["gather"][g][0][j * n:(j + 1) * n].copy_(st["gather_peer"][g][j], non_blocking=True)
+                        st["pulled"][g][j].record(stream)
+            if 1 <= k <= count:                                     # the shard over batch k - 1
+                b, slot = (k - 1) % 2, (k - 1) % self.SLOTS
+                x_ptr = st["gather"][b][0].data_ptr()
+                if self.push == "store":
+                    self._run(st, x_ptr, w * n, handle, targets=st["slot_ptrs"][slot])
+                    for j in range(w):
+                        st["delivered"][slot][j].record(compute)
+                else:
+                    partial = st["partial"][b]
+                    self._run(st, x_ptr, w * n, handle, y_ptr=partial.data_ptr())
+                    st["computed"].record(compute)
+                    for j in range(w):                              # deliveries (copy engines; own slot: local)
+                        stream = st["push_streams"][j]
+                        stream.wait_event(st["computed"])
+                        with torch.cuda.stream(stream):
+                            st["slot_peer"][slot][j].copy_(partial[j * n:(j + 1) * n], non_blocking=True)
+                            st["delivered"][slot][j].record(stream)
+            if 3 <= k:                                              # batch k - 3: every partial has landed
+                native.check(native.lib.hffn_sum_slots(runtime._code, st["slots"][(k - 3) % self.SLOTS][0].data_ptr(),
+                                                       w, n * d, outs[k - 3].data_ptr(), handle), "hffn_sum_slots")
+        return outs
+
+
+def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, tensor_cores=None, group=None,
+                    segments: int | None = None, comm_sms: int = 0, transport: str = "nccl", push: str = "copy"):
+    """The rank's ``HFFNRuntime`` over its neuron shard and the sharded forward around it: ``transport="nccl"`` a
+    ``ShardedFFN`` (collective kernels), ``"peer"`` a ``PeerShardedFFN`` (NVLink peer memory and copy engines,
+    pipelined over batches, tensor cores only, ``push`` its delivery mode)."""
+    if transport not in ("nccl", "peer"):
+        raise ValueError("transport must be 'nccl' or 'peer'")
+    from .runtime import HFFNLayer, HFFNRuntime
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    bounds = neuron_partition(arrays, world)
+    lo, hi = bounds[rank], bounds[rank + 1]
+    if hi <= lo:
+        raise ValueError(f"rank {rank} owns no hidden neuron (d_ff {arrays['b_up'].numel()} over {world} ranks)")
+    shard = shard_hidden_major(d_model, arrays, lo, hi, with_bias=rank == 0)
+    layer = HFFNLayer.from_hidden_major(shard["d_model"], shard["d_ff"], shard["b_up"], shard["up_offsets"],
+                                        shard["up_idx"], shard["up_val"], shard["b_down"], shard["down_offsets"],
+                                        shard["down_idx"], shard["down_val"])
+    runtime = HFFNRuntime([layer], device, dtype, tensor_cores=tensor_cores)
+    if transport == "peer":
+        return runtime, PeerShardedFFN(runtime, d_model, group, push=push), (lo, hi)
     ffn = ShardedFFN(lambda x, out: runtime.forward(0, x, out=out), d_model, group, segments=segments,
                      comm_sms=comm_sms)
     return runtime, ffn, (lo, hi)

@@ -65,17 +65,25 @@ def _worker(rank: int, world: int, port: int, results) -> None:
             out[f"sharded_tc{int(tensor_cores)}"] = max(rel_rep, rel_own)
             out[f"errors_tc{int(tensor_cores)}"] = runtime.device_errors()
 
-        # the peer-memory form (tensor cores): two batch sizes, each run twice (buffers reused across steps)
-        runtime, peer, _ = sharded_runtime(layer.d_model, arrays, device, tensor_cores=True, transport="peer")
-        worst = 0.0
-        for n_own in (260, 1000):
-            x_own = torch.from_numpy(synth.make_input(case, n_own + rank)[:n_own]).to(device)
-            expected = full.forward(0, x_own).double()
-            for _ in range(2):
-                y_peer = peer.forward(x_own)
-                worst = max(worst, float(((y_peer.double() - expected).abs() / expected.abs().clamp(min=1)).max()))
+        # the peer-memory form (tensor cores), both delivery modes: single batches of two sizes, then a stream of
+        # five different batches (the pipeline across batches; buffers reused within and across calls)
+        worst, errors = 0.0, 0
+        for push in ("copy", "store"):
+            runtime, peer, _ = sharded_runtime(layer.d_model, arrays, device, tensor_cores=True, transport="peer",
+                                               push=push)
+            for n_own in (260, 1000):
+                x_own = torch.from_numpy(synth.make_input(case, n_own + rank)[:n_own]).to(device)
+                expected = full.forward(0, x_own).double()
+                for _ in range(2):
+                    y_peer = peer.forward(x_own)
+                    worst = max(worst, float(((y_peer.double() - expected).abs() / expected.abs().clamp(min=1)).max()))
+            xs = [torch.from_numpy(synth.make_input(case, 300 + 7 * k + rank)[:300]).to(device) for k in range(5)]
+            for x_k, y_k in zip(xs, peer.forward_many(xs)):
+                expected = full.forward(0, x_k).double()
+                worst = max(worst, float(((y_k.double() - expected).abs() / expected.abs().clamp(min=1)).max()))
+            errors += runtime.device_errors()
         out["sharded_peer"] = worst
-        out["errors_peer"] = runtime.device_errors()
+        out["errors_peer"] = errors
 
         # data-parallel training: 2 x 64 tokens against one GPU on the 128 concatenated tokens
         n = 64
