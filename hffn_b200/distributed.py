@@ -395,228 +395,3 @@ class PeerShardedFFN:
                 native.check(native.lib.hffn_sum_slots(runtime._code, st["slots"][(k - 3) % self.SLOTS][0].data_ptr(),
                                                        w, n * d, outs[k - 3].data_ptr(), handle), "hffn_sum_slots")
         return outs
-
-
-def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, tensor_cores=None, group=None,
-                    segments: int | None = None, comm_sms: int = 0, transport: str = "nccl", push: str = "copy"):
-    """The rank's ``HFFNRuntime`` over its neuron shard and the sharded forward around it: ``transport="nccl"`` a
-    ``ShardedFFN`` (collective kernels), ``"peer"`` a ``PeerShardedFFN`` (NVLink peer memory and copy engines,
-    pipelined over batches, tensor cores only, ``push`` its delivery mode)."""
-    if transport not in ("nccl", "peer"):
-        raise ValueError("transport must be 'nccl' or 'peer'")
-    from .runtime import HFFNLayer, HFFNRuntime
-    rank, world = dist.get_rank(group), dist.get_world_size(group)
-    bounds = neuron_partition(arrays, world)
-    lo, hi = bounds[rank], bounds[rank + 1]
-    if hi <= lo:
-        raise ValueError(f"rank {rank} owns no hidden neuron (d_ff {arrays['b_up'].numel()} over {world} ranks)")
-    shard = shard_hidden_major(d_model, arrays, lo, hi, with_bias=rank == 0)
-    layer = HFFNLayer.from_hidden_major(shard["d_model"], shard["d_ff"], shard["b_up"], shard["up_offsets"],
-                                        shard["up_idx"], shard["up_val"], shard["b_down"], shard["down_offsets"],
-                                        shard["down_idx"], shard["down_val"])
-    runtime = HFFNRuntime([layer], device, dtype, tensor_cores=tensor_cores)
-    if transport == "peer":
-        return runtime, PeerShardedFFN(runtime, d_model, group, push=push), (lo, hi)
-    ffn = ShardedFFN(lambda x, out: runtime.forward(0, x, out=out), d_model, group, segments=segments,
-                     comm_sms=comm_sms)
-    return runtime, ffn, (lo, hi)
-
-
-class DataParallelTrainer:
-    """Data-parallel MSE training step over an ``HFFNTrainRuntime`` replica per rank."""
-
-    def __init__(self, train, group=None) -> None:
-        self.train = train
-        self.group = group
-        self.world = dist.get_world_size(group)
-        self._loss = torch.zeros(1, dtype=torch.float64, device=train.runtime.device)
-
-    def step_mse(self, index: int, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
-        """One step on this rank's tokens; returns the mean loss over all ranks' tokens (before the update)."""
-        from . import _native as native
-        train = self.train
-        n = train._check_tokens(target, "target")
-        if train.uses_tensor_cores(index, n):
-            # gradients of the mean over all ranks' tokens (n_total = world n): summed, not averaged
-            train.step_mse_tc(index, x, target, n_total=n * self.world, apply=False)
-            grads = train.gradients(index)
-            for name in ("up_val", "b_up", "out_val", "b_down"):
-                dist.all_reduce(grads[name], op=dist.ReduceOp.SUM, group=self.group)
-            train.apply_adamw(index)
-            self._loss.copy_(train._loss)
-            dist.all_reduce(self._loss, op=dist.ReduceOp.SUM, group=self.group)
-            return self._loss / self.world
-        y = train.forward(index, x, train._z)
-        gy = train._gy[:n]
-        native.check(native.lib.hffn_mse(y.data_ptr(), target.data_ptr(), gy.data_ptr(), train._loss.data_ptr(), n,
-                                         train.d_model, train._work.data_ptr(),
-                                         native.stream_handle(train.runtime.device)), "hffn_mse")
-        train.backward(index, gy)
-        grads = train.gradients(index)
-        for name in ("up_val", "b_up", "out_val", "b_down"):
-            dist.all_reduce(grads[name], op=dist.ReduceOp.SUM, group=self.group)
-            grads[name].mul_(1.0 / self.world)
-        train.adamw(index)
-        self._loss.copy_(train._loss)
-        dist.all_reduce(self._loss, op=dist.ReduceOp.SUM, group=self.group)
-        return self._loss / self.world
-
-
-class PeerShardedFFN:
-    """The neuron-sharded forward with its exchange over NVLink peer memory instead of collective kernels.
-
-    Buffers in symmetric memory (``torch.distributed._symmetric_memory``, plain peer mappings): each rank's staged
-    batch ``x_in [n, d]`` and its receive slots ``slots [world, n, d]`` (slot p: the partial output that rank p computed
-    for this rank's tokens). A step:
-
-    1. stage x into ``x_in``; barrier (a 1-element NCCL all-reduce): every rank's batch is staged;
-    2. the other ranks' batches are pulled into local memory by copy-engine copies, one stream per peer (no SM);
-    3. the rank's shard runs on its own batch first (overlapping the pulls), its partial output going straight to its
-       own slot; then on the pulled batches in groups of ``peers_per_chunk`` owners, each group once its pulls have
-       landed. A group's partial outputs reach their owners' slots either from the down GEMM's epilogue (``push=
-       "store"``: ``hffn_down_tc_peer`` stores over NVLink tile by tile) or by copy-engine copies from a local buffer
-       overlapping the next group's GEMMs (``push="copy"``);
-    4. barrier: every partial has landed; each rank sums its slots in rank order (``hffn_sum_slots``).
-
-    The summation order of a token's output is fixed (slot order), whatever the timing. Requires the tensor-core
-    runtime; every rank passes batches of the same shape. No collective kernel runs beside the GEMMs, and no load
-    with multicast is issued.
-    """
-
-    def __init__(self, runtime, d_model: int, group=None, peers_per_chunk: int | None = None,
-                 push: str = "copy") -> None:
-        if not runtime.tensor_cores:
-            raise ValueError("the peer-memory sharded forward runs on the tensor-core path")
-        if push not in ("store", "copy"):
-            raise ValueError("push must be 'store' or 'copy'")
-        self.runtime = runtime
-        self.d_model = d_model
-        self.group = group if group is not None else dist.group.WORLD
-        self.rank = dist.get_rank(self.group)
-        self.world = dist.get_world_size(self.group)
-        if self.world > 8:
-            raise ValueError("at most 8 ranks (one box)")
-        self.peers_per_chunk = max(1, peers_per_chunk or 2)
-        self.push = push
-        self._state: dict = {}
-
-    def _chunks(self) -> list[list[int]]:
-        """Positions 1 .. world - 1 (rotated peer order: position j is rank (rank + j) % world) in groups."""
-        rest = list(range(1, self.world))
-        k = self.peers_per_chunk
-        return [rest[i:i + k] for i in range(0, len(rest), k)]
-
-    def _setup(self, n: int, dtype: torch.dtype, device) -> dict:
-        import os
-
-        import torch.distributed._symmetric_memory as symm_mem
-
-        from . import _native as native
-        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")   # plain peer mappings: no multicast object
-        d, w, r = self.d_model, self.world, self.rank
-        elem = torch.empty(0, dtype=dtype).element_size()
-        x_in = symm_mem.empty(n, d, dtype=dtype, device=device)
-        hx = symm_mem.rendezvous(x_in, self.group)
-        slots = symm_mem.empty(w, n, d, dtype=dtype, device=device)
-        hs = symm_mem.rendezvous(slots, self.group)
-        order = [(r + j) % w for j in range(w)]                       # rotated: own batch first
-        chunks = self._chunks()
-        runtime = self.runtime
-        m = max([n] + [len(c) * n for c in chunks])
-        work = torch.empty(int(native.lib.hffn_forward_tc_workspace(runtime._code, runtime._structs[0], m)),
-                           dtype=torch.uint8, device=device)
-        targets = [int(hs.buffer_ptrs[p]) + r * n * d * elem for p in order]
-        rest = max(1, w - 1) * n
-        return {
-            "x_in": x_in, "hx": hx, "slots": slots, "hs": hs, "work": work,
-            "peers_x": [hx.get_buffer(p, (n, d), dtype) for p in order],
-            "peer_slot": [hs.get_buffer(p, (w, n, d), dtype)[r] for p in order],
-            "x_all": torch.empty(rest, d, dtype=dtype, device=device),
-            "y_part": torch.empty(rest, d, dtype=dtype, device=device) if self.push == "copy" else None,
-            "chunks": chunks,
-            "targets": [(ctypes.c_uint64 * len(c))(*(targets[j] for j in c)) for c in chunks],
-            "flag": torch.zeros(1, device=device),
-            "streams": [torch.cuda.Stream(device) for _ in range(w)],
-            "pulled": [torch.cuda.Event() for _ in range(w)],
-            "computed": [torch.cuda.Event() for _ in range(len(chunks))],
-            "pushed": [torch.cuda.Event() for _ in range(w)],
-            "staged": torch.cuda.Event()}
-
-    def _barrier(self, state: dict) -> None:
-        dist.all_reduce(state["flag"], op=dist.ReduceOp.SUM, group=self.group)
-
-    def _run(self, state: dict, x_ptr: int, m: int, stream, y_ptr=None, targets=None, count: int = 0) -> None:
-        """The shard's up GEMM over ``m`` tokens at ``x_ptr``, then its down GEMM into ``y_ptr`` (local) or, with
-        ``targets``, into the ``count`` owners' slots (``m = count n``)."""
-        from . import _native as native
-        runtime = self.runtime
-        dense, struct = runtime._dense[0], runtime._structs[0]
-        ptr = lambda v: None if v is None else v.data_ptr()  # noqa: E731
-        d, f = self.d_model, runtime.d_ff
-        work = state["work"].data_ptr()
-        if runtime.dtype == torch.float32:
-            x_split, act_hi = work, work + 2 * m * d * 4
-            act_lo = act_hi + m * f * 4
-        else:
-            x_split, act_hi, act_lo = None, work, None
-        err = runtime._err.data_ptr()
-        native.check(native.lib.hffn_up_tc(runtime._code, x_ptr, ptr(dense["up_hi"]), ptr(dense["up_lo"]), struct.b_up,
-                                           act_hi, act_lo, None, x_split, err, d, f, m, stream), "hffn_up_tc")
-        if targets is None:
-            native.check(native.lib.hffn_down_tc(runtime._code, act_hi, act_lo, ptr(dense["down_hi"]),
-                                                 ptr(dense["down_lo"]), struct.b_down, y_ptr, err, d, f, m, stream),
-                         "hffn_down_tc")
-        else:
-            native.check(native.lib.hffn_down_tc_peer(runtime._code, act_hi, act_lo, ptr(dense["down_hi"]),
-                                                      ptr(dense["down_lo"]), struct.b_down, targets, count, m // count,
-                                                      err, d, f, m, stream), "hffn_down_tc_peer")
-        runtime.calls["tc", "tc"] += 1
-
-    def forward(self, x_local: torch.Tensor) -> torch.Tensor:
-        from . import _native as native
-        runtime = self.runtime
-        n, d = x_local.shape[0], self.d_model
-        runtime._check_input(x_local)
-        key = (n, x_local.dtype)
-        if key not in self._state:
-            self._state[key] = self._setup(n, x_local.dtype, x_local.device)
-        state = self._state[key]
-        if runtime._dense_stale[0]:
-            runtime._densify(0)
-        compute = torch.cuda.current_stream(x_local.device)
-        handle = compute.cuda_stream
-        streams, pulled, pushed = state["streams"], state["pulled"], state["pushed"]
-        state["x_in"].copy_(x_local)
-        self._barrier(state)                                   # every rank's batch is staged
-        state["staged"].record(compute)
-        for j in range(1, self.world):                         # copy-engine pulls, one stream per peer
-            streams[j].wait_event(state["staged"])
-            with torch.cuda.stream(streams[j]):
-                state["x_all"][(j - 1) * n:j * n].copy_(state["peers_x"][j], non_blocking=True)
-                pulled[j].record(streams[j])
-        # the own batch first, overlapping the pulls: its partial output goes to this rank's own slot
-        self._run(state, x_local.data_ptr(), n, handle, y_ptr=state["slots"][self.rank].data_ptr())
-        for c, chunk in enumerate(state["chunks"]):
-            for j in chunk:
-                compute.wait_event(pulled[j])
-            first = chunk[0] - 1
-            x_ptr = state["x_all"][first * n:].data_ptr()
-            m = len(chunk) * n
-            if self.push == "store":
-                self._run(state, x_ptr, m, handle, targets=state["targets"][c], count=len(chunk))
-                continue
-            self._run(state, x_ptr, m, handle, y_ptr=state["y_part"][first * n:].data_ptr())
-            state["computed"][c].record(compute)
-            for j in chunk:                                    # copy-engine pushes into the owners' slots
-                streams[j].wait_event(state["computed"][c])
-                with torch.cuda.stream(streams[j]):
-                    state["peer_slot"][j].copy_(state["y_part"][(j - 1) * n:j * n], non_blocking=True)
-                    pushed[j].record(streams[j])
-        if self.push == "copy":
-            for j in range(1, self.world):
-                compute.wait_event(pushed[j])
-        self._barrier(state)                                   # every partial has landed in its owner's slots
-        out = torch.empty(n, d, dtype=x_local.dtype, device=x_local.device)
-        native.check(native.lib.hffn_sum_slots(runtime._code, state["slots"].data_ptr(), self.world, n * d,
-                                               out.data_ptr(), handle), "hffn_sum_slots")
-        return out

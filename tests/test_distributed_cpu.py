@@ -95,3 +95,16 @@ def test_gloo_two_ranks():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert dict(results) == {0: (True, True), 1: (True, True)}
+
+
+def test_peer_forward_requires_tensor_cores_and_checks_push():
+    """The peer-memory sharded forward refuses a runtime without the tensor-core path and an unknown delivery mode
+    before touching the process group (its exchange is exercised on GPUs)."""
+    import types
+
+    from hffn_b200.distributed import PeerShardedFFN
+    assert callable(getattr(PeerShardedFFN, "forward_many", None))
+    with pytest.raises(ValueError):
+        PeerShardedFFN(types.SimpleNamespace(tensor_cores=False), 64)
+    with pytest.raises(ValueError):
+        PeerShardedFFN(types.SimpleNamespace(tensor_cores=True), 64, push="broadcast")
