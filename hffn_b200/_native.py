@@ -26,6 +26,13 @@ class Layer(ctypes.Structure):
                 ("b_down", _P), ("out_offsets", _P), ("out_hidden", _P), ("out_val", _P)]
 
 
+class PeerConfig(ctypes.Structure):
+    _fields_ = [("world", _I32), ("rank", _I32), ("tokens", _I64), ("dtype", _I32),
+                ("gather", _P * 2), ("gather_peer", (ctypes.c_uint64 * 8) * 2),
+                ("slots", _P * 3), ("slot_peer", (ctypes.c_uint64 * 8) * 3),
+                ("partial", _P * 2), ("signal", _P), ("signal_peer", ctypes.c_uint64 * 8), ("work", _P)]
+
+
 class Supports(ctypes.Structure):
     _fields_ = [("in_offsets", _P), ("in_pos", _P), ("in_hidden", _P),
                 ("hid_offsets", _P), ("hid_pos", _P), ("hid_output", _P)]
@@ -72,6 +79,12 @@ SIGNATURES = {
     "hffn_down_tc_peer": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, ctypes.POINTER(ctypes.c_uint64), _I32, _I64,
                                          _P, _I32, _I32, _I64, _P]),
     "hffn_sum_slots": (ctypes.c_int, [ctypes.c_int, _P, _I32, _I64, _P, _P]),
+    "hffn_peer_pipeline_create": (ctypes.c_int, [ctypes.POINTER(PeerConfig), ctypes.POINTER(Layer),
+                                                  ctypes.POINTER(Dense), _P, ctypes.POINTER(_P)]),
+    "hffn_peer_pipeline_run": (ctypes.c_int, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), _I32, _P]),
+    "hffn_peer_pipeline_destroy": (ctypes.c_int, [_P]),
+    "hffn_peer_barrier": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint64), _I32, _I32, ctypes.c_uint32, _I64, _P,
+                                         _P]),
     "hffn_gemm_tc_f32": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64,
                                         _P, _P]),
     "hffn_train_step_tc_workspace": (_I64, [ctypes.POINTER(Layer), _I64]),

@@ -220,27 +220,22 @@ class DataParallelTrainer:
 
 class PeerShardedFFN:
     """The neuron-sharded forward over a stream of batches, its exchange through NVLink peer memory and copy engines
-    instead of collective kernels, pipelined across batches.
+    instead of collective kernels, pipelined across batches (the native loop ``hffn_peer_pipeline_run``).
 
-    Every rank holds its neuron shard and hands in one batch [n, d] per step (all ranks the same n). Batch k of rank
-    r goes through: staging into this rank's symmetric gather buffer; copy-engine pulls into every other rank (one
-    stream per peer, no SM); on each rank, one call of its shard (up, down on the tensor cores) over all ranks'
-    batches; the partial outputs of the tokens of rank p delivered into rank p's receive slot for r, by copy-engine
-    pushes from a local buffer (``push="copy"``) or by the down GEMM's epilogue storing straight into the peer's slot
-    over NVLink (``push="store"``, ``hffn_down_tc_peer``); each rank sums its slots in rank order
-    (``hffn_sum_slots``: a fixed summation order, whatever the timing).
+    Every rank holds its neuron shard and hands in batches [n, d] (all ranks the same n and count). Batch k of rank
+    r is staged into r's gather buffer, pulled by copy engines into every other rank's gather buffer, run through
+    every rank's shard (one up + down call over all ranks' batches), and each rank's partial outputs for the tokens
+    of rank p are delivered into p's receive slot for it: by copy engines from a local buffer (``push="copy"``) or by
+    the down GEMM's epilogue storing into the peer's slot over NVLink (``push="store"``); every rank sums its slots
+    in rank order (a fixed summation order, whatever the timing). Iteration k stages batch k, waits for the pulls of
+    batch k - 1 and the deliveries of batch k - 3, passes a barrier over signal pads in peer memory (bounded waits: a
+    dead or late peer ends in error flag 201, never a hang), starts the pulls of batch k, runs batch k - 1, starts
+    its deliveries and sums batch k - 3: the copy engines move one batch in and another out while the SMs run a third.
 
-    Iteration k of ``forward_many`` stages batch k, waits for the pulls of batch k - 1 and the deliveries of batch
-    k - 3, passes one barrier (a 1-element NCCL all-reduce), starts the pulls of batch k, runs the shard over batch
-    k - 1, starts the delivery of its partial outputs and sums the slots of batch k - 3. So the pulls of one batch and
-    the deliveries of another run on the copy engines while the GEMMs of a third run on the SMs. Gather buffers and
-    partial outputs are double-buffered, receive slots triple-buffered; the barrier orders every reuse (a buffer is
-    rewritten only after every rank has passed the barrier that follows its last reader). Buffers live in symmetric
-    memory (``torch.distributed._symmetric_memory``, plain peer mappings, no multicast object); no collective kernel
-    runs beside the GEMMs and no load with multicast is issued. Requires the tensor-core runtime.
+    Buffers live in symmetric memory (``torch.distributed._symmetric_memory``, plain peer mappings, no multicast
+    object); no collective kernel runs beside the GEMMs and no load with multicast is issued. Requires the
+    tensor-core runtime.
     """
-
-    SLOTS = 3
 
     def __init__(self, runtime, d_model: int, group=None, push: str = "copy") -> None:
         if not runtime.tensor_cores:
@@ -265,65 +260,64 @@ class PeerShardedFFN:
         from . import _native as native
         os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")   # plain peer mappings: no multicast object
         d, w, r = self.d_model, self.world, self.rank
+        runtime = self.runtime
         elem = torch.empty(0, dtype=dtype).element_size()
-        order = [(r + j) % w for j in range(w)]        # position j of a gathered batch: the tokens of rank order[j]
-        gather, gather_peer = [], []
-        for _ in range(2):
+        order = [(r + j) % w for j in range(w)]        # position j: rank (r + j) % w
+        cfg = native.PeerConfig()
+        cfg.world, cfg.rank, cfg.tokens, cfg.dtype = w, r, n, runtime._code
+        keep = []
+        for b in range(2):
             buf = symm_mem.empty(w * n, d, dtype=dtype, device=device)
             handle = symm_mem.rendezvous(buf, self.group)
-            gather.append((buf, handle))
-            gather_peer.append([handle.get_buffer(p, (w * n, d), dtype)[:n] for p in order])
-        slots, slot_peer, slot_ptrs = [], [], []
-        for _ in range(self.SLOTS):
+            keep += [buf, handle]
+            cfg.gather[b] = buf.data_ptr()
+            for j, p in enumerate(order):
+                cfg.gather_peer[b][j] = int(handle.buffer_ptrs[p])
+        slots = []
+        for b in range(3):
             buf = symm_mem.empty(w, n, d, dtype=dtype, device=device)
             handle = symm_mem.rendezvous(buf, self.group)
-            slots.append((buf, handle))
-            slot_peer.append([handle.get_buffer(p, (w, n, d), dtype)[r] for p in order])
-            slot_ptrs.append((ctypes.c_uint64 * w)(*(int(handle.buffer_ptrs[p]) + r * n * d * elem for p in order)))
-        runtime = self.runtime
-        m = w * n
-        work = torch.empty(int(native.lib.hffn_forward_tc_workspace(runtime._code, runtime._structs[0], m)),
+            keep += [buf, handle]
+            slots.append(buf)
+            cfg.slots[b] = buf.data_ptr()
+            for j, p in enumerate(order):
+                cfg.slot_peer[b][j] = int(handle.buffer_ptrs[p]) + r * n * d * elem
+        signal = symm_mem.empty(w, dtype=torch.int32, device=device)
+        signal_handle = symm_mem.rendezvous(signal, self.group)
+        keep += [signal, signal_handle]
+        signal.zero_()
+        cfg.signal = signal.data_ptr()
+        for j, p in enumerate(order):
+            cfg.signal_peer[j] = int(signal_handle.buffer_ptrs[p])
+        partial = [torch.empty(w * n, d, dtype=dtype, device=device) for _ in range(2)] if self.push == "copy" else []
+        for b, buf in enumerate(partial):
+            cfg.partial[b] = buf.data_ptr()
+        work = torch.empty(int(native.lib.hffn_forward_tc_workspace(runtime._code, runtime._structs[0], w * n)),
                            dtype=torch.uint8, device=device)
-        return {
-            "gather": gather, "gather_peer": gather_peer, "slots": slots, "slot_peer": slot_peer,
-            "slot_ptrs": slot_ptrs, "work": work,
-            "partial": [torch.empty(m, d, dtype=dtype, device=device) for _ in range(2)] if self.push == "copy" else None,
-            "flag": torch.zeros(1, device=device),
-            "pull_streams": [torch.cuda.Stream(device) for _ in range(w)],
-            "push_streams": [torch.cuda.Stream(device) for _ in range(w)],
-            "pulled": [[torch.cuda.Event() for _ in range(w)] for _ in range(2)],
-            "delivered": [[torch.cuda.Event() for _ in range(w)] for _ in range(self.SLOTS)],
-            "barrier_done": torch.cuda.Event(), "computed": torch.cuda.Event()}
+        cfg.work = work.data_ptr()
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)                # every rank's pad is zeroed before any signal
+        if runtime._dense_stale[0]:
+            runtime._densify(0)
+        pipeline = ctypes.c_void_p()
+        native.check(native.lib.hffn_peer_pipeline_create(ctypes.byref(cfg), ctypes.byref(runtime._structs[0]),
+                                                          ctypes.byref(runtime._dense_structs[0]),
+                                                          runtime._err.data_ptr(), ctypes.byref(pipeline)),
+                     "hffn_peer_pipeline_create")
+        return {"pipeline": pipeline, "config": cfg, "keep": keep, "slots": slots, "partial": partial, "work": work}
 
-    def _barrier(self, state: dict) -> None:
-        dist.all_reduce(state["flag"], op=dist.ReduceOp.SUM, group=self.group)
-
-    def _run(self, state: dict, x_ptr: int, m: int, stream, y_ptr=None, targets=None) -> None:
-        """The shard's up GEMM over ``m`` tokens at ``x_ptr``, then its down GEMM into ``y_ptr`` or, with ``targets``
-        (one per rank, rotated order), into the owners' receive slots."""
+    def close(self) -> None:
+        """Release the native pipelines (their buffers go with this object)."""
         from . import _native as native
-        runtime = self.runtime
-        dense, struct = runtime._dense[0], runtime._structs[0]
-        ptr = lambda v: None if v is None else v.data_ptr()  # noqa: E731
-        d, f = self.d_model, runtime.d_ff
-        work = state["work"].data_ptr()
-        if runtime.dtype == torch.float32:
-            x_split, act_hi = work, work + 2 * m * d * 4
-            act_lo = act_hi + m * f * 4
-        else:
-            x_split, act_hi, act_lo = None, work, None
-        err = runtime._err.data_ptr()
-        native.check(native.lib.hffn_up_tc(runtime._code, x_ptr, ptr(dense["up_hi"]), ptr(dense["up_lo"]), struct.b_up,
-                                           act_hi, act_lo, None, x_split, err, d, f, m, stream), "hffn_up_tc")
-        if targets is None:
-            native.check(native.lib.hffn_down_tc(runtime._code, act_hi, act_lo, ptr(dense["down_hi"]),
-                                                 ptr(dense["down_lo"]), struct.b_down, y_ptr, err, d, f, m, stream),
-                         "hffn_down_tc")
-        else:
-            native.check(native.lib.hffn_down_tc_peer(runtime._code, act_hi, act_lo, ptr(dense["down_hi"]),
-                                                      ptr(dense["down_lo"]), struct.b_down, targets, self.world,
-                                                      m // self.world, err, d, f, m, stream), "hffn_down_tc_peer")
-        runtime.calls["tc", "tc"] += 1
+        for state in self._state.values():
+            native.lib.hffn_peer_pipeline_destroy(state["pipeline"])
+        self._state.clear()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
 
     def forward(self, x_local: torch.Tensor) -> torch.Tensor:
         """One batch: ``forward_many([x_local])[0]``."""
@@ -336,7 +330,7 @@ class PeerShardedFFN:
         runtime = self.runtime
         if not xs:
             return []
-        n, d, w = xs[0].shape[0], self.d_model, self.world
+        n, d = xs[0].shape[0], self.d_model
         for x in xs:
             runtime._check_input(x)
             if x.shape[0] != n:
@@ -344,54 +338,17 @@ class PeerShardedFFN:
         if outs is None:
             outs = [torch.empty(n, d, dtype=xs[0].dtype, device=xs[0].device) for _ in xs]
         elif len(outs) != len(xs) or any(o.shape != (n, d) or o.dtype != xs[0].dtype or not o.is_contiguous()
-                                         for o in outs):
-            raise ValueError("outs: one contiguous [n, d] tensor of the input dtype per batch")
+                                         or o.device != xs[0].device for o in outs):
+            raise ValueError("outs: one contiguous [n, d] tensor of the input dtype and device per batch")
         key = (n, xs[0].dtype)
         if key not in self._state:
             self._state[key] = self._setup(n, xs[0].dtype, xs[0].device)
-        st = self._state[key]
         if runtime._dense_stale[0]:
             runtime._densify(0)
-        compute = torch.cuda.current_stream(xs[0].device)
-        handle = compute.cuda_stream
         count = len(xs)
-        for k in range(count + 3):
-            g = k % 2
-            if k < count:                                           # stage batch k
-                st["gather"][g][0][:n].copy_(xs[k])
-            if 1 <= k <= count:                                     # pulls of batch k - 1 landed
-                for j in range(1, w):
-                    compute.wait_event(st["pulled"][(k - 1) % 2][j])
-            if 3 <= k:                                              # deliveries of batch k - 3 started here
-                for j in range(w):
-                    compute.wait_event(st["delivered"][(k - 3) % self.SLOTS][j])
-            self._barrier(st)
-            st["barrier_done"].record(compute)
-            if k < count:                                           # pulls of batch k (copy engines)
-                for j in range(1, w):
-                    stream = st["pull_streams"][j]
-                    stream.wait_event(st["barrier_done"])
-                    with torch.cuda.stream(stream):
-                        st["gather"][g][0][j * n:(j + 1) * n].copy_(st["gather_peer"][g][j], non_blocking=True)
-                        st["pulled"][g][j].record(stream)
-            if 1 <= k <= count:                                     # the shard over batch k - 1
-                b, slot = (k - 1) % 2, (k - 1) % self.SLOTS
-                x_ptr = st["gather"][b][0].data_ptr()
-                if self.push == "store":
-                    self._run(st, x_ptr, w * n, handle, targets=st["slot_ptrs"][slot])
-                    for j in range(w):
-                        st["delivered"][slot][j].record(compute)
-                else:
-                    partial = st["partial"][b]
-                    self._run(st, x_ptr, w * n, handle, y_ptr=partial.data_ptr())
-                    st["computed"].record(compute)
-                    for j in range(w):                              # deliveries (copy engines; own slot: local)
-                        stream = st["push_streams"][j]
-                        stream.wait_event(st["computed"])
-                        with torch.cuda.stream(stream):
-                            st["slot_peer"][slot][j].copy_(partial[j * n:(j + 1) * n], non_blocking=True)
-                            st["delivered"][slot][j].record(stream)
-            if 3 <= k:                                              # batch k - 3: every partial has landed
-                native.check(native.lib.hffn_sum_slots(runtime._code, st["slots"][(k - 3) % self.SLOTS][0].data_ptr(),
-                                                       w, n * d, outs[k - 3].data_ptr(), handle), "hffn_sum_slots")
+        x_ptrs = (ctypes.c_void_p * count)(*(x.data_ptr() for x in xs))
+        out_ptrs = (ctypes.c_void_p * count)(*(o.data_ptr() for o in outs))
+        native.check(native.lib.hffn_peer_pipeline_run(self._state[key]["pipeline"], x_ptrs, out_ptrs, count,
+                                                       native.stream_handle(xs[0].device)), "hffn_peer_pipeline_run")
+        runtime.calls["tc", "tc"] += count
         return outs

@@ -190,6 +190,46 @@ int hffn_down_tc_peer(int dtype, const void* act_hi, const void* act_lo, const v
  * outputs its peers stored. */
 int hffn_sum_slots(int dtype, const void* slots, int32_t count, int64_t elems, void* out, void* stream);
 
+/* The neuron-sharded forward over a stream of batches, exchanged through NVLink peer memory (no reference
+ * counterpart: the reference runs one GPU). Buffers come from the caller (symmetric memory mapped on every rank);
+ * positions j = 0 .. world - 1 name rank (rank + j) % world. Per batch of n tokens: gather[b] [world n, d] holds the
+ * gathered batch (rows [0, n) this rank's, staged from the caller's input; rows of position j pulled from
+ * gather_peer[b][j]); the shard runs over it; its partial outputs go to slot_peer[s][j] (this rank's slot in the
+ * receive buffer of position j) from partial[b] by copy engines, or, with partial == NULL, from the down GEMM's
+ * epilogue; slots[s] [world, n, d] receives the peers' partials and is summed in rank order into the output. The
+ * signal pads (uint32 [world], zeroed on every rank before the first run) carry the barrier between iterations. */
+typedef struct hffn_peer_config {
+  int32_t world;
+  int32_t rank;
+  int64_t tokens;                 /* n: tokens per rank per batch */
+  int32_t dtype;
+  void* gather[2];
+  uint64_t gather_peer[2][8];
+  void* slots[3];
+  uint64_t slot_peer[3][8];
+  void* partial[2];               /* both NULL: delivery by the down GEMM's epilogue */
+  uint32_t* signal;
+  uint64_t signal_peer[8];
+  void* work;                     /* hffn_forward_tc_workspace(world n) bytes */
+} hffn_peer_config;
+
+/* A pipeline over the rank's shard (layer: its compact arrays; dense: its densified operands). err: the device error
+ * flag its kernels set (201: a barrier wait ran out: a peer is dead or late). */
+int hffn_peer_pipeline_create(const hffn_peer_config* config, const hffn_layer* layer, const hffn_dense* dense,
+                              int32_t* err, void** pipeline);
+
+/* outs[k] [n, d] = the layer's output for this rank's batch xs[k] [n, d], k < count; every rank calls with the same
+ * count. Iteration k stages batch k, waits for the pulls of batch k - 1 and the deliveries of batch k - 3, passes the
+ * barrier, pulls batch k, runs the shard over batch k - 1, delivers its partials and sums batch k - 3. */
+int hffn_peer_pipeline_run(void* pipeline, const void* const* xs, void* const* outs, int32_t count, void* stream);
+
+int hffn_peer_pipeline_destroy(void* pipeline);
+
+/* One barrier over the signal pads: writes epoch into this rank's slot of every peer's pad, then waits until every
+ * peer's slot of signal holds at least epoch, for at most timeout_ns (then err = 201 and the kernel returns). */
+int hffn_peer_barrier(uint32_t* signal, const uint64_t* signal_peer, int32_t world, int32_t rank, uint32_t epoch,
+                      int64_t timeout_ns, int32_t* err, void* stream);
+
 /* Cap on the CTAs of the persistent tensor-core GEMMs, process-wide (0: one per SM, the default). A tuning knob with
  * no reference counterpart: the neuron-sharded forward leaves a few SMs to the NCCL kernels so that its collectives
  * run alongside the GEMMs. */

@@ -69,3 +69,38 @@ def test_tuning_knobs_check_their_arguments():
     for tokens in (64, 128, 256, 0):
         assert n.lib.hffn_set_tc_tile_tokens(tokens) == n.HFFN_OK
     assert n.lib.hffn_set_tc_max_ctas(0) == n.HFFN_OK
+
+
+def test_peer_config_layout_matches_the_header(tmp_path):
+    """The ctypes mirror of hffn_peer_config has the C layout (size and field offsets, from a probe built with gcc)."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+
+    from hffn_b200 import _native as n
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    include = Path(n.__file__).resolve().parents[1] / "include"
+    fields = ["gather", "gather_peer", "slots", "slot_peer", "partial", "signal", "signal_peer", "work"]
+    probe = tmp_path / "probe.c"
+    probe.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"hffn_b200.h\"\nint main(void){printf(\"%zu"
+                     + " %zu" * len(fields) + "\\n\", sizeof(hffn_peer_config)"
+                     + "".join(f", offsetof(hffn_peer_config, {f})" for f in fields) + ");return 0;}\n")
+    subprocess.run(["gcc", f"-I{include}", str(probe), "-o", str(tmp_path / "probe")], check=True)
+    c_side = [int(v) for v in subprocess.run([str(tmp_path / "probe")], capture_output=True, text=True,
+                                             check=True).stdout.split()]
+    py_side = [ctypes.sizeof(n.PeerConfig)] + [getattr(n.PeerConfig, f).offset for f in fields]
+    assert c_side == py_side
+
+
+def test_peer_entries_check_their_arguments():
+    from hffn_b200 import _native as n
+    handle = ctypes.c_void_p()
+    cfg = n.PeerConfig()
+    cfg.world, cfg.rank, cfg.tokens, cfg.dtype = 2, 2, 16, n.F32          # rank outside the world
+    assert n.lib.hffn_peer_pipeline_create(ctypes.byref(cfg), ctypes.byref(n.Layer()), ctypes.byref(n.Dense()), 1,
+                                           ctypes.byref(handle)) == n.HFFN_ERR_ARGUMENT
+    assert n.lib.hffn_peer_pipeline_run(None, None, None, 0, None) == n.HFFN_ERR_ARGUMENT
+    peers = (ctypes.c_uint64 * 2)(0, 0)
+    assert n.lib.hffn_peer_barrier(1, peers, 2, 0, 1, 1000, 1, None) == n.HFFN_ERR_ARGUMENT    # rank 1's pad missing
+    assert n.lib.hffn_peer_barrier(1, peers, 2, 0, 1, 0, 1, None) == n.HFFN_ERR_ARGUMENT       # no time limit
