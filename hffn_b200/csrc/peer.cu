@@ -13,7 +13,7 @@
 // rewritten only after every rank passed the barrier that follows its last reader).
 //
 // The barrier: every rank writes the barrier's epoch into its slot of every peer's signal pad (system-scope release
-// store) and waits until every peer's slot of its own pad holds at least the epoch (acquire loads), for at most
+// store) and waits until every peer's slot of its own pad holds at least the epoch (polled, then an acquire fence), for at most
 // timeout_ns, after which it records kErrBarrierTimeout and returns: a dead or late peer ends the wait with an error
 // status, never a hang. Only ranks on distinct GPUs wait on one another.
 #include <cuda_runtime.h>
@@ -50,9 +50,9 @@ __device__ __forceinline__ void store_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t load_relaxed_sys(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -67,13 +67,16 @@ __global__ void barrier_kernel(PeerSignals sig, int world, int rank, uint32_t ep
   if (p >= world || p == rank) return;
   __threadfence_system();                      // this rank's earlier writes before the signal
   store_release_sys(sig.peer[p] + rank, epoch);
+  // poll with relaxed loads and a short back-off (no stream of system-scope fences), then one acquire fence
   const uint64_t start = now_ns();
-  while ((int32_t)(load_acquire_sys(sig.own + p) - epoch) < 0) {
+  while ((int32_t)(load_relaxed_sys(sig.own + p) - epoch) < 0) {
     if ((int64_t)(now_ns() - start) > timeout_ns) {
       atomicCAS(err, 0, kErrBarrierTimeout);
       return;
     }
+    __nanosleep(256);
   }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 }  // namespace
@@ -197,7 +200,7 @@ static int create_pipeline(const hffn_peer_config* cfg, const hffn_layer* layer,
   p->elem = cfg->dtype == HFFN_BF16 ? 2 : 4;
   cudaGetDevice(&p->device);
   bool ok = true;
-  for (int j = 0; j < kMaxWorld && ok; ++j) {
+  for (int j = 0; j < cfg->world && ok; ++j) {
     ok = cudaStreamCreateWithFlags(&p->pull[j], cudaStreamNonBlocking) == cudaSuccess &&
          cudaStreamCreateWithFlags(&p->push[j], cudaStreamNonBlocking) == cudaSuccess;
     for (int b = 0; b < 2 && ok; ++b) ok = cudaEventCreateWithFlags(&p->pulled[b][j], cudaEventDisableTiming) == cudaSuccess;
