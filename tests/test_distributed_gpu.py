@@ -1,10 +1,10 @@
-"""GPU, NCCL, 2 ranks (skipped with fewer than 2 GPUs): the neuron-sharded forward and the data-parallel training
+"""GPU, NCCL, 2 and 4 ranks (each skipped with fewer GPUs): the neuron-sharded forward and the data-parallel training
 step against one GPU.
 
 Sharded forward (the replicated and the per-rank-batch forms, tensor cores and CUDA cores, and the peer-memory form
 on tensor cores) equals the single-GPU runtime's output within the forward tolerance (the partial sums are added in
 another order). The data-parallel MSE
-step of two ranks gives the gradients (all-reduced mean) and the loss of a single-GPU step on the concatenation of
+step of the ranks gives the gradients (all-reduced mean) and the loss of a single-GPU step on the concatenation of
 their batches within float32 tolerance (the update itself is AdamW of those gradients, tested on one GPU)."""
 import os
 import socket
@@ -85,14 +85,14 @@ def _worker(rank: int, world: int, port: int, results) -> None:
         out["sharded_peer"] = worst
         out["errors_peer"] = errors
 
-        # data-parallel training: 2 x 64 tokens against one GPU on the 128 concatenated tokens
+        # data-parallel training: world x 64 tokens against one GPU on the concatenated tokens
         n = 64
-        xs = [synth.make_input(case, 128)[k * n:(k + 1) * n] for k in range(world)]
-        ts = [synth.make_target(case, 128)[k * n:(k + 1) * n] for k in range(world)]
+        xs = [synth.make_input(case, world * n)[k * n:(k + 1) * n] for k in range(world)]
+        ts = [synth.make_target(case, world * n)[k * n:(k + 1) * n] for k in range(world)]
         dp_train = HFFNTrainRuntime(HFFNRuntime([_kernel_layer(layer)], device, tensor_cores=False), max_tokens=n)
         dp = DataParallelTrainer(dp_train)
         loss = float(dp.step_mse(0, torch.from_numpy(xs[rank]).to(device), torch.from_numpy(ts[rank]).to(device)))
-        one = HFFNTrainRuntime(HFFNRuntime([_kernel_layer(layer)], device, tensor_cores=False), max_tokens=2 * n)
+        one = HFFNTrainRuntime(HFFNRuntime([_kernel_layer(layer)], device, tensor_cores=False), max_tokens=world * n)
         loss_one = float(one.step_mse(0, torch.from_numpy(np.concatenate(xs)).to(device),
                                       torch.from_numpy(np.concatenate(ts)).to(device)))
         worst = 0.0
@@ -107,13 +107,15 @@ def _worker(rank: int, world: int, port: int, results) -> None:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_ranks():
+@pytest.mark.parametrize("world", [2, 4])
+def test_ranks(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     manager = ctx.Manager()
     results = manager.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(rank, 2, port, results)) for rank in range(2)]
+    procs = [ctx.Process(target=_worker, args=(rank, world, port, results)) for rank in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -121,7 +123,7 @@ def test_two_ranks():
         if p.is_alive():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    for rank in range(2):
+    for rank in range(world):
         r = results[rank]
         assert r["sharded_tc1"] <= 1e-5 and r["sharded_tc0"] <= 1e-5, r
         assert r["errors_tc1"] == 0 and r["errors_tc0"] == 0, r
