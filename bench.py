@@ -40,6 +40,12 @@ WORKLOADS = {
     "pythia410m": {"case": "c4_1024_4096_k512", "n": 8 * 512, "dtype": "bf16", "batch": 8, "prompt": 512,
                    "decode": 128},
 }
+# DRAM bytes (read + write) per launch of the dominant kernel from one `ncu --set full` capture of the same workload
+# on a B200 (dram__bytes_read.sum + dram__bytes_write.sum); the command and the figures are in the named summary under
+# profiles/. Keyed by (workload, kernel); a kernel without a capture reports null.
+NCU_TRAFFIC = {
+    ("fwd", "tc_gemm_up"): (142.489e6 + 96.618e6, "profiles/fwd_tensor_cores_c2_fp32.md"),
+}
 CLOCK_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
                "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
                "clocks_event_reasons.sw_power_cap")
@@ -400,9 +406,12 @@ def gpu_arm(args, workload: dict) -> dict | None:
         passes = 3 if elem == 4 else 1
         dense_flops = 2.0 * n_kernel * f_local * d * passes
         pipe_peak = pk["bf16_tflops"] / (2 if elem == 4 else 1)
+        traffic, traffic_source = NCU_TRAFFIC.get((args.workload, f"tc_gemm_{top}"), (None, None)) \
+            if world == 1 else (None, None)
         roofline = {"bound": "tensor", "kernel": f"tc_gemm_{top}", "achieved": achieved_tflops,
                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved_tflops / pk["bf16_tflops"],
-                    "traffic": None, "algorithmic_flops": alg[top]["flops"], "launch_ms": kernel_ms[top],
+                    "traffic": traffic, "traffic_source": traffic_source,
+                    "algorithmic_flops": alg[top]["flops"], "launch_ms": kernel_ms[top],
                     "peak_source": pk_source,
                     "tensor_pipe": {"kind": "tf32 x3 (3xTF32 split)" if elem == 4 else "bf16",
                                     "executed_tflops": dense_flops / seconds / 1e12, "peak_tflops": pipe_peak,
