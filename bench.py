@@ -45,6 +45,7 @@ WORKLOADS = {
 # profiles/. Keyed by (workload, kernel); a kernel without a capture reports null.
 NCU_TRAFFIC = {
     ("fwd", "tc_gemm_up"): (142.489e6 + 96.618e6, "profiles/fwd_tensor_cores_c2_fp32.md"),
+    ("fwd_bf16", "tc_gemm_up"): (16.834e6 + 0.433e6, "profiles/fwd_tensor_cores_c2_bf16.md"),
 }
 CLOCK_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
                "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"

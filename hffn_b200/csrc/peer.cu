@@ -13,13 +13,10 @@
 // rewritten only after every rank passed the barrier that follows its last reader).
 //
 // The barrier: every rank writes the barrier's epoch into its slot of every peer's signal pad (system-scope release
-// store) and waits until every peer's slot of its own pad holds at least the epoch (polled, then an acquire fence), for at most
-// timeout_ns, after which it records kErrBarrierTimeout and returns: a dead or late peer ends the wait with an error
-// status, never a hang. Only ranks on distinct GPUs wait on one another.
+// store) and waits until every peer's slot of its own pad holds at least the epoch (polled with back-off, then an
+// acquire fence), for at most timeout_ns, after which it records kErrBarrierTimeout and returns: a dead or late peer
+// ends the wait with an error status, never a hang. Only ranks on distinct GPUs wait on one another.
 #include <cuda_runtime.h>
-
-#include <cstring>
-#include <vector>
 
 #include "common.cuh"
 
@@ -203,7 +200,8 @@ static int create_pipeline(const hffn_peer_config* cfg, const hffn_layer* layer,
   for (int j = 0; j < cfg->world && ok; ++j) {
     ok = cudaStreamCreateWithFlags(&p->pull[j], cudaStreamNonBlocking) == cudaSuccess &&
          cudaStreamCreateWithFlags(&p->push[j], cudaStreamNonBlocking) == cudaSuccess;
-    for (int b = 0; b < 2 && ok; ++b) ok = cudaEventCreateWithFlags(&p->pulled[b][j], cudaEventDisableTiming) == cudaSuccess;
+    for (int b = 0; b < 2 && ok; ++b)
+      ok = cudaEventCreateWithFlags(&p->pulled[b][j], cudaEventDisableTiming) == cudaSuccess;
     for (int b = 0; b < 3 && ok; ++b)
       ok = cudaEventCreateWithFlags(&p->delivered[b][j], cudaEventDisableTiming) == cudaSuccess;
   }

@@ -15,10 +15,11 @@
 // float32 accumulation runs in K chunks of 128 values (48 MMAs) into fresh TMEM accumulators that the epilogue adds
 // into float32 registers with round-to-nearest: the accumulation bias of the tensor core stays bounded by one chunk.
 //
-// Kernel shape: persistent, one CTA per SM, 6 warps: warp 0 issues the TMA loads (one elected thread), warp 1 owns
-// the TMEM allocation and issues the MMAs (one elected thread), warps 2-9 run the epilogue (one TMEM lane = one
-// feature row per thread, two warps per lane quarter splitting the token columns). Two accumulator buffers in TMEM let the epilogue of one tile overlap the MMAs of the
-// next. Shared-memory stages are recycled through mbarriers (full: TMA -> MMA, empty: MMA commit -> TMA); every wait
+// Kernel shape: persistent, one CTA per SM: warp 0 issues the TMA loads (lane 0 arms each stage, then one box per
+// lane), warp 1 owns the TMEM allocation and issues the MMAs (one elected thread), EW = 8 or 16 epilogue warps
+// follow (one TMEM lane = one feature row per thread, EW / 4 warps per lane quarter splitting the token columns).
+// Two accumulator buffers in TMEM let the epilogue of one tile overlap the MMAs of the next. Shared-memory stages are
+// recycled through mbarriers (full: TMA -> MMA, empty: MMA commit -> TMA); every wait
 // is bounded by a 2 s timer after which the kernel records an error code, stops issuing work, waits (bounded) for its
 // own copies in flight, frees its TMEM and returns. No TMA multicast is used.
 #include <cuda.h>
