@@ -39,6 +39,7 @@ WORKLOADS = {
     "train_small": {"case": "c3_2048_8192_k1638", "n": 1024, "dtype": "fp32"},
     "pythia410m": {"case": "c4_1024_4096_k512", "n": 8 * 512, "dtype": "bf16", "batch": 8, "prompt": 512,
                    "decode": 128},
+    "decode": {"case": "c4_1024_4096_k512", "n": 8, "dtype": "bf16", "layers": 24},
 }
 # DRAM bytes (read + write) per launch of the dominant kernel from one `ncu --set full` capture of the same workload
 # on a B200 (dram__bytes_read.sum + dram__bytes_write.sum); the command and the figures are in the named summary under
@@ -234,6 +235,8 @@ def gpu_arm(args, workload: dict) -> dict | None:
         return train_arm(args, workload, rank, world, local, device)
     if args.workload == "pythia410m":
         return pythia_arm(args, workload, rank, world, local, device)
+    if args.workload == "decode":
+        return decode_arm(args, workload, rank, world, local, device)
     case = synth.CASES[workload["case"]]
     n = workload["n"]
     dtype = torch.float32 if workload["dtype"] == "fp32" else torch.bfloat16
@@ -572,6 +575,125 @@ def train_arm(args, workload: dict, rank: int, world: int, local: int, device) -
         "gpu_launches": (10 if tc else 8) * args.steps, "device_errors": runtime.device_errors(),
         "clocks": clocks.summary(),
         "loss_last": float(loss_host),
+    }
+
+
+def decode_arm(args, workload: dict, rank: int, world: int, local: int, device) -> dict | None:
+    """The decode FFN step of the Pythia-410M shape: 24 layers (C4: d_model 1024, d_ff 4096, 50 % supports, bf16),
+    8 tokens per call, one call per layer, through ``PreparedRuntime`` (the decode path: prepared per (layer, N),
+    the cooperative kernels), the 24 calls of a step replayed as one CUDA graph. Every layer has its own copy of the
+    compact arrays in HBM (403 MB of edge streams per step, above L2: no flush needed). HBM-bound: the roofline is
+    the algorithmic bytes of the 48 kernels (edges, offsets, biases, x, act, y) per step over the step time. Replicas
+    only: with N > 1 every rank runs its own copy."""
+    import torch
+    import torch.distributed as dist
+
+    from hffn_b200 import synth
+    from hffn_b200.runtime import HFFNLayer, PreparedRuntime
+    from oracle import x86ref
+    case = synth.CASES[workload["case"]]
+    layers_n, n = workload["layers"], workload["n"]
+    layer = synth.make_layer(case)
+    t = torch.from_numpy
+    kl = HFFNLayer.from_hidden_major(layer.d_model, layer.d_ff, t(layer.b_up), t(layer.up_offsets), t(layer.up_idx),
+                                     t(layer.up_val), t(layer.b_down), t(layer.down_offsets), t(layer.down_idx),
+                                     t(layer.down_val))
+    runtime = PreparedRuntime([kl] * layers_n, device, torch.bfloat16)
+    d = case.d_model
+    x_host = torch.from_numpy(np.stack([rank_input(case, n, rank + 31 * k) for k in range(layers_n)])).to(
+        torch.bfloat16).pin_memory()
+    x = x_host.to(device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        for index in range(layers_n):
+            runtime.forward(index, x[index])
+
+    step()                                                   # prepares every (layer, N) entry outside the capture
+    up, down = runtime.modes(n)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        step()
+        with torch.cuda.graph(graph, stream=side):
+            step()
+    stream.wait_stream(side)
+    torch.cuda.synchronize(device)
+    for _ in range(args.warmup):
+        graph.replay()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        graph_ms = a.elapsed_time(b) / args.steps
+        a.record(stream)
+        for _ in range(args.steps):
+            step()
+        b.record(stream)
+        torch.cuda.synchronize(device)
+        eager_ms = a.elapsed_time(b) / args.steps
+    # end to end: the step's 24 inputs copied in from pinned host memory, the 24 outputs copied back, every step
+    y_host = torch.empty(layers_n, n, d, dtype=torch.bfloat16).pin_memory()
+    e2e = []
+    for k in range(args.warmup + args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        x.copy_(x_host, non_blocking=True)
+        for index in range(layers_n):
+            y_host[index].copy_(runtime.forward(index, x[index]), non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        if k >= args.warmup:
+            e2e.append(a.elapsed_time(b))
+    step_s, e2e_s = max_over_ranks(torch, [graph_ms / 1e3, sum(e2e) / len(e2e) / 1e3], world, device)
+    pk, pk_source = peaks()
+    alg = algorithmic(case, n, 2)
+    step_bytes = layers_n * (alg["up"]["bytes"] + alg["down"]["bytes"])
+    achieved = step_bytes / step_s / 1e9
+    errors = runtime.device_errors()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and x86ref.available():
+        threads = len(os.sched_getaffinity(0))
+        kernel = x86ref.X86Kernel(layer, threads=threads)
+        xs = x_host.float().numpy()
+        kernel.forward(xs[0])
+        steps, start = 0, time.perf_counter()
+        while time.perf_counter() - start < args.cpu_seconds:
+            for index in range(layers_n):
+                kernel.forward(xs[index])
+            steps += 1
+        elapsed = time.perf_counter() - start
+        cpu = {"value": steps * n * layers_n / elapsed, "unit": "layer-tokens/s", "cores": threads,
+               "kind": "reference", "sample": f"{steps} decode steps (24 calls of 8 tokens, float32: the reference "
+                                              f"kernel's only type), {elapsed:.1f} s"}
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    return {
+        "metric": "HFFN FFN layer tokens/s (decode, bf16)", "value": n * layers_n * world / step_s,
+        "unit": "layer-tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{case.name}: Pythia-410M FFN shape, {layers_n} layers x {n} tokens per decode step "
+                               f"(one call per layer, CUDA graph)", "modes": [up, down],
+                   "parallelism": "single" if world == 1 else f"replicas x{world}",
+                   "l2": f"inputs larger than L2 (edge streams {step_bytes / 1e6:.0f} MB per step)"},
+        "roofline": {"bound": "hbm", "kernel": f"whole decode step ({up} + {down}, {2 * layers_n} launches)",
+                     "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "traffic": None, "algorithmic_bytes": step_bytes, "peak_source": pk_source},
+        "eager_ms_per_step": eager_ms,
+        "e2e": {"value": n * layers_n * world / e2e_s, "unit": "layer-tokens/s",
+                "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 2},
+        "gpu_launches": 2 * layers_n * args.steps, "device_errors": errors, "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
     }
 
 
