@@ -10,6 +10,8 @@
 // from L2 without staging; here a CTA stages one token tile of x (up) or of act (down), transposed to
 // [feature][tile + 1] so that both the staging stores and the gathered loads are free of bank conflicts, and its
 // warps walk the compact index/value streams against it.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace hffn {
@@ -101,6 +103,138 @@ up_tile_kernel(const T* __restrict__ x, const int32_t* __restrict__ off, const i
   }
 }
 
+// Decode form of the cooperative mode (n <= 8 tokens, the decode calls): HBM-bound on the compact index and value
+// streams, so each lane streams 8 consecutive slots per load (16-byte index loads, 16- or 32-byte value loads) and
+// the rows it gathers come from shared memory (up: x staged as [feature][NT] floats, one or two vector reads per
+// slot) or from one vector load (down: the act row of a hidden neuron, n contiguous values). A row's slots before
+// its first multiple of 8 and after its last run one per lane. Each sum still has a fixed order (per lane: its head
+// slot, its tail slot, its chunks in order; then the xor tree; down: then the warps of the output in order).
+constexpr int kDecodeThreads = 256;
+constexpr int kDecodeWarps = kDecodeThreads / 32;
+constexpr int kDecodeSplit = 4;        // warps per output in the down kernel
+
+__device__ __forceinline__ void load_idx8(const int16_t* p, int (&i)[8]) {
+  const int4 raw = __ldg(reinterpret_cast<const int4*>(p));
+  const int words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    i[2 * k] = (int)(int16_t)(words[k] & 0xffff);
+    i[2 * k + 1] = (int)(int16_t)((uint32_t)words[k] >> 16);
+  }
+}
+
+__device__ __forceinline__ void load_val8(const float* p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p + 4));
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ void load_val8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v[2 * k] = __uint_as_float(words[k] << 16);
+    v[2 * k + 1] = __uint_as_float(words[k] & 0xffff0000u);
+  }
+}
+
+// NT floats of a shared-memory row (row start aligned to NT * 4 bytes).
+template <int NT>
+__device__ __forceinline__ void load_row_smem(const float* p, float (&r)[NT]) {
+  if constexpr (NT >= 4) {
+#pragma unroll
+    for (int k = 0; k < NT; k += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(p + k);
+      r[k] = a.x; r[k + 1] = a.y; r[k + 2] = a.z; r[k + 3] = a.w;
+    }
+  } else if constexpr (NT == 2) {
+    const float2 a = *reinterpret_cast<const float2*>(p);
+    r[0] = a.x; r[1] = a.y;
+  } else {
+    r[0] = *p;
+  }
+}
+
+// The n <= NT values of a global row (hidden-major act: row start aligned to n * sizeof(T) bytes); vector loads when
+// the row fills the tile (n == NT), else one load per value.
+template <typename T, int NT>
+__device__ __forceinline__ void load_row_global(const T* p, int n, float (&r)[NT]) {
+  if (n == NT) {
+    if constexpr (sizeof(T) == 4 && NT >= 4) {
+#pragma unroll
+      for (int k = 0; k < NT; k += 4) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p) + k / 4);
+        r[k] = a.x; r[k + 1] = a.y; r[k + 2] = a.z; r[k + 3] = a.w;
+      }
+      return;
+    } else if constexpr (sizeof(T) == 2 && NT == 8) {
+      float v[8];
+      load_val8(reinterpret_cast<const __nv_bfloat16*>(p), v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) r[k] = v[k];
+      return;
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) r[t] = t < n ? to_f(ldg(p + t)) : 0.f;
+}
+
+template <typename T, int NT, bool kStoreZ>
+__global__ void __launch_bounds__(kDecodeThreads)
+up_decode_kernel(const T* __restrict__ x, const int32_t* __restrict__ off, const int16_t* __restrict__ idx,
+                 const T* __restrict__ w, const T* __restrict__ b, T* __restrict__ act, float* __restrict__ z,
+                 int d, int H, int n) {
+  extern __shared__ __align__(16) float xs[];   // [d][NT], zero past n
+  for (int k = threadIdx.x; k < NT * d; k += kDecodeThreads) {
+    const int t = k / d, i = k - t * d;
+    xs[i * NT + t] = t < n ? to_f(x[(int64_t)t * d + i]) : 0.f;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int r = blockIdx.x * kDecodeWarps + warp; r < H; r += gridDim.x * kDecodeWarps) {
+    const int begin = off[r], end = off[r + 1];
+    const int body = min(end, (begin + 7) & ~7);
+    const int body_end = max(body, end & ~7);
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+    auto one = [&](int e) {
+      const float wv = to_f(w[e]);
+      float rv[NT];
+      load_row_smem<NT>(xs + (int)idx[e] * NT, rv);
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[t] += wv * rv[t];
+    };
+    if (begin + lane < body) one(begin + lane);
+    if (body_end + lane < end) one(body_end + lane);
+#pragma unroll 2
+    for (int c = body + 8 * lane; c < body_end; c += 256) {
+      int iv[8];
+      float wv[8];
+      load_idx8(idx + c, iv);
+      load_val8(w + c, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float rv[NT];
+        load_row_smem<NT>(xs + iv[j] * NT, rv);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] += wv[j] * rv[t];
+      }
+    }
+    const float bias = to_f(b[r]);
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const float sum = warp_sum(acc[t]);
+      if (lane == t && t < n) {
+        const float zz = bias + sum;
+        const int64_t at = (int64_t)r * n + t;
+        if (kStoreZ) z[at] = zz;
+        act[at] = from_f<T>(gelu(zz));
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // down
 
@@ -131,6 +265,67 @@ down_coop_kernel(const T* __restrict__ act, const int32_t* __restrict__ off, con
       const float s = warp_sum(acc[t]);
       if (lane == t && t < m) y[(int64_t)(t0 + t) * d + o] = from_f<T>(s + bo);
     }
+  }
+}
+
+// Decode form of the down projection: kDecodeSplit warps per output share its edges (chunks of 8 dealt round-robin
+// over the group's lanes), reduce them with the xor tree, and the output's first warp adds the warps' partial sums in
+// warp order, then the bias.
+template <typename T, int NT>
+__global__ void __launch_bounds__(kDecodeThreads)
+down_decode_kernel(const T* __restrict__ act, const int32_t* __restrict__ off, const int16_t* __restrict__ hid,
+                   const T* __restrict__ v, const T* __restrict__ bias, T* __restrict__ y, int d, int n) {
+  constexpr int kGroups = kDecodeWarps / kDecodeSplit;      // outputs per pass of a CTA
+  __shared__ float part[kDecodeWarps][NT];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int group = warp / kDecodeSplit, member = warp - group * kDecodeSplit;
+  const int glane = member * 32 + lane;
+  for (int o0 = blockIdx.x * kGroups; o0 < d; o0 += gridDim.x * kGroups) {   // uniform over the CTA
+    const int o = o0 + group;
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+    if (o < d) {
+      const int begin = off[o], end = off[o + 1];
+      const int body = min(end, (begin + 7) & ~7);
+      const int body_end = max(body, end & ~7);
+      auto one = [&](int q) {
+        const float vv = to_f(v[q]);
+        float rv[NT];
+        load_row_global<T, NT>(act + (int64_t)hid[q] * n, n, rv);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] += vv * rv[t];
+      };
+      if (begin + glane < body) one(begin + glane);
+      if (body_end + glane < end) one(body_end + glane);
+#pragma unroll 2
+      for (int c = body + 8 * glane; c < body_end; c += 8 * 32 * kDecodeSplit) {
+        int hv[8];
+        float vv[8];
+        load_idx8(hid + c, hv);
+        load_val8(v + c, vv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float rv[NT];
+          load_row_global<T, NT>(act + (int64_t)hv[j] * n, n, rv);
+#pragma unroll
+          for (int t = 0; t < NT; ++t) acc[t] += vv[j] * rv[t];
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const float sum = warp_sum(acc[t]);
+      if (lane == 0) part[warp][t] = sum;
+    }
+    __syncthreads();
+    if (o < d && member == 0 && lane < NT && lane < n) {
+      float sum = 0.f;
+#pragma unroll
+      for (int m = 0; m < kDecodeSplit; ++m) sum += part[group * kDecodeSplit + m][lane];
+      y[(int64_t)lane * d + o] = from_f<T>(sum + to_f(bias[o]));
+    }
+    __syncthreads();
   }
 }
 
@@ -196,9 +391,25 @@ static int units_per_cta(int units, int64_t tiles, int per_pass) {
 
 bool up_fits(int64_t d) { return d * 2 * 4 <= kSmemBudget; }
 
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 template <typename T, bool kZ>
 static int launch_up_t(int mode, const T* x, const int32_t* off, const int16_t* idx, const T* w, const T* b, T* act,
                        float* z, int d, int H, int64_t n, cudaStream_t s) {
+  if (mode == HFFN_UP_COOP && n <= 8 && aligned16(idx) && aligned16(w) && (int64_t)d * 8 * 4 <= kSmemBudget) {
+    const int nn = (int)n;
+    const int grid = (int)std::min<int64_t>(ceil_div(H, kDecodeWarps), 3 * 148);
+    auto run = [&](auto kernel, int nt) {
+      const size_t smem = (size_t)d * nt * 4;
+      if (smem > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      kernel<<<grid, kDecodeThreads, smem, s>>>(x, off, idx, w, b, act, z, d, H, nn);
+    };
+    if (n <= 1) run(up_decode_kernel<T, 1, kZ>, 1);
+    else if (n <= 2) run(up_decode_kernel<T, 2, kZ>, 2);
+    else if (n <= 4) run(up_decode_kernel<T, 4, kZ>, 4);
+    else run(up_decode_kernel<T, 8, kZ>, 8);
+    return launch_status("up_decode");
+  }
   if (mode == HFFN_UP_COOP) {
     dim3 grid((unsigned)ceil_div(H, kCoopThreads / 32));
     const int nn = (int)n;
@@ -238,6 +449,14 @@ template <typename T>
 static int launch_down_t(int mode, const T* act, const int32_t* off, const int16_t* hid, const T* v, const T* bias,
                          T* y, int d, int H, int64_t n, cudaStream_t s) {
   const int nn = (int)n;
+  if (mode == HFFN_DOWN_COOP && n <= 8 && aligned16(hid) && aligned16(v) && aligned16(act)) {
+    const int grid = (int)std::min<int64_t>(ceil_div(d, kDecodeWarps / kDecodeSplit), 4 * 148);
+    if (n <= 1) down_decode_kernel<T, 1><<<grid, kDecodeThreads, 0, s>>>(act, off, hid, v, bias, y, d, nn);
+    else if (n <= 2) down_decode_kernel<T, 2><<<grid, kDecodeThreads, 0, s>>>(act, off, hid, v, bias, y, d, nn);
+    else if (n <= 4) down_decode_kernel<T, 4><<<grid, kDecodeThreads, 0, s>>>(act, off, hid, v, bias, y, d, nn);
+    else down_decode_kernel<T, 8><<<grid, kDecodeThreads, 0, s>>>(act, off, hid, v, bias, y, d, nn);
+    return launch_status("down_decode");
+  }
   if (mode == HFFN_DOWN_COOP) {
     dim3 grid((unsigned)ceil_div(d, kCoopThreads / 32));
     if (n <= 1) down_coop_kernel<T, 1><<<grid, kCoopThreads, 0, s>>>(act, off, hid, v, bias, y, d, nn);
