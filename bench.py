@@ -1,15 +1,22 @@
 """Benchmark of the HFFN sparse FFN hot path on B200: one JSON line on rank 0.
 
 Default workload (``--workload fwd``): the Pythia-410M-shape synthetic HFFN layer of the benchmark plan, d_model 1024,
-d_ff 4096, 512-of-1024 supports per neuron (50 %), N = 4096 tokens per step, float32. A step is one forward of the
-layer over one batch: the up kernel (+ bias + GELU) then the down kernel, launched through the C ABI on inputs
-resident in HBM. ``--workload fwd_bf16`` runs the same in bfloat16 storage; ``--workload train`` the training step
-(d_model 2048, d_ff 8192, 80 %, N = 8192, MSE loss, fused backward + AdamW).
+d_ff 4096, 512-of-1024 supports per neuron (50 %), N = 4096 tokens per GPU per step, float32. A step is one forward
+of the layer over one batch: the up kernel (+ bias + GELU) then the down kernel, launched through the C ABI on inputs
+resident in HBM (the tensor-core pair by the runtime's policy; ``--path cuda_cores`` forces the gather kernels).
+Other workloads: ``fwd_bf16`` (the same in bfloat16 storage); ``train`` (the training step: d_model 2048, d_ff 8192,
+80 %, N = 8192, MSE loss, backward and AdamW); ``decode`` (24 Pythia-410M-shape FFN layers x 8 tokens per step,
+the prepared decode path in a CUDA graph, HBM roofline); ``pythia410m`` (the model: prefill and greedy decode, HFFN
+arm and dense arm).
 
 Timing: W warm-up steps, then exactly K timed steps bracketed by a barrier and a device synchronisation; every step
 is timed with CUDA events on the launching stream and the L2 is flushed (a 512 MiB write) between steps, outside the
-events. Multi-GPU (torchrun, one process per GPU): each rank runs its own replica of the layer on its own batch
-(weak scaling, no collective on the data path); the time is the max over ranks.
+events (workloads whose per-step inputs exceed L2 say so instead). ``e2e``: the same metric through the public API
+with host batches in pinned memory, copied in and the outputs copied back every step (``HostPipeline`` overlaps the
+copies with the kernels). Multi-GPU (torchrun, one process per GPU): the forward is neuron-sharded (each rank holds a
+slice of the hidden neurons and sends every rank's batch through it: NCCL all-gather / reduce-scatter, or
+``--transport peer`` for the NVLink peer-memory pipeline); training is data-parallel with a gradient all-reduce;
+``decode`` runs replicas. Weak scaling: each rank brings its own batch; the time is the max over ranks.
 
 ``--impl reference`` times the reference's own x86 AVX2 kernel (compiled from the reference sources into
 ``oracle/_ref``) on this host's cores, on the same workload (rank 0 only).
