@@ -179,47 +179,16 @@ __device__ __forceinline__ void load_row_global(const T* p, int n, float (&r)[NT
   for (int t = 0; t < NT; ++t) r[t] = t < n ? to_f(ldg(p + t)) : 0.f;
 }
 
-// Four consecutive values of x (16-byte aligned for float32, 8-byte for bfloat16) as floats.
-__device__ __forceinline__ void load_x4(const float* p, float (&v)[4]) {
-  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-}
-
-__device__ __forceinline__ void load_x4(const __nv_bfloat16* p, float (&v)[4]) {
-  const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
-  v[0] = __uint_as_float(raw.x << 16); v[1] = __uint_as_float(raw.x & 0xffff0000u);
-  v[2] = __uint_as_float(raw.y << 16); v[3] = __uint_as_float(raw.y & 0xffff0000u);
-}
-
-// x [n, d] token-major staged as xs [d][NT] floats, zero past n. kVec: d % 4 == 0 and x 16-byte aligned: four values
-// per load, the loads of a thread unrolled so that they are in flight together.
-template <typename T, int NT, bool kVec>
-__device__ __forceinline__ void stage_x(const T* __restrict__ x, float* xs, int d, int n) {
-  if constexpr (kVec) {
-    const int chunks = NT * d / 4;
-#pragma unroll 8
-    for (int k = threadIdx.x; k < chunks; k += kDecodeThreads) {
-      const int t = (4 * k) / d, i = 4 * k - t * d;
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
-      if (t < n) load_x4(x + (int64_t)t * d + i, v);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) xs[(i + j) * NT + t] = v[j];
-    }
-  } else {
-    for (int k = threadIdx.x; k < NT * d; k += kDecodeThreads) {
-      const int t = k / d, i = k - t * d;
-      xs[i * NT + t] = t < n ? to_f(x[(int64_t)t * d + i]) : 0.f;
-    }
-  }
-}
-
-template <typename T, int NT, bool kStoreZ, bool kVec>
+template <typename T, int NT, bool kStoreZ>
 __global__ void __launch_bounds__(kDecodeThreads)
 up_decode_kernel(const T* __restrict__ x, const int32_t* __restrict__ off, const int16_t* __restrict__ idx,
                  const T* __restrict__ w, const T* __restrict__ b, T* __restrict__ act, float* __restrict__ z,
                  int d, int H, int n) {
   extern __shared__ __align__(16) float xs[];   // [d][NT], zero past n
-  stage_x<T, NT, kVec>(x, xs, d, n);
+  for (int k = threadIdx.x; k < NT * d; k += kDecodeThreads) {
+    const int t = k / d, i = k - t * d;
+    xs[i * NT + t] = t < n ? to_f(x[(int64_t)t * d + i]) : 0.f;
+  }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int r = blockIdx.x * kDecodeWarps + warp; r < H; r += gridDim.x * kDecodeWarps) {
@@ -435,17 +404,10 @@ static int launch_up_t(int mode, const T* x, const int32_t* off, const int16_t* 
       if (smem > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       kernel<<<grid, kDecodeThreads, smem, s>>>(x, off, idx, w, b, act, z, d, H, nn);
     };
-    if (d % 4 == 0 && aligned16(x)) {
-      if (n <= 1) run(up_decode_kernel<T, 1, kZ, true>, 1);
-      else if (n <= 2) run(up_decode_kernel<T, 2, kZ, true>, 2);
-      else if (n <= 4) run(up_decode_kernel<T, 4, kZ, true>, 4);
-      else run(up_decode_kernel<T, 8, kZ, true>, 8);
-    } else {
-      if (n <= 1) run(up_decode_kernel<T, 1, kZ, false>, 1);
-      else if (n <= 2) run(up_decode_kernel<T, 2, kZ, false>, 2);
-      else if (n <= 4) run(up_decode_kernel<T, 4, kZ, false>, 4);
-      else run(up_decode_kernel<T, 8, kZ, false>, 8);
-    }
+    if (n <= 1) run(up_decode_kernel<T, 1, kZ>, 1);
+    else if (n <= 2) run(up_decode_kernel<T, 2, kZ>, 2);
+    else if (n <= 4) run(up_decode_kernel<T, 4, kZ>, 4);
+    else run(up_decode_kernel<T, 8, kZ>, 8);
     return launch_status("up_decode");
   }
   if (mode == HFFN_UP_COOP) {
