@@ -646,6 +646,26 @@ def decode_arm(args, workload: dict, rank: int, world: int, local: int, device) 
         b.record(stream)
         torch.cuda.synchronize(device)
         eager_ms = a.elapsed_time(b) / args.steps
+    # the two kernels of a layer apart: every layer's up kernel, then every layer's down kernel, eager launches
+    from hffn_b200 import _native as native
+    handle = stream.cuda_stream
+    act = runtime._act.data_ptr()
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    marks[0].record(stream)
+    for index in range(layers_n):
+        st = runtime._structs[index]
+        native.check(native.lib.hffn_up(runtime._code, native.UP_CODES[up], x[index].data_ptr(), st.up_offsets,
+                                        st.up_idx, st.up_val, st.b_up, act, None, d, case.d_ff, n, handle), "hffn_up")
+    marks[1].record(stream)
+    for index in range(layers_n):
+        st = runtime._structs[index]
+        native.check(native.lib.hffn_down(runtime._code, native.DOWN_CODES[down], act, st.out_offsets, st.out_hidden,
+                                          st.out_val, st.b_down, runtime._y.data_ptr(), d, case.d_ff, n, handle),
+                     "hffn_down")
+    marks[2].record(stream)
+    torch.cuda.synchronize(device)
+    kernel_us = {"up": 1e3 * marks[0].elapsed_time(marks[1]) / layers_n,
+                 "down": 1e3 * marks[1].elapsed_time(marks[2]) / layers_n}
     # end to end: the step's 24 inputs copied in from pinned host memory, the 24 outputs copied back, every step
     y_host = torch.empty(layers_n, n, d, dtype=torch.bfloat16).pin_memory()
     e2e = []
@@ -697,6 +717,7 @@ def decode_arm(args, workload: dict, rank: int, world: int, local: int, device) 
                      "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                      "traffic": None, "algorithmic_bytes": step_bytes, "peak_source": pk_source},
         "eager_ms_per_step": eager_ms,
+        "kernel_us_eager": kernel_us,
         "e2e": {"value": n * layers_n * world / e2e_s, "unit": "layer-tokens/s",
                 "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 2},
         "gpu_launches": 2 * layers_n * args.steps, "device_errors": errors, "clocks": clocks.summary(),
