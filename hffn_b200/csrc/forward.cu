@@ -398,7 +398,8 @@ static int launch_up_t(int mode, const T* x, const int32_t* off, const int16_t* 
                        float* z, int d, int H, int64_t n, cudaStream_t s) {
   if (mode == HFFN_UP_COOP && n <= 8 && aligned16(idx) && aligned16(w) && (int64_t)d * 8 * 4 <= kSmemBudget) {
     const int nn = (int)n;
-    const int grid = (int)std::min<int64_t>(ceil_div(H, kDecodeWarps), 3 * 148);
+    // one neuron per warp, every CTA resident at once (x staged in <= 64 KB per CTA for the decode shapes)
+    const int grid = (int)std::min<int64_t>(ceil_div(H, kDecodeWarps), 8 * 148);
     auto run = [&](auto kernel, int nt) {
       const size_t smem = (size_t)d * nt * 4;
       if (smem > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
