@@ -185,9 +185,22 @@ up_decode_kernel(const T* __restrict__ x, const int32_t* __restrict__ off, const
                  const T* __restrict__ w, const T* __restrict__ b, T* __restrict__ act, float* __restrict__ z,
                  int d, int H, int n) {
   extern __shared__ __align__(16) float xs[];   // [d][NT], zero past n
-  for (int k = threadIdx.x; k < NT * d; k += kDecodeThreads) {
-    const int t = k / d, i = k - t * d;
-    xs[i * NT + t] = t < n ? to_f(x[(int64_t)t * d + i]) : 0.f;
+  // staged in batches of 8 elements per thread: the 8 loads first (in flight together), then the 8 stores
+  const int total = NT * d;
+  for (int k0 = 0; k0 < total; k0 += 8 * kDecodeThreads) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int k = k0 + u * kDecodeThreads + (int)threadIdx.x;
+      const int t = k / d, i = k - t * d;
+      v[u] = k < total && t < n ? to_f(x[(int64_t)t * d + i]) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int k = k0 + u * kDecodeThreads + (int)threadIdx.x;
+      const int t = k / d, i = k - t * d;
+      if (k < total) xs[i * NT + t] = v[u];
+    }
   }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
