@@ -155,6 +155,31 @@ __device__ __forceinline__ void load_row_smem(const float* p, float (&r)[NT]) {
   }
 }
 
+// The same for a row staged in bfloat16 (the bf16 runtimes: x is bf16, so staging it as is loses nothing): 16-byte
+// rows at NT = 8, one load per slot, consecutive rows in distinct bank groups. Element k is the low half of its
+// 32-bit word; the conversion is exact.
+template <int NT>
+__device__ __forceinline__ void load_row_smem(const __nv_bfloat16* p, float (&r)[NT]) {
+  if constexpr (NT == 8) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      r[2 * k] = __uint_as_float(words[k] << 16);
+      r[2 * k + 1] = __uint_as_float(words[k] & 0xffff0000u);
+    }
+  } else if constexpr (NT == 4) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(p);
+    r[0] = __uint_as_float(raw.x << 16); r[1] = __uint_as_float(raw.x & 0xffff0000u);
+    r[2] = __uint_as_float(raw.y << 16); r[3] = __uint_as_float(raw.y & 0xffff0000u);
+  } else if constexpr (NT == 2) {
+    const uint32_t raw = *reinterpret_cast<const uint32_t*>(p);
+    r[0] = __uint_as_float(raw << 16); r[1] = __uint_as_float(raw & 0xffff0000u);
+  } else {
+    r[0] = __bfloat162float(*p);
+  }
+}
+
 // The n <= NT values of a global row (hidden-major act: row start aligned to n * sizeof(T) bytes); vector loads when
 // the row fills the tile (n == NT), else one load per value.
 template <typename T, int NT>
@@ -184,16 +209,17 @@ __global__ void __launch_bounds__(kDecodeThreads)
 up_decode_kernel(const T* __restrict__ x, const int32_t* __restrict__ off, const int16_t* __restrict__ idx,
                  const T* __restrict__ w, const T* __restrict__ b, T* __restrict__ act, float* __restrict__ z,
                  int d, int H, int n) {
-  extern __shared__ __align__(16) float xs[];   // [d][NT], zero past n
+  extern __shared__ __align__(16) unsigned char xs_raw[];
+  T* xs = reinterpret_cast<T*>(xs_raw);       // [d][NT] in the storage type, zero past n
   // staged in batches of 8 elements per thread: the 8 loads first (in flight together), then the 8 stores
   const int total = NT * d;
   for (int k0 = 0; k0 < total; k0 += 8 * kDecodeThreads) {
-    float v[8];
+    T v[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int k = k0 + u * kDecodeThreads + (int)threadIdx.x;
       const int t = k / d, i = k - t * d;
-      v[u] = k < total && t < n ? to_f(x[(int64_t)t * d + i]) : 0.f;
+      v[u] = k < total && t < n ? x[(int64_t)t * d + i] : from_f<T>(0.f);
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -414,7 +440,7 @@ static int launch_up_t(int mode, const T* x, const int32_t* off, const int16_t* 
     // one neuron per warp, every CTA resident at once (x staged in <= 64 KB per CTA for the decode shapes)
     const int grid = (int)std::min<int64_t>(ceil_div(H, kDecodeWarps), 8 * 148);
     auto run = [&](auto kernel, int nt) {
-      const size_t smem = (size_t)d * nt * 4;
+      const size_t smem = (size_t)d * nt * sizeof(T);
       if (smem > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       kernel<<<grid, kDecodeThreads, smem, s>>>(x, off, idx, w, b, act, z, d, H, nn);
     };

@@ -159,3 +159,27 @@ def test_prepared_runtime_and_cuda_graph():
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(y_graph, plain.forward(0, x2))
+
+
+@pytest.mark.parametrize("name", ["irreg_512_2048", "homog_512_2048"])
+def test_bf16_decode_sizes(name):
+    """bfloat16 runtimes at the decode sizes (the cooperative kernels, n <= 8, irregular row starts included): within
+    the bf16 bar of the oracle on the layer and input the runtime holds (values rounded to bf16), same bits on
+    repeat."""
+    import dataclasses
+    case = synth.TEST_CASES[name]
+    layer = synth.make_layer(case)
+    r = lambda a: torch.from_numpy(a).to(torch.bfloat16).float().numpy()  # noqa: E731
+    held = dataclasses.replace(layer, up_val=r(layer.up_val), b_up=r(layer.b_up), down_val=r(layer.down_val),
+                               b_down=r(layer.b_down))
+    runtime = runtime_for(layer, torch.bfloat16, None)
+    runtime.force("coop", "coop")
+    for n in (1, 2, 3, 4, 5, 7, 8):
+        x = torch.from_numpy(synth.make_input(case, n)).to(torch.bfloat16)
+        first = runtime.forward(0, x.cuda()).clone()
+        assert torch.equal(first, runtime.forward(0, x.cuda())), n
+        expected = forward64.forward(held, x.float().numpy())
+        y = first.float().cpu().numpy()
+        relative = np.max(np.abs(y - expected) / np.maximum(1.0, np.abs(expected)))
+        assert relative <= BF16_TOLERANCE, (n, relative)
+    assert runtime.device_errors() == 0
