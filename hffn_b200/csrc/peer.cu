@@ -86,6 +86,7 @@ struct PeerPipeline {
   int device;
   int64_t elem;
   uint32_t epoch = 0;
+  bool failed = false;     // a run stopped part-way: the ranks' barrier epochs may differ, the pipeline is unusable
   cudaStream_t pull[kMaxWorld] = {}, push[kMaxWorld] = {};
   cudaEvent_t pulled[2][kMaxWorld] = {}, delivered[3][kMaxWorld] = {};
   cudaEvent_t barrier_done = nullptr, computed = nullptr;
@@ -261,8 +262,20 @@ int hffn_peer_pipeline_run(void* handle, const void* const* xs, void* const* out
   HFFN_REQUIRE(handle != nullptr, "null pipeline");
   HFFN_REQUIRE(count >= 0 && (count == 0 || (xs && outs)), "batches");
   for (int k = 0; k < count; ++k) HFFN_REQUIRE(xs[k] && outs[k], "batch %d: null pointer", k);
+  PeerPipeline* p = static_cast<PeerPipeline*>(handle);
+  if (p->failed) {
+    set_error("peer pipeline: an earlier run failed part-way (the ranks' barriers are out of step); recreate it");
+    return HFFN_ERR_CUDA;
+  }
   HFFN_TRY(bind_stream_device(stream));
-  return static_cast<PeerPipeline*>(handle)->run(xs, outs, count, static_cast<cudaStream_t>(stream));
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess || device != p->device) {
+    set_error("peer pipeline: created on device %d, run on a stream of device %d", p->device, device);
+    return HFFN_ERR_ARGUMENT;
+  }
+  const int status = p->run(xs, outs, count, static_cast<cudaStream_t>(stream));
+  if (status != HFFN_OK) p->failed = true;
+  return status;
 }
 
 int hffn_peer_pipeline_destroy(void* handle) {

@@ -219,8 +219,10 @@ int hffn_peer_pipeline_create(const hffn_peer_config* config, const hffn_layer* 
                               int32_t* err, void** pipeline);
 
 /* outs[k] [n, d] = the layer's output for this rank's batch xs[k] [n, d], k < count; every rank calls with the same
- * count. Iteration k stages batch k, waits for the pulls of batch k - 1 and the deliveries of batch k - 3, passes the
- * barrier, pulls batch k, runs the shard over batch k - 1, delivers its partials and sums batch k - 3. */
+ * count, on a stream of the pipeline's device. Iteration k stages batch k, waits for the pulls of batch k - 1 and the
+ * deliveries of batch k - 3, passes the barrier, pulls batch k, runs the shard over batch k - 1, delivers its
+ * partials and sums batch k - 3. A run that fails part-way leaves the pipeline unusable (its later runs are refused:
+ * the ranks' barriers may be out of step); destroy it and create a new one on every rank. */
 int hffn_peer_pipeline_run(void* pipeline, const void* const* xs, void* const* outs, int32_t count, void* stream);
 
 int hffn_peer_pipeline_destroy(void* pipeline);
