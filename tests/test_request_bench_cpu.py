@@ -49,3 +49,46 @@ def test_share_non_ffn_keeps_only_the_ffns_distinct():
     ids = torch.randint(0, 128, (1, 9))
     with torch.no_grad():
         assert torch.equal(target(input_ids=ids).logits, source(input_ids=ids).logits)
+
+
+class _Worker:
+    """Stands in for the fresh worker process of a cell: one JSON row per call, gate held or not."""
+
+    def __init__(self, gate_fails_at=None):
+        self.calls, self.gate_fails_at = [], gate_fails_at
+
+    def __call__(self, command, text, capture_output, cwd):
+        import json
+        import types
+        job = json.loads(command[command.index("--worker") + 1])
+        self.calls.append(job)
+        passed = len(self.calls) != self.gate_fails_at
+        row = {**{k: v for k, v in job.items() if k != "assets"}, "repeats": 3, "bitwise_copy": passed,
+               "hffn_vs_dense_relative_gap": 1e-6, "gate_passed": passed,
+               "samples_ms": {"hffn": [1.0, 1.0], "dense": [2.0, 2.0], "hffn_copy": [1.01, 1.01]}}
+        return types.SimpleNamespace(returncode=0 if passed else 4, stdout=json.dumps(row) + "\n", stderr="")
+
+
+def test_orchestrate_runs_every_cell_in_alternating_order(tmp_path, monkeypatch):
+    import json
+    worker = _Worker()
+    monkeypatch.setattr(rb.subprocess, "run", worker)
+    grid = {"sizes": (70,), "densities": (20, 50), "shapes": ("prefill_b1", "decode_b1"), "sessions": 2, "blocks": 1,
+            "window_ms": 10.0}
+    assert rb.orchestrate("smoke", tmp_path / "assets", tmp_path / "run", grid=grid) == 0
+    cells = [(c["density"], c["shape"]) for c in worker.calls]
+    assert len(cells) == 8 and cells[4:] == cells[:4][::-1]          # the second session runs in reverse order
+    summary = json.loads((tmp_path / "run" / "summary.json").read_text())
+    assert summary["verdict"]["admissible"] and len(summary["cells"]) == 4
+    assert all(c["hffn_over_dense"] == pytest.approx(0.5) for c in summary["cells"])
+    assert (tmp_path / "run" / "REPORT.md").read_text().count("| 70M |") == 4
+
+
+def test_orchestrate_stops_at_a_failed_gate(tmp_path, monkeypatch):
+    import json
+    monkeypatch.setattr(rb.subprocess, "run", _Worker(gate_fails_at=2))
+    grid = {"sizes": (70,), "densities": (20,), "shapes": ("prefill_b1", "decode_b1"), "sessions": 1, "blocks": 1,
+            "window_ms": 10.0}
+    assert rb.orchestrate("smoke", tmp_path / "assets", tmp_path / "run", grid=grid) == 1
+    summary = json.loads((tmp_path / "run" / "summary.json").read_text())
+    assert summary["failure"]["returncode"] == 4 and not summary["verdict"]["admissible"]
