@@ -46,6 +46,41 @@ class HFFNMLP(nn.Module):
         return self.runtime.forward(self.index, hidden_states.reshape(-1, shape[-1]).contiguous()).view(shape)
 
 
+class ShardedHFFNMLP(nn.Module):
+    """``block.mlp`` of a neuron-sharded model (one process per GPU, every rank running the same tokens through the
+    rest of the model): this rank's shard of the FFN's hidden neurons (``b_down`` on rank 0 only), its partial output
+    all-reduced (sum) over ``group``. The output is a view of the runtime's output buffer, consumed by the block
+    before the next FFN call overwrites it."""
+
+    def __init__(self, runtime, index: int, group) -> None:
+        super().__init__()
+        self.runtime, self.index, self.group = runtime, index, group
+
+    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        import torch.distributed as dist
+        shape = hidden_states.shape
+        y = self.runtime.forward(self.index, hidden_states.reshape(-1, shape[-1]).contiguous())
+        dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
+        return y.view(shape)
+
+
+def shard_layers(layers: list[dict], rank: int, world: int) -> list[dict]:
+    """This rank's neuron shard of every export layer (hidden ranges balanced by edge count, multiples of 8; down
+    edges restricted to the shard; ``b_down`` kept on rank 0 only): canonical hidden-major arrays."""
+    from .distributed import neuron_partition, shard_hidden_major
+    shards = []
+    for layer in layers:
+        arrays = {"b_up": layer["b_up"], "up_offsets": layer["up_row_offsets"], "up_idx": layer["up_idx"],
+                  "up_val": layer["up_val"], "b_down": layer["b_down"], "down_offsets": layer["down_row_offsets"],
+                  "down_idx": layer["down_idx"], "down_val": layer["down_val"]}
+        bounds = neuron_partition(arrays, world)
+        if bounds[rank + 1] <= bounds[rank]:
+            raise ValueError(f"rank {rank} owns no hidden neuron of a layer (d_ff {layer['d_ff']}, {world} ranks)")
+        shards.append(shard_hidden_major(layer["d_model"], arrays, bounds[rank], bounds[rank + 1],
+                                         with_bias=rank == 0))
+    return shards
+
+
 class _NoFFN(nn.Module):
     """Parameterless stand-in for ``GPTNeoXMLP`` while the HFFN arm is built: no dense FFN is allocated."""
 
@@ -91,8 +126,12 @@ def _load_non_ffn(model: nn.Module, checkpoint: Path) -> None:
 
 
 def load_pythia(model_dir: str | Path, export_dir: str | Path, ffn: str, device: str | torch.device = "cuda",
-                dtype: torch.dtype = torch.float32, tensor_cores: bool | None = None) -> nn.Module:
-    """Pythia in eval mode (``dtype``, on ``device``) with its FFNs from ``export_dir``, executed dense or by HFFN."""
+                dtype: torch.dtype = torch.float32, tensor_cores: bool | None = None, group=None) -> nn.Module:
+    """Pythia in eval mode (``dtype``, on ``device``) with its FFNs from ``export_dir``, executed dense or by HFFN.
+
+    ``group`` (a process group of more than one rank, HFFN arm): every FFN neuron-sharded over the group's ranks
+    (``ShardedHFFNMLP``), the rest of the model replicated; every rank runs the same tokens and gets the whole
+    model's output. ``model.hffn_runtimes`` holds the rank's runtimes (one per distinct shard width)."""
     from transformers import AutoConfig, AutoModelForCausalLM
     if ffn not in ("dense", "hffn"):
         raise ValueError("ffn must be 'dense' or 'hffn'")
@@ -111,15 +150,42 @@ def load_pythia(model_dir: str | Path, export_dir: str | Path, ffn: str, device:
     if ffn == "dense":
         for block, layer in zip(blocks, layers):
             set_dense_mlp(block.mlp, layer)
-    else:
+    elif group is None or _world(group) == 1:
         from .runtime import PreparedRuntime
         runtime = PreparedRuntime([export.kernel_layer(layer) for layer in layers], device, dtype,
                                   tensor_cores=tensor_cores)
         for index, block in enumerate(blocks):
             block.mlp = HFFNMLP(runtime, index)
+    else:
+        import torch.distributed as dist
+
+        from .runtime import HFFNLayer, PreparedRuntime
+        shards = shard_layers(layers, dist.get_rank(group), dist.get_world_size(group))
+        by_width: dict = {}
+        for index, shard in enumerate(shards):
+            by_width.setdefault(shard["d_ff"], []).append(index)
+        runtimes = []
+        for width, indices in by_width.items():
+            kls = [HFFNLayer.from_hidden_major(shards[i]["d_model"], width, shards[i]["b_up"], shards[i]["up_offsets"],
+                                               shards[i]["up_idx"], shards[i]["up_val"], shards[i]["b_down"],
+                                               shards[i]["down_offsets"], shards[i]["down_idx"], shards[i]["down_val"])
+                   for i in indices]
+            shard_runtime = PreparedRuntime(kls, device, dtype, tensor_cores=tensor_cores)
+            runtimes.append(shard_runtime)
+            for local, index in enumerate(indices):
+                blocks[index].mlp = ShardedHFFNMLP(shard_runtime, local, group)
+        runtime = runtimes[0]
+        model.hffn_runtimes = runtimes
     model = model.to(device=device, dtype=dtype).eval().requires_grad_(False)
     model.hffn_runtime = runtime
+    if runtime is not None and not hasattr(model, "hffn_runtimes"):
+        model.hffn_runtimes = [runtime]
     return model
+
+
+def _world(group) -> int:
+    import torch.distributed as dist
+    return dist.get_world_size(group)
 
 
 def make_random_pythia(model_dir: str | Path, export_dir: str | Path, architecture: dict, support: int,

@@ -108,3 +108,56 @@ def test_peer_forward_requires_tensor_cores_and_checks_push():
         PeerShardedFFN(types.SimpleNamespace(tensor_cores=False), 64)
     with pytest.raises(ValueError):
         PeerShardedFFN(types.SimpleNamespace(tensor_cores=True), 64, push="broadcast")
+
+
+def test_pythia_shard_layers_partition_every_ffn():
+    """``pythia.shard_layers``: the ranks' shards of every export layer hold its hidden neurons once each, in order,
+    with their own up slots and down edges, and b_down on rank 0 only."""
+    from hffn_b200 import export, pythia
+    layers = [export.from_compact(synth.make_layer(synth.TEST_CASES[name]))
+              for name in ("irreg_512_2048", "homog_512_2048")]
+    world = 4
+    shards = [pythia.shard_layers(layers, rank, world) for rank in range(world)]
+    for index, layer in enumerate(layers):
+        parts = [shards[rank][index] for rank in range(world)]
+        assert sum(p["d_ff"] for p in parts) == layer["d_ff"]
+        assert torch.equal(torch.cat([p["b_up"] for p in parts]), layer["b_up"])
+        assert torch.equal(torch.cat([p["up_val"] for p in parts]), layer["up_val"])
+        assert torch.equal(torch.cat([p["up_idx"] for p in parts]), layer["up_idx"])
+        assert sum(int(p["down_val"].numel()) for p in parts) == layer["down_val"].numel()
+        assert torch.equal(parts[0]["b_down"], layer["b_down"])
+        assert all(not p["b_down"].any() for p in parts[1:])
+
+
+def _mlp_worker(rank: int, world: int, port: int, results) -> None:
+    import torch.distributed as dist
+
+    from hffn_b200.pythia import ShardedHFFNMLP
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        class Partial:                      # stands in for the rank's shard runtime: partial output = (rank + 1) x
+            def forward(self, index, x):
+                return x * (rank + 1) + index
+
+        mlp = ShardedHFFNMLP(Partial(), 2, None)
+        h = torch.arange(24, dtype=torch.float32).view(2, 3, 4)
+        results[rank] = mlp(h)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_mlp_all_reduces_the_partials():
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_mlp_worker, args=(rank, 2, port, results)) for rank in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs)
+    h = torch.arange(24, dtype=torch.float32).view(2, 3, 4)
+    for rank in range(2):
+        assert torch.equal(results[rank], h * 3 + 4)
