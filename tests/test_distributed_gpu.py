@@ -129,3 +129,62 @@ def test_ranks(world):
         assert r["errors_tc1"] == 0 and r["errors_tc0"] == 0, r
         assert r["sharded_peer"] <= 1e-5 and r["errors_peer"] == 0, r
         assert r["dp_param_rel"] <= 1e-5 and r["dp_loss_rel"] <= 1e-5, r
+
+
+def _pythia_worker(rank: int, world: int, port: int, root: str, results) -> None:
+    import datetime
+
+    import torch.distributed as dist
+
+    from hffn_b200 import pythia
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=device,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        sharded = pythia.load_pythia(f"{root}/model", f"{root}/export", "hffn", device, group=dist.group.WORLD)
+        single = pythia.load_pythia(f"{root}/model", f"{root}/export", "hffn", device)
+        ids = torch.randint(0, 2048, (2, 300), generator=torch.Generator().manual_seed(5)).to(device)
+        with torch.no_grad():
+            a = sharded(input_ids=ids, use_cache=True)
+            b = single(input_ids=ids, use_cache=True)
+            nxt = b.logits[:, -1:].argmax(-1)
+            a2 = sharded(input_ids=nxt, past_key_values=a.past_key_values, use_cache=True)
+            b2 = single(input_ids=nxt, past_key_values=b.past_key_values, use_cache=True)
+        results[rank] = {
+            "prefill": float((a.logits - b.logits).abs().max() / b.logits.abs().max()),
+            "decode": float((a2.logits - b2.logits).abs().max() / b2.logits.abs().max()),
+            "errors": sum(r.device_errors() for r in sharded.hffn_runtimes)}
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_pythia_with_sharded_ffns(world, tmp_path):
+    """Every FFN of a small random-init GPT-NeoX neuron-sharded over the ranks (``load_pythia(group=...)``): the
+    logits of a 300-token prefill (tensor cores) and of one cached decode step (decode kernels) equal the single-GPU
+    HFFN model's within 1e-4 of max|logit| (the partial outputs are summed in another order)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from hffn_b200 import pythia
+    small = dict(pythia.PYTHIA_410M, hidden_size=256, num_hidden_layers=4, num_attention_heads=4,
+                 intermediate_size=1024, vocab_size=2048)
+    pythia.make_random_pythia(tmp_path / "model", tmp_path / "export", small, support=128, seed=11)
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    results = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_pythia_worker, args=(rank, world, port, str(tmp_path), results))
+             for rank in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for rank in range(world):
+        r = results[rank]
+        assert r["prefill"] <= 1e-4 and r["decode"] <= 1e-4 and r["errors"] == 0, r
