@@ -58,7 +58,7 @@ const char* last_error() { return g_error; }
 constexpr int64_t kMaxTokens = int64_t(1) << 30;
 constexpr int kCoopMaxTokens = 8;
 
-static int check_shape(int dtype, int32_t d, int32_t H, int64_t n) {
+int check_shape(int dtype, int32_t d, int32_t H, int64_t n) {
   HFFN_REQUIRE(dtype == HFFN_F32 || dtype == HFFN_BF16, "unknown dtype %d", dtype);
   HFFN_REQUIRE(d >= 1 && d <= 32767 && H >= 1 && H <= 32767, "d_model %d / d_ff %d out of range [1, 32767]", d, H);
   HFFN_REQUIRE(n >= 1 && n <= kMaxTokens, "token count %lld out of range", (long long)n);
@@ -75,7 +75,7 @@ static int resolve_down(int mode, int64_t n, int32_t H) {
   return mode;
 }
 
-static int check_layer(const hffn_layer* L) {
+int check_layer(const hffn_layer* L) {
   HFFN_REQUIRE(L != nullptr, "null layer");
   HFFN_REQUIRE(L->b_up && L->up_offsets && L->up_idx && L->up_val && L->b_down && L->out_offsets && L->out_hidden &&
                    L->out_val,

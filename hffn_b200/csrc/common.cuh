@@ -41,6 +41,9 @@ template <typename T> __device__ __forceinline__ T ldg(const T* p) { return __ld
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Internal status (never returned by the C ABI): a specialised launcher declines a call, the general one runs it.
+constexpr int kNotApplicable = -1000;
+
 // Per-thread last error message of the C ABI (hffn_last_error).
 void set_error(const char* fmt, ...);
 const char* last_error();

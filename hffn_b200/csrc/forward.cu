@@ -530,8 +530,17 @@ static int launch_down_t(int mode, const T* act, const int32_t* off, const int16
   return launch_status("down_tile");
 }
 
+int launch_up_decode(int dtype, const void* x, const int32_t* off, const int16_t* idx, const void* w, const void* b,
+                     void* act, float* z, int d, int H, int64_t n, cudaStream_t s);
+int launch_down_decode(int dtype, const void* act, const int32_t* off, const int16_t* hid, const void* v,
+                       const void* bias, void* y, int d, int H, int64_t n, cudaStream_t s);
+
 int launch_up(int dtype, int mode, const void* x, const int32_t* off, const int16_t* idx, const void* w,
               const void* b, void* act, float* z, int d, int H, int64_t n, cudaStream_t s) {
+  if (mode == HFFN_UP_COOP && n <= 8) {     // the decode kernels (decode.cu) when the shape fits them
+    const int status = launch_up_decode(dtype, x, off, idx, w, b, act, z, d, H, n, s);
+    if (status != kNotApplicable) return status;
+  }
   if (dtype == HFFN_F32) {
     auto f = z ? launch_up_t<float, true> : launch_up_t<float, false>;
     return f(mode, (const float*)x, off, idx, (const float*)w, (const float*)b, (float*)act, z, d, H, n, s);
@@ -543,6 +552,10 @@ int launch_up(int dtype, int mode, const void* x, const int32_t* off, const int1
 
 int launch_down(int dtype, int mode, const void* act, const int32_t* off, const int16_t* hid, const void* v,
                 const void* bias, void* y, int d, int H, int64_t n, cudaStream_t s) {
+  if (mode == HFFN_DOWN_COOP && n <= 8) {
+    const int status = launch_down_decode(dtype, act, off, hid, v, bias, y, d, H, n, s);
+    if (status != kNotApplicable) return status;
+  }
   if (dtype == HFFN_F32)
     return launch_down_t<float>(mode, (const float*)act, off, hid, (const float*)v, (const float*)bias, (float*)y, d,
                                 H, n, s);

@@ -5,7 +5,9 @@
 // The scratch lives in `g_noalloc_scratch`, a file-scope __device__ array of kNoAllocScratchBytes (16 MiB) that every
 // GPU loading this library holds until the process exits. Host code cannot use the array's name as a device address
 // (on the host it names a host-side stand-in), so the first call on each device, with that device current, asks the
-// runtime for the device address with cudaGetSymbolAddress and caches it; later calls reuse it.
+// runtime for the device address with cudaGetSymbolAddress and caches it; later calls reuse it. The cached address
+// belongs to the device's primary context (the one the CUDA runtime and torch use): it stays valid while that context
+// lives, not across cudaDeviceReset, and not for a caller that makes its own context current.
 #include <mutex>
 
 #include "common.cuh"
@@ -22,6 +24,8 @@ int launch_up(int dtype, int mode, const void* x, const int32_t* off, const int1
 int launch_down(int dtype, int mode, const void* act, const int32_t* off, const int16_t* hid, const void* v,
                 const void* bias, void* y, int d, int H, int64_t n, cudaStream_t s);
 int64_t max_staged_rows();
+int check_shape(int dtype, int32_t d, int32_t H, int64_t n);   // abi.cu: the argument checks of hffn_forward
+int check_layer(const hffn_layer* L);
 
 static std::mutex g_scratch_mutex;
 static void* g_scratch_address[kMaxDevices] = {};
@@ -61,15 +65,11 @@ extern "C" {
 int64_t hffn_forward_noalloc_max_bytes(void) { return (int64_t)kNoAllocScratchBytes; }
 
 int hffn_forward_noalloc(int dtype, const hffn_layer* layer, const void* x, void* y, int64_t n, void* stream) {
-  HFFN_REQUIRE(layer != nullptr, "null layer");
-  HFFN_REQUIRE(layer->b_up && layer->up_offsets && layer->up_idx && layer->up_val && layer->b_down &&
-                   layer->out_offsets && layer->out_hidden && layer->out_val,
-               "null layer array");
-  HFFN_REQUIRE(dtype == HFFN_F32 || dtype == HFFN_BF16, "unknown dtype %d", dtype);
+  // the same refusals as hffn_forward (layer arrays, edge-count range, dtype, dimensions, token range)
+  HFFN_TRY(check_layer(layer));
+  HFFN_TRY(check_shape(dtype, layer->d_model, layer->d_ff, n));
   HFFN_REQUIRE(x && y, "null pointer argument");
   const int32_t d = layer->d_model, H = layer->d_ff;
-  HFFN_REQUIRE(d >= 1 && d <= 32767 && H >= 1 && H <= 32767, "d_model %d / d_ff %d out of range [1, 32767]", d, H);
-  HFFN_REQUIRE(n >= 1, "token count %lld out of range", (long long)n);
   const int64_t elem = dtype == HFFN_F32 ? 4 : 2;
   HFFN_REQUIRE(n <= (int64_t)(kNoAllocScratchBytes / (elem * H)),
                "noalloc: d_ff x n x %lld bytes = %lld exceeds the %lld-byte scratch (at most %lld tokens for d_ff %d)",

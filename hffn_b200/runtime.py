@@ -201,8 +201,15 @@ class HFFNRuntime:
         return self._act.element_size() * (self._act.numel() + self._y.numel()) + extra
 
     def device_errors(self) -> int:
-        """The error flag of the tensor-core kernels (0: none; a wait timed out otherwise). Synchronises."""
-        return int(self._err.item())
+        """The error flags of the tensor-core kernels and of the decode kernels (0: none; the code of a wait that
+        timed out otherwise). Synchronises."""
+        code = int(self._err.item())
+        if code:
+            return code
+        flag = native.ctypes.c_int32(0)
+        with torch.cuda.device(self.device):
+            native.check(native.lib.hffn_decode_error(native.ctypes.byref(flag), 0), "hffn_decode_error")
+        return int(flag.value)
 
     def _check_input(self, x: torch.Tensor) -> int:
         if x.dim() != 2 or x.shape[1] != self.d_model or x.dtype != self.dtype or x.device != self._y.device \

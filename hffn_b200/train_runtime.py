@@ -31,6 +31,12 @@ from .runtime import MAX_TOKENS, TC, TC_MIN_TOKENS, HFFNLayer, HFFNRuntime
 PARAMETERS = ("up_val", "b_up", "out_val", "b_down")
 SUPPORTS = ("in_offsets", "in_pos", "in_hidden", "hid_offsets", "hid_pos", "hid_output")
 PARTIAL_MAX_TOKENS = 2048
+GRAD_TILE = 256          # tokens per tile of the reference's partial workspace (kernels_train.py:85)
+
+
+def grad_tiles(n: int) -> int:
+    """Tiles of GRAD_TILE tokens the reference's gradient kernels cut N into."""
+    return -(-n // GRAD_TILE)
 
 
 def transposed_supports(layer: HFFNLayer) -> dict[str, torch.Tensor]:
@@ -111,6 +117,17 @@ class HFFNTrainRuntime:
         self._fused_structs = [native.TrainParams(*(
             native.Param(p.value, p.grad if store_gradients else None, p.m, p.v, p.count)
             for p in (s.up_val, s.b_up, s.out_val, s.b_down))) for s in self._param_structs]
+        # Columns of the partial workspace per layer, the reference's layout (train_runtime.py:79-89): g_down [0, c1),
+        # gb_down [c1, c2), g_up [c2, c3), gb_up [c3, S); hffn_backward's token-group partials use the same columns.
+        self._columns = []
+        for params in runtime._tensors:
+            for offsets, values in (("out_offsets", "out_val"), ("up_offsets", "up_val")):
+                if int(params[offsets][0]) != 0 or int(params[offsets][-1]) != params[values].numel():
+                    raise ValueError(f"{offsets} must cover {values} exactly (partial workspace columns)")
+            c1 = params["out_val"].numel()
+            c2 = c1 + self.d_model
+            c3 = c2 + params["up_val"].numel()
+            self._columns.append((c1, c2, c3, c3 + self.d_ff))
         self.steps = [0] * len(runtime.layers)
         self.calls: Counter = Counter()
         self._saved: tuple | None = None
@@ -123,26 +140,37 @@ class HFFNTrainRuntime:
 
     # -- buffers -------------------------------------------------------------------------------------------------
     def reserve(self, n: int) -> None:
-        """Size every dense buffer for N tokens; allocates only when N grows (call it with the largest N)."""
-        runtime = self.runtime
-        if n > runtime._tokens:
-            runtime._reserve(n)
-            self._saved = None
-            self.growths += 1
-        if n > self._tokens:
+        """Size every dense buffer for N tokens; allocates only when N grows (call it with the largest N).
+
+        ``growths`` counts each buffer family that had to grow (the runtime's forward buffers, this step's
+        activation buffers, the backward workspace): a timed window must leave it unchanged."""
+        if n > self.runtime._tokens:             # forward buffers (act, y, the tensor-core workspace)
+            self.runtime._reserve(n)
+            self._grown()
+        if n > self._tokens:                     # this step's token-sized buffers
             self._tokens = n
-            self.growths += 1
-            device = runtime.device
-            self._z = torch.empty(self.d_ff * n, device=device)
-            self._gz = torch.empty(self.d_ff * n, device=device)
-            self._gx = torch.empty(n, self.d_model, device=device)
-            self._gy = torch.empty(n, self.d_model, device=device)
-            self._loss = torch.zeros(1, device=device)
-            self._saved = None
+            make = lambda *shape: torch.empty(*shape, device=self.runtime.device)  # noqa: E731
+            self._z, self._gz = make(self.d_ff * n), make(self.d_ff * n)
+            self._gx, self._gy = make(n, self.d_model), make(n, self.d_model)
+            self._loss = torch.zeros(1, device=self.runtime.device)
+            self._grown()
         self._reserve_partials(n)
 
+    def _grown(self) -> None:
+        """A buffer was replaced: count it, and forget the forward state the backward would read from the old one."""
+        self.growths += 1
+        self._saved = None
+
     def _reserve_partials(self, n: int) -> None:
-        """Size the backward workspace for N tokens (grows only with N)."""
+        """Size the backward workspace for N tokens (grows only with N).
+
+        Refuses (ValueError) an N at which the reference's partial workspace, ``grad_tiles(N)`` rows of the widest
+        layer's columns, would pass 32-bit indexing (``train_runtime.py:119-127``): the drop-in accepts the token
+        range the reference accepts. This build's workspace holds at most 16 token groups and is indexed with 64-bit
+        offsets, so the bound is the reference's contract rather than a limit of these kernels."""
+        stride = max(c[3] for c in self._columns)
+        if grad_tiles(n) * stride >= 2 ** 32:
+            raise ValueError(f"partial workspace of {grad_tiles(n)} tiles x {stride} columns exceeds 32-bit indexing")
         if n <= self._work_tokens:
             return
         floats = max(int(native.lib.hffn_backward_workspace(s, n)) for s in self.runtime._structs)
@@ -280,6 +308,9 @@ class HFFNTrainRuntime:
 
     # -- read access for the checks (views, no copy) -------------------------------------------------------------
     def parameters(self, index: int) -> dict[str, torch.Tensor]:
+        """The compact values of layer ``index`` (views: a caller may write through them, as the reference's checks
+        do to restore a state, so the layer's dense tensor-core operands are marked for a rebuild)."""
+        self.runtime.mark_updated(index)
         return {name: self.runtime._tensors[index][name] for name in PARAMETERS}
 
     def gradients(self, index: int) -> dict[str, torch.Tensor]:
@@ -299,13 +330,15 @@ class HFFNTrainRuntime:
                 "gz": self._gz[:self.d_ff * n].view(self.d_ff, n), "gx": self._gx[:n]}
 
     def nbytes(self, index: int) -> dict[str, int]:
-        def size(tensors) -> int:
-            return sum(t.numel() * t.element_size() for t in tensors)
-        params = self.runtime._tensors[index]
-        return {"values": size(params[name] for name in PARAMETERS),
-                "gradients": size(self._grads[index].values()),
-                "moments": size(t for pair in self._moments[index].values() for t in pair),
-                "indices": size(params[name] for name in ("up_offsets", "up_idx", "out_offsets", "out_hidden"))
-                + size(self._supports[index].values()),
-                "workspace": self.runtime.workspace_bytes() + size((self._z, self._gz, self._gx, self._gy)),
-                "partials": size((self._work,))}
+        """Device bytes by role for layer ``index``: its compact values, gradients, moments and index arrays, and the
+        buffers shared by the layers (forward work buffers with this step's activations; backward workspace)."""
+        def total(*groups) -> int:
+            return sum(t.numel() * t.element_size() for group in groups for t in group)
+        own = self.runtime._tensors[index]
+        return {"values": total(own[k] for k in PARAMETERS),
+                "gradients": total(self._grads[index].values()),
+                "moments": total(*self._moments[index].values()),
+                "indices": total((own[k] for k in ("up_offsets", "up_idx", "out_offsets", "out_hidden")),
+                                 self._supports[index].values()),
+                "workspace": self.runtime.workspace_bytes() + total((self._z, self._gz, self._gx, self._gy)),
+                "partials": total((self._work,))}

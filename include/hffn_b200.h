@@ -134,6 +134,11 @@ int hffn_adamw(const hffn_param* param, const hffn_adamw_step* step, void* strea
 int hffn_mse(const float* y, const float* target, float* gy, float* loss, int64_t n, int32_t d_model, float* work,
              void* stream);
 
+/* The error flag of the decode kernels (hffn_up / hffn_down / hffn_forward in the cooperative mode at n <= 8, which
+ * stage their slot windows with TMA bulk copies): 0, or the code of the first bounded wait that expired (301) on the
+ * current device. Synchronous; clear != 0 resets it. No counterpart in the reference (its kernels do not wait). */
+int hffn_decode_error(int32_t* value, int clear);
+
 /* Device-side check of a layer's arrays (offsets from 0 to nnz, non-decreasing, indices in range): sets *flag
  * (device int32, cleared by the call) to 1 if any array is invalid. The export reader's checks
  * (runtime/common/pythia/hffn_pythia/export.py:37-45) on device-resident arrays. */
@@ -271,8 +276,10 @@ int hffn_train_step_tc(const hffn_layer* layer, const hffn_dense* dense, const f
  * hidden activations in a 16 MiB array that the library holds on every GPU that loads it, until the process exits.
  * Limit: d_ff x n x sizeof(storage) <= hffn_forward_noalloc_max_bytes() (16 MiB); larger calls return
  * HFFN_ERR_ARGUMENT before any launch. The first call on a device looks up the array's device address with that
- * device current; make that first call before any stream capture. Every call uses the same array: calls that
- * overlap on the GPU (other streams, other host threads) race on it. */
+ * device current; make that first call before any stream capture. The address is cached per device ordinal and
+ * belongs to the device's primary context (the runtime's and torch's): it is valid while that context lives, not
+ * after cudaDeviceReset and not under a context the caller created and made current. Every call uses the same
+ * array: calls that overlap on the GPU (other streams, other host threads) race on it. */
 int64_t hffn_forward_noalloc_max_bytes(void);
 int hffn_forward_noalloc(int dtype, const hffn_layer* layer, const void* x, void* y, int64_t n, void* stream);
 

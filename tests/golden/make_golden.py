@@ -19,6 +19,7 @@ from __future__ import annotations
 import ast
 import hashlib
 import json
+import os
 import sys
 from dataclasses import dataclass
 from pathlib import Path
@@ -27,7 +28,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REFERENCE = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+REFERENCE = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("HFFN_REFERENCE", "/root/reference"))
 FFN_COMMON = REFERENCE / "runtime/common/ffn"
 TRAINING = REFERENCE / "runtime/gpu/nvidia/ffn/training"
 RUNTIME_PY = REFERENCE / "runtime/gpu/nvidia/common/kernels/hffn_cuda/runtime.py"

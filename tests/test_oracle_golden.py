@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 
 from hffn_b200 import synth
-from oracle import forward64, layout, train64, x86ref
+from oracle import forward64, layout, train64, x86ref, x86train
 
 
 def load(golden, name):
@@ -93,3 +93,27 @@ def test_reference_x86_kernel_matches_forward64(name, n):
     x = synth.make_input(case, n)
     y = x86ref.X86Kernel(layer, threads=4).forward(x)
     assert np.max(np.abs(y - forward64.forward(layer, x))) <= 2e-5
+
+
+@pytest.mark.skipif(not x86train.available(), reason="oracle/_ref not built (make -C oracle)")
+@pytest.mark.parametrize("name,n", [("homog_256_1024", 64), ("irreg_512_2048", 40)])
+def test_reference_g4_training_step_matches_train64(name, n):
+    """The reference's own CPU training step (forward, backward, AdamW of the G4 kernel) against the float64 oracle:
+    every gradient group within 2e-5 of its scale, the updated values against the AdamW closed form."""
+    case = synth.TEST_CASES[name]
+    layer = synth.make_layer(case)
+    x, target = synth.make_input(case, n), synth.make_target(case, n)
+    step = x86train.G4Step(layer, n, **train64.HYPER)
+    before = step.up_val.copy()
+    loss = step.step_mse(x, target)
+    ref = train64.step_groups(layer, x, train64.mse_upstream(target, n))
+    assert abs(loss - train64.mse_loss(ref["y"], target)) <= 1e-5 * train64.mse_loss(ref["y"], target)
+    got = step.gradients()
+    for key in ("g_up", "g_down", "gb_up", "gb_down", "gx"):
+        expected = np.asarray(ref[key])
+        assert np.max(np.abs(got[key] - expected)) <= 2e-5 * np.abs(expected).max(), key
+    p1, _, _ = train64.adamw_closed_form(before.astype(np.float64), got["g_up"].astype(np.float64), 0.0, 0.0, 1,
+                                         **train64.HYPER)
+    mask = np.abs(ref["g_up"]) >= 1e-3 * np.abs(ref["g_up"]).max()
+    scale = np.maximum(np.abs(p1), np.abs(before))
+    assert np.max((np.abs(step.up_val - p1) / scale)[mask]) <= 1e-5

@@ -4,7 +4,9 @@ It exists for callers that can pass the library only their input and output devi
 device memory themselves, for instance a plugin whose host framework owns all device memory. The entry keeps the
 hidden activations in a fixed array inside the library, so the caller passes no workspace. Checked here against the
 existing entry (hffn_forward with a caller-provided workspace) on two calls in a row, within the forward tolerance of
-the other tests, and the size limit is refused before any launch. This file is collected last on purpose.
+the other tests (float32; bf16 within the bf16 tolerance), at the largest token count the array admits (computed from
+the entry's own limit, so the last row of the array stays covered if the limit changes), and the size limit is
+refused before any launch in both storage types. This file is collected last on purpose.
 """
 import numpy as np
 import pytest
@@ -16,6 +18,8 @@ pytestmark = pytest.mark.gpu
 
 ABS_TOLERANCE = 2e-5
 REL_TOLERANCE = 1e-5
+BF16_REL_TOLERANCE = 2e-2
+ELEMENT = {torch.float32: 4, torch.bfloat16: 2}
 
 
 def kernel_layer(layer):
@@ -26,37 +30,56 @@ def kernel_layer(layer):
                                        t(layer.down_val))
 
 
-@pytest.mark.parametrize("name,n", [("irreg_512_2048", 300), ("c2_1024_4096_k512", 1024), ("homog_256_1024", 3)])
-def test_noalloc_matches_forward_on_two_calls(name, n):
+def largest_n(case, dtype) -> int:
     from hffn_b200 import _native as native
-    from hffn_b200.runtime import HFFNRuntime
+    return int(native.lib.hffn_forward_noalloc_max_bytes()) // (ELEMENT[dtype] * case.d_ff)
+
+
+def compare_two_calls(name, n, dtype):
+    from hffn_b200 import _native as native
+    from hffn_b200.runtime import DTYPES, HFFNRuntime
     case = synth.CASES[name]
-    runtime = HFFNRuntime([kernel_layer(synth.make_layer(case))], "cuda", tensor_cores=False)
-    x = torch.from_numpy(synth.make_input(case, n)).cuda()
+    runtime = HFFNRuntime([kernel_layer(synth.make_layer(case))], "cuda", dtype, tensor_cores=False)
+    n = largest_n(case, dtype) if n is None else n
+    x = torch.from_numpy(synth.make_input(case, n)).to(dtype).cuda()
     expected = runtime.forward(0, x).double().clone()      # hffn_forward, caller-provided act workspace
     stream = native.stream_handle(runtime.device)
     scale = expected.abs().clamp(min=1.0)
     for _ in range(2):
-        y = torch.full((n, case.d_model), float("nan"), device="cuda")
-        status = native.lib.hffn_forward_noalloc(native.F32, runtime._structs[0], x.data_ptr(), y.data_ptr(), n, stream)
+        y = torch.full((n, case.d_model), float("nan"), device="cuda", dtype=dtype)
+        status = native.lib.hffn_forward_noalloc(DTYPES[dtype], runtime._structs[0], x.data_ptr(), y.data_ptr(), n,
+                                                 stream)
         native.check(status, "hffn_forward_noalloc")
         torch.cuda.synchronize()
         distance = (y.double() - expected).abs()
-        assert float(distance.max()) <= ABS_TOLERANCE
-        assert float((distance / scale).max()) <= REL_TOLERANCE
+        if dtype == torch.float32:
+            assert float(distance.max()) <= ABS_TOLERANCE
+            assert float((distance / scale).max()) <= REL_TOLERANCE
+        else:
+            assert float((distance / scale).max()) <= BF16_REL_TOLERANCE
 
 
-def test_noalloc_refuses_beyond_its_scratch():
+@pytest.mark.parametrize("name,n", [("irreg_512_2048", 300), ("c2_1024_4096_k512", None), ("homog_256_1024", 3)])
+def test_noalloc_matches_forward_on_two_calls(name, n):
+    compare_two_calls(name, n, torch.float32)
+
+
+@pytest.mark.parametrize("name,n", [("homog_256_1024", 3), ("irreg_512_2048", 300), ("c2_1024_4096_k512", None)])
+def test_noalloc_bf16_matches_forward_on_two_calls(name, n):
+    compare_two_calls(name, n, torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_noalloc_refuses_beyond_its_scratch(dtype):
     from hffn_b200 import _native as native
-    from hffn_b200.runtime import HFFNRuntime
+    from hffn_b200.runtime import DTYPES, HFFNRuntime
     case = synth.CONFIGS["c2_1024_4096_k512"]
-    runtime = HFFNRuntime([kernel_layer(synth.make_layer(case))], "cuda", tensor_cores=False)
-    limit = native.lib.hffn_forward_noalloc_max_bytes()
-    n_max = limit // (4 * case.d_ff)
-    x = torch.zeros(n_max + 1, case.d_model, device="cuda")
+    runtime = HFFNRuntime([kernel_layer(synth.make_layer(case))], "cuda", dtype, tensor_cores=False)
+    n_max = largest_n(case, dtype)
+    x = torch.zeros(n_max + 1, case.d_model, device="cuda", dtype=dtype)
     y = torch.zeros_like(x)
-    status = native.lib.hffn_forward_noalloc(native.F32, runtime._structs[0], x.data_ptr(), y.data_ptr(), n_max + 1,
-                                             native.stream_handle(runtime.device))
+    status = native.lib.hffn_forward_noalloc(DTYPES[dtype], runtime._structs[0], x.data_ptr(), y.data_ptr(),
+                                             n_max + 1, native.stream_handle(runtime.device))
     assert status == native.HFFN_ERR_ARGUMENT
     assert b"scratch" in native.lib.hffn_last_error()
-    assert np.all(y.cpu().numpy() == 0)
+    assert np.all(y.float().cpu().numpy() == 0)
