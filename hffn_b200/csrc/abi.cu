@@ -7,7 +7,8 @@
 namespace hffn {
 
 int launch_up(int dtype, int mode, const void* x, const int32_t* off, const int16_t* idx, const void* w,
-              const void* b, void* act, float* z, int d, int H, int64_t n, cudaStream_t s);
+              const void* b, void* act, float* z, int d, int H, int64_t n, cudaStream_t s,
+              const int16_t* next_idx = nullptr, const void* next_val = nullptr, int64_t next_nnz = 0);
 int launch_down(int dtype, int mode, const void* act, const int32_t* off, const int16_t* hid, const void* v,
                 const void* bias, void* y, int d, int H, int64_t n, cudaStream_t s);
 int64_t max_staged_rows();
@@ -108,8 +109,10 @@ int hffn_down_mode(int64_t n, int32_t d_ff) {
   return n <= kCoopMaxTokens ? HFFN_DOWN_COOP : HFFN_DOWN_BLOCKED;
 }
 
-int hffn_up(int dtype, int mode, const void* x, const int32_t* up_offsets, const int16_t* up_idx, const void* up_val,
-            const void* b_up, void* act, float* z, int32_t d_model, int32_t d_ff, int64_t n, void* stream) {
+// hffn_up, and the up half of hffn_forward, whose decode kernel also prefetches the down arrays (next_*) into L2.
+static int up_call(int dtype, int mode, const void* x, const int32_t* up_offsets, const int16_t* up_idx,
+                   const void* up_val, const void* b_up, void* act, float* z, int32_t d_model, int32_t d_ff, int64_t n,
+                   void* stream, const int16_t* next_idx, const void* next_val, int64_t next_nnz) {
   HFFN_TRY(check_shape(dtype, d_model, d_ff, n));
   HFFN_REQUIRE(x && up_offsets && up_idx && up_val && b_up && act, "null pointer argument");
   HFFN_REQUIRE(z == nullptr || dtype == HFFN_F32, "z is stored by the float32 path only");
@@ -118,7 +121,13 @@ int hffn_up(int dtype, int mode, const void* x, const int32_t* up_offsets, const
   HFFN_REQUIRE(mode == HFFN_UP_COOP || d_model <= max_staged_rows(), "d_model %d exceeds the staged tile", d_model);
   HFFN_TRY(bind_stream_device(stream));
   return launch_up(dtype, mode, x, up_offsets, up_idx, up_val, b_up, act, z, d_model, d_ff, n,
-                   static_cast<cudaStream_t>(stream));
+                   static_cast<cudaStream_t>(stream), next_idx, next_val, next_nnz);
+}
+
+int hffn_up(int dtype, int mode, const void* x, const int32_t* up_offsets, const int16_t* up_idx, const void* up_val,
+            const void* b_up, void* act, float* z, int32_t d_model, int32_t d_ff, int64_t n, void* stream) {
+  return up_call(dtype, mode, x, up_offsets, up_idx, up_val, b_up, act, z, d_model, d_ff, n, stream, nullptr,
+                 nullptr, 0);
 }
 
 int hffn_down(int dtype, int mode, const void* act, const int32_t* out_offsets, const int16_t* out_hidden,
@@ -138,8 +147,8 @@ int hffn_down(int dtype, int mode, const void* act, const int32_t* out_offsets, 
 int hffn_forward(int dtype, const hffn_layer* layer, const void* x, void* y, void* act, float* z, int64_t n,
                  int up_mode, int down_mode, void* stream) {
   HFFN_TRY(check_layer(layer));
-  HFFN_TRY(hffn_up(dtype, up_mode, x, layer->up_offsets, layer->up_idx, layer->up_val, layer->b_up, act, z,
-                   layer->d_model, layer->d_ff, n, stream));
+  HFFN_TRY(up_call(dtype, up_mode, x, layer->up_offsets, layer->up_idx, layer->up_val, layer->b_up, act, z,
+                   layer->d_model, layer->d_ff, n, stream, layer->out_hidden, layer->out_val, layer->nnz_down));
   return hffn_down(dtype, down_mode, act, layer->out_offsets, layer->out_hidden, layer->out_val, layer->b_down, y,
                    layer->d_model, layer->d_ff, n, stream);
 }

@@ -1,31 +1,32 @@
 // Decode kernels of the forward: the cooperative mode at n <= 8 tokens per call (the decode steps of a language model,
-// one call per layer). A call moves the layer's compact index / value streams once (C4 bf16: 8.4 MB per projection)
-// and does 2 x n FLOPs per slot, so it is bound by HBM in principle. What bounds a plain kernel in practice is latency:
-// a warp that walks its rows' slots with vector loads keeps 32 bytes per lane in flight, far from the megabytes HBM
-// needs in flight to stream at full rate. Design:
+// one call per layer). A call streams the layer's compact index / value arrays once (C4 bf16: 8.4 MB per projection)
+// and does 2 n FLOPs per slot: HBM-bound in principle. Measured on B200 (ncu and per-phase %globaltimer stamps of an
+// instrumented copy), a plain design is bound instead by shared-memory wavefronts of the random-row gathers and by
+// barrier-separated passes with too little independent work per warp. Design:
 //
-//  - one CTA per SM, persistent over a contiguous range of output rows (neurons for up, output features for down),
-//    whose slots are contiguous in the compact arrays;
-//  - the CTA's slot range is cut into row-aligned windows of at most `window` slots; two windows are in flight at a
-//    time in two shared-memory slots, each moved by one TMA bulk copy per array (cp.async.bulk, completion counted on
-//    an mbarrier). Both are issued at kernel start, before griddepcontrol.wait, and the rest of the CTA's range is
-//    sent to L2 (cp.async.bulk.prefetch.L2): the compact arrays are constants of the layer, only the gathered table
-//    (x or act) is written by the preceding kernel. Launched with programmatic dependent launch, a kernel starts
-//    while its predecessor still computes (shared memory is budgeted so that an up CTA and a down CTA fit one SM),
-//    so one projection's stream overlaps the other's compute;
+//  - one CTA per SM, persistent over a contiguous range of output rows (neurons for up, output features for down);
+//  - prologue, before griddepcontrol.wait (launched with programmatic dependent launch, the kernel starts while its
+//    predecessor still runs): the CTA's slice of its own compact arrays is copied into shared memory by TMA bulk
+//    copies (cp.async.bulk, completion counted on an mbarrier) when it fits, else sent to L2
+//    (cp.async.bulk.prefetch.L2); the up kernel of a layer also sends a slice of the down projection's arrays to L2.
+//    The compact arrays are constants of the layer; only the gathered table (x or act) is written by the predecessor.
+//    The wait on the copies is bounded (2 s of %globaltimer): on expiry the CTA records code 301 in the decode error
+//    flag (hffn_decode_error), waits (bounded) for its copies and returns;
 //  - the gathered table is staged once per CTA after griddepcontrol.wait, [row][plane][copy] in 16-byte units (a
-//    plane holds 8 bf16 or 4 float tokens of a row), read at L2 (the predecessor wrote it); replicated when shared
-//    memory allows: lane L of a quarter-warp reads copy L mod COPIES, which spreads its random rows over more bank
-//    groups (8 copies: never a conflict);
-//  - a row's slots are walked by `split` warps (a power of two picked per window), 8 consecutive slots per lane per
-//    16-byte load from the window's slot; each warp sums its lanes with the xor tree and the row's warps are added in
-//    warp order: a fixed summation order, the same bits on every call;
-//  - every wait is bounded (2 s of %globaltimer): on expiry the CTA records kErrDecodeTimeout in the library's decode
-//    error flag (hffn_decode_error), waits (bounded) for its copies in flight and returns.
+//    plane holds 8 bf16 or 4 float tokens of a row), read at L2 (ld.global.cg: the predecessor wrote it), replicated
+//    COPIES times: lane L of a quarter-warp reads copy L mod COPIES; with 8 copies (up: x of 1024 features, 128 KB)
+//    the eight 16-byte gathers of a quarter-warp always fall in distinct bank groups;
+//  - warps walk rows independently: a row owned by one warp is reduced by its xor tree and stored by its lanes, with
+//    no CTA-wide barrier; a row shared by `split` warps (few rows per CTA: the down projection) is combined through
+//    shared memory under a named barrier of just those warps. 8 consecutive slots per lane per 16-byte index load
+//    (from shared memory, or from L2 where the prologue put them); products accumulated in pairs by the packed
+//    fma.rn.f32x2; a fixed summation order: per lane its head slot, its tail slot, its
+//    chunks in order; the xor tree; the warps of a row in warp order. The same bits on every call.
 //   up    act[r, t] = gelu(b_up[r] + sum of up_val[e] x[t, up_idx[e]] over the slots e of neuron r)  (z optional)
 //   down  y[t, o] = (sum of out_val[q] act[out_hidden[q], t] over the edges q of output o) + b_down[o]
 #include <algorithm>
 #include <atomic>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -35,14 +36,17 @@ namespace dec {
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxDevices = 64;
-constexpr int kMaxRowsPerCta = 256;          // off slice staged per CTA: rows_out <= 256 x SMs
-constexpr size_t kUpBudget = 92 * 1024;      // an up CTA and a down CTA together stay within one SM's shared memory
-constexpr size_t kDownBudget = 126 * 1024;
-constexpr size_t kMinBuffer = 16 * 1024;     // smallest slot buffer worth the staging
+constexpr size_t kBudget = 132 * 1024;   // table copies + warp partials of one CTA
+constexpr size_t kTotal = 200 * 1024;    // with the edge buffer (one CTA per SM)
+constexpr int kMaxRowsPerCta = 256;
+// shared memory after the table: warp partials [2][kWarps][8] floats, the CTA's offsets, the mbarrier and the staging
+// record, then the edge buffer
+constexpr size_t kPartBytes = 2 * kWarps * 8 * 4, kOffsBytes = ((kMaxRowsPerCta + 1) * 4 + 15) / 16 * 16;
+constexpr size_t kHeaderBytes = kPartBytes + kOffsBytes + 64;
 constexpr int kErrDecodeTimeout = 301;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-__device__ int g_decode_error;               // first error code recorded by a decode kernel (0: none)
+__device__ int g_decode_error;           // first error code recorded by a decode kernel (0: none)
 
 struct Params {
   const void* src;      // up: x [n, rows_in] token-major; down: act [rows_in, n] hidden-major
@@ -52,18 +56,17 @@ struct Params {
   const void* bias;     // [rows_out]
   void* out;            // up: act [rows_out, n]; down: y [n, rows_out]
   float* z;             // up, optional: z [rows_out, n]
-  int rows_in, rows_out, n, copies;
-  int buffer;           // bytes of the window buffer (a multiple of 32)
+  const void* hint[2];  // optional: two more arrays the next kernel streams (the down projection's), prefetched
+  int64_t hint_bytes[2];
+  int rows_in, rows_out, n, copies, split;
+  int buffer;           // bytes of the edge buffer after the table and the partials (0: none)
   int vector_src;       // down: act rows are whole 16-byte units (n fills the planes, 16-byte aligned base)
 };
 
-// One window of the CTA's rows, written by the producer thread before its copies. Elements [i0, i1) of idx and
-// [v0, v1) of val are in shared memory at byte offsets idx_at and val_at of the buffer (i1 <= i0: none; those
-// elements are read from global memory).
-struct Window {
-  int ra, rb;           // rows [ra, rb); ra == rb: no rows left
-  int i0, i1, v0, v1;
-  int idx_at, val_at;
+// The CTA's slots in shared memory: elements [i0, i1) of idx at byte 0 of the buffer, [v0, v1) of val at val_at
+// (i1 = v1 = 0: none, the kernel reads its slots from global memory).
+struct Staged {
+  int i0, i1, v0, v1, val_at;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -72,15 +75,6 @@ __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)));
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
@@ -125,6 +119,11 @@ __device__ __forceinline__ void prefetch_l2(const void* base, int64_t lo, int64_
 __device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void wait_for_predecessor() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Barrier of the `count` threads of one row group (ids 1..15; 0 is __syncthreads).
+__device__ __forceinline__ void group_barrier(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 template <typename T> struct Unit;
 template <> struct Unit<__nv_bfloat16> {
   static constexpr int kTokens = 8;
@@ -152,8 +151,7 @@ template <> struct Unit<float> {
   __device__ static __forceinline__ uint4 pack(const uint32_t (&v)[4]) { return make_uint4(v[0], v[1], v[2], v[3]); }
 };
 
-// The 16-byte unit (row, plane) of the table: tokens plane * TPP + k, zero past n. Read at L2 (ld.global.cg): the
-// table was written by the preceding kernel, which may still have been running when this CTA started.
+// The 16-byte unit (row, plane) of the table: tokens plane * TPP + k, zero past n.
 template <typename T, bool kUp>
 __device__ __forceinline__ uint4 load_unit(const Params& p, int row, int plane) {
   constexpr int TPP = Unit<T>::kTokens;
@@ -169,15 +167,47 @@ __device__ __forceinline__ uint4 load_unit(const Params& p, int row, int plane) 
   return Unit<T>::pack(v);
 }
 
-template <typename T, int PLANES>
-__device__ __forceinline__ void load_row(const uint4* table, int copies, int row, int copy,
-                                         float (&r)[Unit<T>::kTokens * PLANES]) {
-#pragma unroll
-  for (int plane = 0; plane < PLANES; ++plane)
-    Unit<T>::unpack(table[((size_t)row * PLANES + plane) * copies + copy], r + plane * Unit<T>::kTokens);
+// Pairs of float32 in one 64-bit register, multiplied and added by the packed fma.rn.f32x2 of sm_100: per element the
+// same fused multiply-add, rounded once, as a scalar FFMA (the same bits), at half the instruction count.
+using f32x2 = unsigned long long;
+
+__device__ __forceinline__ f32x2 pair_bits(uint32_t lo, uint32_t hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
 }
 
-__device__ __forceinline__ void unpack_idx8(const int4 raw, int (&i)[8]) {
+__device__ __forceinline__ void fma2(f32x2& acc, f32x2 a, f32x2 b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+
+__device__ __forceinline__ float pair_lo(f32x2 v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float pair_hi(f32x2 v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+// acc[k] += w * (tokens 2k, 2k + 1) of the 16-byte unit u (bf16: 8 tokens, 4 pairs; float: 4 tokens, 2 pairs).
+__device__ __forceinline__ void fma_unit(f32x2* acc, f32x2 w2, uint4 u, __nv_bfloat16*) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) fma2(acc[k], w2, pair_bits(w[k] << 16, w[k] & 0xffff0000u));
+}
+__device__ __forceinline__ void fma_unit(f32x2* acc, f32x2 w2, uint4 u, float*) {
+  fma2(acc[0], w2, pair_bits(u.x, u.y));
+  fma2(acc[1], w2, pair_bits(u.z, u.w));
+}
+
+// acc += w * row `row` of the table (copy `copy`), all its planes.
+template <typename T, int PLANES, int COPIES>
+__device__ __forceinline__ void fma_row(f32x2* acc, float w, const uint4* table, int row, int copy) {
+  const f32x2 w2 = pair_bits(__float_as_uint(w), __float_as_uint(w));
+#pragma unroll
+  for (int plane = 0; plane < PLANES; ++plane)
+    fma_unit(acc + plane * (Unit<T>::kTokens / 2), w2, table[((size_t)row * PLANES + plane) * COPIES + copy],
+             static_cast<T*>(nullptr));
+}
+
+// 8 slots from 16-byte aligned shared or global memory (the compact arrays: constants while a kernel runs).
+__device__ __forceinline__ void load_idx8(const int16_t* p, int (&i)[8]) {
+  const int4 raw = *reinterpret_cast<const int4*>(p);
   const int words[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
@@ -186,162 +216,111 @@ __device__ __forceinline__ void unpack_idx8(const int4 raw, int (&i)[8]) {
   }
 }
 
-// 8 values from 16-byte aligned memory (shared or global).
 __device__ __forceinline__ void load_val8(const float* p, float (&v)[8]) {
   const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
+
 __device__ __forceinline__ void load_val8(const __nv_bfloat16* p, float (&v)[8]) {
   Unit<__nv_bfloat16>::unpack(*reinterpret_cast<const uint4*>(p), v);
 }
 
-// Shared-memory layout of a CTA (byte offsets; every part 16-byte aligned).
-struct Layout {
-  size_t table, buffer, offs, part, windows, bars, total;
-};
-
-__host__ __device__ inline size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
-
-template <int PLANES>
-__host__ __device__ inline Layout layout(int rows_in, int copies, int buffer) {
-  Layout l;
-  l.table = 0;
-  l.buffer = align16((size_t)rows_in * PLANES * copies * 16);
-  l.offs = l.buffer + (size_t)buffer;
-  l.part = l.offs + align16((size_t)(kMaxRowsPerCta + 1) * 4);
-  l.windows = l.part + (size_t)kWarps * 8 * 4;
-  l.bars = l.windows + align16(2 * sizeof(Window));
-  l.total = l.bars + 2 * 8;
-  return l;
-}
-
-// Bytes a window of elements [e0, e1) takes in the buffer: each array's 16-byte aligned cover of the range.
-__device__ __forceinline__ int64_t window_bytes(int64_t e0, int64_t e1, int elem) {
-  return (((2 * e1 + 15) & ~int64_t(15)) - ((2 * e0) & ~int64_t(15))) +
-         (((elem * e1 + 15) & ~int64_t(15)) - ((elem * e0) & ~int64_t(15)));
-}
-
-template <typename T, int PLANES, bool kUp, bool kStoreZ>
-__global__ void __launch_bounds__(kThreads, 2) window_kernel(const Params p) {
+template <typename T, int PLANES, int COPIES, bool kUp, bool kStoreZ>
+__global__ void __launch_bounds__(kThreads, 1) gather_kernel(const Params p) {
   constexpr int NT = Unit<T>::kTokens * PLANES;
   constexpr int E = (int)sizeof(T);
   extern __shared__ __align__(16) unsigned char smem[];
-  const Layout L = layout<PLANES>(p.rows_in, p.copies, p.buffer);
-  uint4* table = reinterpret_cast<uint4*>(smem + L.table);
-  unsigned char* buffer = smem + L.buffer;
-  int32_t* offs = reinterpret_cast<int32_t*>(smem + L.offs);
-  float* part = reinterpret_cast<float*>(smem + L.part);
-  Window* windows = reinterpret_cast<Window*>(smem + L.windows);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  const size_t table_bytes = (size_t)p.rows_in * PLANES * COPIES * 16;
+  uint4* table = reinterpret_cast<uint4*>(smem);                                   // [rows_in][PLANES][COPIES]
+  float* part = reinterpret_cast<float*>(smem + table_bytes);                      // [2][kWarps][NT]
+  int32_t* offs = reinterpret_cast<int32_t*>(smem + table_bytes + kPartBytes);     // off[r0 .. r1]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + table_bytes + kPartBytes + kOffsBytes);
+  Staged* staged = reinterpret_cast<Staged*>(bar + 2);
+  unsigned char* buffer = smem + table_bytes + kHeaderBytes;
+  const T* val = static_cast<const T*>(p.val);
 
   const int r0 = (int)((int64_t)p.rows_out * blockIdx.x / gridDim.x);
   const int r1 = (int)((int64_t)p.rows_out * (blockIdx.x + 1) / gridDim.x);
   for (int r = threadIdx.x; r <= r1 - r0; r += kThreads) offs[r] = __ldg(p.off + r0 + r);
   if (threadIdx.x == 0) {
-    mbar_init(&bars[0]);
-    mbar_init(&bars[1]);
-  }
-  __syncthreads();
-
-  // Producer (thread 0). The CTA's whole range is one window in the whole buffer when it fits; otherwise row-aligned
-  // windows of at most half the buffer alternate between its two halves (slot s at s x buffer / 2), two in flight.
-  // issue(s) stages the next window from row `next` into slot s and always arrives once on the slot's barrier.
-  const int64_t nnz = __ldg(p.off + p.rows_out);
-  const bool whole = window_bytes(offs[0], offs[r1 - r0], E) <= p.buffer;
-  const int capacity = whole ? p.buffer : p.buffer / 2;
-  int next = r0;
-  auto issue = [&](int s) {
-    Window w{next, next, 0, 0, 0, 0, 0, 0};
-    int rb = next;
-    while (rb < r1 && window_bytes(offs[next - r0], offs[rb + 1 - r0], E) <= capacity) ++rb;
-    if (rb == next && next < r1) rb = next + 1;            // a row larger than a slot: read from global memory
-    w.rb = rb;
-    uint32_t bytes = 0;
-    const int64_t e0 = offs[next - r0], e1 = offs[rb - r0];
-    if (rb > next && window_bytes(e0, e1, E) <= capacity) {
+    Staged st{0, 0, 0, 0, 0};
+    if (r1 > r0) {
+      const int64_t e0 = __ldg(p.off + r0), e1 = __ldg(p.off + r1), nnz = __ldg(p.off + p.rows_out);
       const int64_t ia = (2 * e0) & ~int64_t(15), ib = min((2 * e1 + 15) & ~int64_t(15), (2 * nnz) & ~int64_t(15));
       const int64_t va = (E * e0) & ~int64_t(15), vb = min((E * e1 + 15) & ~int64_t(15), (E * nnz) & ~int64_t(15));
-      const int at = whole ? 0 : s * capacity;
-      w.idx_at = at;
-      w.val_at = at + (int)max(int64_t(0), ib - ia);
-      w.i0 = (int)(ia / 2);
-      w.i1 = (int)(max(ia, ib) / 2);
-      w.v0 = (int)(va / E);
-      w.v1 = (int)(max(va, vb) / E);
-      // the slot's previous contents were read through the generic proxy: order those reads before the async copies
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      bytes = (uint32_t)(max(int64_t(0), ib - ia) + max(int64_t(0), vb - va));
-      windows[s] = w;
-      mbar_arrive_expect(&bars[s], bytes);
-      if (ib > ia) bulk_copy(buffer + w.idx_at, reinterpret_cast<const char*>(p.idx) + ia, (uint32_t)(ib - ia), &bars[s]);
-      if (vb > va)
-        bulk_copy(buffer + w.val_at, static_cast<const char*>(p.val) + va, (uint32_t)(vb - va), &bars[s]);
-    } else {
-      windows[s] = w;
-      mbar_arrive_expect(&bars[s], 0);
+      if (ib > ia && vb > va && (ib - ia) + (vb - va) <= p.buffer) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        st = Staged{(int)(ia / 2), (int)(ib / 2), (int)(va / E), (int)(vb / E), (int)(ib - ia)};
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                     "r"((uint32_t)((ib - ia) + (vb - va)))
+                     : "memory");
+        bulk_copy(buffer, reinterpret_cast<const char*>(p.idx) + ia, (uint32_t)(ib - ia), bar);
+        bulk_copy(buffer + st.val_at, static_cast<const char*>(p.val) + va, (uint32_t)(vb - va), bar);
+      } else {
+        prefetch_l2(p.idx, e0 * 2, e1 * 2);
+        prefetch_l2(p.val, e0 * E, e1 * E);
+      }
     }
-    next = rb;
-  };
-  if (threadIdx.x == 0) {
-    issue(0);
-    if (!whole) issue(1);
-    if (next < r1) {                                        // the rest of the CTA's range: on its way to L2
-      prefetch_l2(p.idx, 2 * (int64_t)offs[next - r0], 2 * (int64_t)offs[r1 - r0]);
-      prefetch_l2(p.val, E * (int64_t)offs[next - r0], E * (int64_t)offs[r1 - r0]);
-    }
+    *staged = st;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (p.hint[h] != nullptr)
+        prefetch_l2(p.hint[h], p.hint_bytes[h] * blockIdx.x / gridDim.x, p.hint_bytes[h] * (blockIdx.x + 1) / gridDim.x);
   }
   allow_dependents();
   wait_for_predecessor();   // the table (x or act) is written by the preceding kernel
+  if (r1 <= r0) return;
 
-  if (r1 > r0) {
-    const int units = p.rows_in * PLANES;
-    for (int u = threadIdx.x; u < units; u += kThreads) {
-      const int row = PLANES == 1 ? u : u >> 1, plane = PLANES == 1 ? 0 : u & 1;
-      const uint4 v = load_unit<T, kUp>(p, row, plane);
-      uint4* line = table + (size_t)u * p.copies;
-      for (int c = 0; c < p.copies; ++c) line[(c + threadIdx.x) & (p.copies - 1)] = v;
-    }
+  for (int u = threadIdx.x; u < p.rows_in * PLANES; u += kThreads) {
+    const int row = PLANES == 1 ? u : u >> 1, plane = PLANES == 1 ? 0 : u & 1;
+    const uint4 v = load_unit<T, kUp>(p, row, plane);
+    uint4* line = table + (size_t)u * COPIES;
+#pragma unroll
+    for (int c = 0; c < COPIES; ++c) line[(c + threadIdx.x) & (COPIES - 1)] = v;
   }
   __syncthreads();
+  const Staged st = *staged;
+  if (st.i1 > 0) {                     // the CTA's slots are on their way into shared memory
+    const bool failed = !mbar_wait(bar, 0);
+    if (__syncthreads_or(failed)) {
+      if (threadIdx.x == 0) {
+        atomicCAS(&g_decode_error, 0, kErrDecodeTimeout);
+        mbar_wait(bar, 0);             // the copies land in this CTA's shared memory: let them finish (bounded)
+      }
+      return;
+    }
+  }
+  const int16_t* sidx = reinterpret_cast<const int16_t*>(buffer) - st.i0;   // indexed by slot
+  const T* sval = reinterpret_cast<const T*>(buffer + st.val_at) - st.v0;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int copy = lane & (p.copies - 1);
-  const T* val = static_cast<const T*>(p.val);
-  const int slots = whole ? 1 : 2;
-  bool failed = false;
-  for (int k = 0; r1 > r0; ++k) {
-    const int s = k % slots;
-    failed = !mbar_wait(&bars[s], (k / slots) & 1);
-    if (__syncthreads_or(failed)) {
-      failed = true;
-      break;
-    }
-    const Window w = windows[s];
-    if (w.ra >= w.rb) break;
-    const int16_t* sidx = reinterpret_cast<const int16_t*>(buffer + w.idx_at) - w.i0;   // indexed by element
-    const T* sval = reinterpret_cast<const T*>(buffer + w.val_at) - w.v0;
-    const int rows = w.rb - w.ra;
-    int split = 1;
-    while (split < kWarps && rows * split * 2 <= kWarps) split <<= 1;
-    const int per_pass = kWarps / split;
-    const int group = warp / split, member = warp - group * split;
-    const int glane = member * 32 + lane, stride = 8 * 32 * split;
-    for (int base = w.ra; base < w.rb; base += per_pass) {   // uniform over the CTA
-      const int row = base + group;
-      float acc[NT];
+  const int copy = lane & (COPIES - 1);
+  const int split = p.split, per_pass = kWarps / split;
+  const int group = warp / split, member = warp - group * split;
+  const int glane = member * 32 + lane, stride = 8 * 32 * split;
+  // the rows, with the slots read from the shared-memory copy (kStaged) or from global memory (L2); in the staged
+  // walk a slot past the copied range (the last bytes of an array whose end is not 16-byte aligned) is read from
+  // global memory
+  auto walk = [&](auto staged_tag) {
+    constexpr bool kStaged = decltype(staged_tag)::value;
+    int pass = 0;
+    for (int row = r0 + group; row - group < r1; row += per_pass, ++pass) {   // uniform over the group's warps
+      f32x2 acc[NT / 2];
 #pragma unroll
-      for (int t = 0; t < NT; ++t) acc[t] = 0.f;
-      if (row < w.rb) {
+      for (int k = 0; k < NT / 2; ++k) acc[k] = 0ull;
+      if (row < r1) {
         const int begin = offs[row - r0], end = offs[row + 1 - r0];
         const int body = min(end, (begin + 7) & ~7);
         const int body_end = max(body, end & ~7);
         auto one = [&](int e) {
-          const int id = e >= w.i0 && e < w.i1 ? sidx[e] : (int)__ldg(p.idx + e);
-          const float wv = to_f(e >= w.v0 && e < w.v1 ? sval[e] : val[e]);
-          float r[NT];
-          load_row<T, PLANES>(table, p.copies, id, copy, r);
-#pragma unroll
-          for (int t = 0; t < NT; ++t) acc[t] += wv * r[t];
+          int id;
+          float w;
+          if (kStaged && e < st.i1) id = sidx[e];
+          else id = p.idx[e];
+          if (kStaged && e < st.v1) w = to_f(sval[e]);
+          else w = to_f(val[e]);
+          fma_row<T, PLANES, COPIES>(acc, w, table, id, copy);
         };
         if (begin + glane < body) one(begin + glane);
         if (body_end + glane < end) one(body_end + glane);
@@ -349,47 +328,47 @@ __global__ void __launch_bounds__(kThreads, 2) window_kernel(const Params p) {
         for (int c = body + 8 * glane; c < body_end; c += stride) {
           int iv[8];
           float wv[8];
-          unpack_idx8(c + 8 <= w.i1 ? *reinterpret_cast<const int4*>(sidx + c)
-                                    : __ldg(reinterpret_cast<const int4*>(p.idx + c)), iv);
-          load_val8(c + 8 <= w.v1 ? sval + c : val + c, wv);
+          if (kStaged && c + 8 <= st.i1) load_idx8(sidx + c, iv);
+          else load_idx8(p.idx + c, iv);
+          if (kStaged && c + 8 <= st.v1) load_val8(sval + c, wv);
+          else load_val8(val + c, wv);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float r[NT];
-            load_row<T, PLANES>(table, p.copies, iv[j], copy, r);
-#pragma unroll
-            for (int t = 0; t < NT; ++t) acc[t] += wv[j] * r[t];
-          }
+          for (int j = 0; j < 8; ++j) fma_row<T, PLANES, COPIES>(acc, wv[j], table, iv[j], copy);
         }
       }
+      float sum[NT];
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        const float v = warp_sum(acc[t]);
-        if (lane == 0) part[warp * NT + t] = v;
+      for (int k = 0; k < NT / 2; ++k) {
+        sum[2 * k] = warp_sum(pair_lo(acc[k]));
+        sum[2 * k + 1] = warp_sum(pair_hi(acc[k]));
       }
-      __syncthreads();
-      if (row < w.rb && member == 0 && lane < p.n) {
-        float v = 0.f;
-        for (int m = 0; m < split; ++m) v += part[(group * split + m) * NT + lane];
+      float mine = sum[0];                         // lane t < NT keeps the sum of token t
+#pragma unroll
+      for (int t = 1; t < NT; ++t) mine = lane == t ? sum[t] : mine;
+      if (split > 1) {   // the row's warps in warp order, through shared memory (two buffers: alternate passes)
+        float* slot = part + (size_t)(pass & 1) * kWarps * NT;
+        if (lane < NT) slot[warp * NT + lane] = mine;
+        group_barrier(1 + group, 32 * split);
+        if (member == 0 && lane < NT) {
+          mine = 0.f;
+          for (int m = 0; m < split; ++m) mine += slot[(group * split + m) * NT + lane];
+        }
+      }
+      if (row < r1 && member == 0 && lane < p.n) {   // lane t stores token t
         const float bias = to_f(static_cast<const T*>(p.bias)[row]);
         if constexpr (kUp) {
-          const float zz = bias + v;
+          const float zz = bias + mine;
           const int64_t at = (int64_t)row * p.n + lane;
           if constexpr (kStoreZ) p.z[at] = zz;
           static_cast<T*>(p.out)[at] = from_f<T>(gelu(zz));
         } else {
-          static_cast<T*>(p.out)[(int64_t)lane * p.rows_out + row] = from_f<T>(v + bias);
+          static_cast<T*>(p.out)[(int64_t)lane * p.rows_out + row] = from_f<T>(mine + bias);
         }
       }
-      __syncthreads();
     }
-    if (threadIdx.x == 0) issue(s);                          // every thread is done with slot s
-  }
-  if (failed && threadIdx.x == 0) {
-    atomicCAS(&g_decode_error, 0, kErrDecodeTimeout);
-    // copies of this CTA still in flight land in its shared memory: wait for them (bounded) before the CTA retires
-    for (int s = 0; s < 2; ++s)
-      for (int parity = 0; parity < 2; ++parity) mbar_wait(&bars[s], parity);
-  }
+  };
+  if (st.i1 > 0) walk(std::true_type{});
+  else walk(std::false_type{});
 }
 
 static int sm_count(int device) {   // device < kMaxDevices (checked by the caller)
@@ -402,14 +381,15 @@ static int sm_count(int device) {   // device < kMaxDevices (checked by the call
   return c;
 }
 
-template <typename T, int PLANES, bool kUp, bool kZ>
-static int launch(const Params& p, size_t smem, int grid, int device, cudaStream_t s, const char* what) {
+template <typename T, int PLANES, int COPIES, bool kUp, bool kZ>
+static int launch(const Params& p, int grid, int device, cudaStream_t s, const char* what) {
   static std::atomic<uint64_t> opted_in{0};   // devices on which this kernel's shared-memory opt-in is set
-  auto kernel = window_kernel<T, PLANES, kUp, kZ>;
+  auto kernel = gather_kernel<T, PLANES, COPIES, kUp, kZ>;
+  const size_t smem = (size_t)p.rows_in * PLANES * COPIES * 16 + kHeaderBytes + p.buffer;
   const uint64_t bit = uint64_t(1) << device;
   cudaError_t e = cudaSuccess;
-  if (!(opted_in.load(std::memory_order_relaxed) & bit)) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (smem > 48 * 1024 && !(opted_in.load(std::memory_order_relaxed) & bit)) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTotal);
     if (e != cudaSuccess) {
       set_error("%s: %s", what, cudaGetErrorString(e));
       return HFFN_ERR_CUDA;
@@ -434,24 +414,39 @@ static int launch(const Params& p, size_t smem, int grid, int device, cudaStream
   return HFFN_OK;
 }
 
-// Shape the launch (grid, table copies, window buffer) within the budget and run it; kNotApplicable when it does not
-// fit. The largest copy count (up to max_copies) that leaves at least kMinBuffer; the buffer takes the rest of the
-// budget. Each CTA stages its whole share as one window when it fits the buffer (C4: up 57 KB of a 58 KB buffer with
-// two copies of x; down 57 KB of a 60 KB buffer beside act), else row-aligned windows of half the buffer.
+// Largest power-of-two copy count (<= max_copies) whose table fits the budget; 0 if one copy does not fit.
+static int copies_for(int rows_in, int planes, int max_copies) {
+  for (int c = max_copies; c >= 1; c >>= 1)
+    if ((size_t)rows_in * planes * c * 16 + kHeaderBytes <= kBudget) return c;
+  return 0;
+}
+
+// Warps per row: a power of two, as many as the CTA's share of rows leaves idle warps for.
+static int split_for(int rows_out, int grid) {
+  const int rows_per_cta = (rows_out + grid - 1) / grid;
+  int split = 1;
+  while (split < kWarps && rows_per_cta * split * 2 <= kWarps) split <<= 1;
+  return split;
+}
+
 template <typename T, int PLANES, bool kUp, bool kZ>
-static int plan_and_launch(Params p, size_t budget, int max_copies, cudaStream_t s, const char* what) {
+static int run(Params p, int max_copies, cudaStream_t s, const char* what) {
+  const int copies = copies_for(p.rows_in, PLANES, max_copies);
+  if (copies == 0) return kNotApplicable;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return kNotApplicable;
   const int grid = std::min(sm_count(device), p.rows_out);
   if ((p.rows_out + grid - 1) / grid > kMaxRowsPerCta) return kNotApplicable;
-  for (int copies = max_copies; copies >= 1; copies >>= 1) {
-    const size_t fixed = layout<PLANES>(p.rows_in, copies, 0).total;
-    if (fixed + kMinBuffer > budget) continue;
-    p.copies = copies;
-    p.buffer = (int)((budget - fixed) & ~size_t(31));
-    return launch<T, PLANES, kUp, kZ>(p, layout<PLANES>(p.rows_in, copies, p.buffer).total, grid, device, s, what);
+  p.copies = copies;
+  p.split = split_for(p.rows_out, grid);
+  const size_t fixed = (size_t)p.rows_in * PLANES * copies * 16 + kHeaderBytes;
+  p.buffer = fixed < kTotal ? (int)((kTotal - fixed) & ~size_t(15)) : 0;
+  switch (copies) {
+    case 8: return launch<T, PLANES, 8, kUp, kZ>(p, grid, device, s, what);
+    case 4: return launch<T, PLANES, 4, kUp, kZ>(p, grid, device, s, what);
+    case 2: return launch<T, PLANES, 2, kUp, kZ>(p, grid, device, s, what);
+    default: return launch<T, PLANES, 1, kUp, kZ>(p, grid, device, s, what);
   }
-  return kNotApplicable;
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -460,20 +455,23 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // The decode forms, tried by the cooperative mode at n <= 8: HFFN_OK / HFFN_ERR_CUDA when launched, kNotApplicable
 // when the shape or the alignment does not fit them (the caller then runs its general cooperative kernels).
+// `next_idx` / `next_val` (optional, `next_nnz` slots): the down projection's arrays, which the up kernel prefetches
+// into L2 for the down kernel that follows it.
 int launch_up_decode(int dtype, const void* x, const int32_t* off, const int16_t* idx, const void* w, const void* b,
-                     void* act, float* z, int d, int H, int64_t n, cudaStream_t s) {
+                     void* act, float* z, int d, int H, int64_t n, cudaStream_t s, const int16_t* next_idx,
+                     const void* next_val, int64_t next_nnz) {
   if (n < 1 || n > 8 || !dec::aligned16(idx) || !dec::aligned16(w)) return kNotApplicable;
-  dec::Params p{x, off, idx, w, b, act, z, d, H, (int)n, 1, 0, 0};
-  constexpr size_t B = dec::kUpBudget;
+  const int64_t elem = dtype == HFFN_F32 ? 4 : 2;
+  const bool hint = next_idx != nullptr && next_val != nullptr && dec::aligned16(next_idx) && dec::aligned16(next_val);
+  dec::Params p{x, off, idx, w, b, act, z, {hint ? next_idx : nullptr, hint ? next_val : nullptr},
+                {2 * next_nnz, elem * next_nnz}, d, H, (int)n, 1, 1, 0, 0};
   if (dtype == HFFN_F32) {
-    if (n <= 4)
-      return z ? dec::plan_and_launch<float, 1, true, true>(p, B, 2, s, "up_decode")
-               : dec::plan_and_launch<float, 1, true, false>(p, B, 2, s, "up_decode");
-    return z ? dec::plan_and_launch<float, 2, true, true>(p, B, 2, s, "up_decode")
-             : dec::plan_and_launch<float, 2, true, false>(p, B, 2, s, "up_decode");
+    if (n <= 4) return z ? dec::run<float, 1, true, true>(p, 8, s, "up_decode")
+                         : dec::run<float, 1, true, false>(p, 8, s, "up_decode");
+    return z ? dec::run<float, 2, true, true>(p, 8, s, "up_decode") : dec::run<float, 2, true, false>(p, 8, s, "up_decode");
   }
   if (z) return kNotApplicable;
-  return dec::plan_and_launch<__nv_bfloat16, 1, true, false>(p, B, 2, s, "up_decode");
+  return dec::run<__nv_bfloat16, 1, true, false>(p, 8, s, "up_decode");
 }
 
 int launch_down_decode(int dtype, const void* act, const int32_t* off, const int16_t* hid, const void* v,
@@ -482,13 +480,13 @@ int launch_down_decode(int dtype, const void* act, const int32_t* off, const int
   const int elem = dtype == HFFN_F32 ? 4 : 2;
   const int tokens_per_unit = 16 / elem;
   const bool vector = dec::aligned16(act) && (n == tokens_per_unit || n == 2 * tokens_per_unit);
-  dec::Params p{act, off, hid, v, bias, y, nullptr, H, d, (int)n, 1, 0, vector ? 1 : 0};
-  constexpr size_t B = dec::kDownBudget;
+  dec::Params p{act, off, hid, v, bias, y, nullptr, {nullptr, nullptr}, {0, 0}, H, d, (int)n, 1, 1, 0,
+                vector ? 1 : 0};
   if (dtype == HFFN_F32) {
-    if (n <= 4) return dec::plan_and_launch<float, 1, false, false>(p, B, 1, s, "down_decode");
-    return dec::plan_and_launch<float, 2, false, false>(p, B, 1, s, "down_decode");
+    if (n <= 4) return dec::run<float, 1, false, false>(p, 1, s, "down_decode");
+    return dec::run<float, 2, false, false>(p, 1, s, "down_decode");
   }
-  return dec::plan_and_launch<__nv_bfloat16, 1, false, false>(p, B, 1, s, "down_decode");
+  return dec::run<__nv_bfloat16, 1, false, false>(p, 1, s, "down_decode");
 }
 
 }  // namespace hffn

@@ -531,14 +531,16 @@ static int launch_down_t(int mode, const T* act, const int32_t* off, const int16
 }
 
 int launch_up_decode(int dtype, const void* x, const int32_t* off, const int16_t* idx, const void* w, const void* b,
-                     void* act, float* z, int d, int H, int64_t n, cudaStream_t s);
+                     void* act, float* z, int d, int H, int64_t n, cudaStream_t s, const int16_t* next_idx,
+                     const void* next_val, int64_t next_nnz);
 int launch_down_decode(int dtype, const void* act, const int32_t* off, const int16_t* hid, const void* v,
                        const void* bias, void* y, int d, int H, int64_t n, cudaStream_t s);
 
 int launch_up(int dtype, int mode, const void* x, const int32_t* off, const int16_t* idx, const void* w,
-              const void* b, void* act, float* z, int d, int H, int64_t n, cudaStream_t s) {
+              const void* b, void* act, float* z, int d, int H, int64_t n, cudaStream_t s, const int16_t* next_idx,
+              const void* next_val, int64_t next_nnz) {
   if (mode == HFFN_UP_COOP && n <= 8) {     // the decode kernels (decode.cu) when the shape fits them
-    const int status = launch_up_decode(dtype, x, off, idx, w, b, act, z, d, H, n, s);
+    const int status = launch_up_decode(dtype, x, off, idx, w, b, act, z, d, H, n, s, next_idx, next_val, next_nnz);
     if (status != kNotApplicable) return status;
   }
   if (dtype == HFFN_F32) {

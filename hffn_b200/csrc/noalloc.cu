@@ -20,7 +20,8 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 int launch_up(int dtype, int mode, const void* x, const int32_t* off, const int16_t* idx, const void* w,
-              const void* b, void* act, float* z, int d, int H, int64_t n, cudaStream_t s);
+              const void* b, void* act, float* z, int d, int H, int64_t n, cudaStream_t s,
+              const int16_t* next_idx = nullptr, const void* next_val = nullptr, int64_t next_nnz = 0);
 int launch_down(int dtype, int mode, const void* act, const int32_t* off, const int16_t* hid, const void* v,
                 const void* bias, void* y, int d, int H, int64_t n, cudaStream_t s);
 int64_t max_staged_rows();

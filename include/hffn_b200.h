@@ -134,9 +134,10 @@ int hffn_adamw(const hffn_param* param, const hffn_adamw_step* step, void* strea
 int hffn_mse(const float* y, const float* target, float* gy, float* loss, int64_t n, int32_t d_model, float* work,
              void* stream);
 
-/* The error flag of the decode kernels (hffn_up / hffn_down / hffn_forward in the cooperative mode at n <= 8, which
- * stage their slot windows with TMA bulk copies): 0, or the code of the first bounded wait that expired (301) on the
- * current device. Synchronous; clear != 0 resets it. No counterpart in the reference (its kernels do not wait). */
+/* The error flag of the decode kernels (the cooperative mode at n <= 8 of hffn_up / hffn_down / hffn_forward, which
+ * copy their slots into shared memory by TMA bulk copies): 0, or the code of the first bounded wait that expired
+ * (301), on the current device. Synchronous; clear != 0 resets it. No counterpart in the reference (whose kernels
+ * do not wait). */
 int hffn_decode_error(int32_t* value, int clear);
 
 /* Device-side check of a layer's arrays (offsets from 0 to nnz, non-decreasing, indices in range): sets *flag
