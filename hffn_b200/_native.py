@@ -72,6 +72,9 @@ SIGNATURES = {
     "hffn_mse": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _P, _P]),
     "hffn_validate_layout": (ctypes.c_int, [ctypes.POINTER(Layer), _P, _P]),
     "hffn_decode_error": (ctypes.c_int, [ctypes.POINTER(_I32), ctypes.c_int]),
+    "hffn_build_layout_workspace": (_I64, [_I32, _I32, _I64, _I64]),
+    "hffn_build_out_major": (ctypes.c_int, [ctypes.c_int, _I32, _I32, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _P]),
+    "hffn_build_supports": (ctypes.c_int, [_I32, _I32, _P, _P, _I64, _P, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "hffn_densify": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _I32, _I32, _P, _P, _P]),
     "hffn_up_tc": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I64, _P]),
     "hffn_down_tc": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I64, _P]),

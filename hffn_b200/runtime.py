@@ -65,7 +65,12 @@ class HFFNLayer:
 
         The up arrays are kept as given; the down slots are put in output-major order by a stable sort of their
         output feature, so that the edges of one output keep ascending neuron order, the order the reference fixes
-        (``runtime.py:55-67``); ``out_offsets`` counts the edges of each output."""
+        (``runtime.py:55-67``); ``out_offsets`` counts the edges of each output. CUDA tensors: the sort runs on their
+        device (``layout_device.out_major``, the same bits) and the layer's arrays stay there."""
+        if down_idx.is_cuda:
+            from . import layout_device
+            out_offsets, out_hidden, out_val = layout_device.out_major(d_model, d_ff, down_offsets, down_idx, down_val)
+            return cls(d_model, d_ff, b_up, up_offsets, up_idx, up_val, b_down, out_offsets, out_hidden, out_val)
         output = down_idx.long().cpu()
         order = torch.argsort(output, stable=True)
         out_offsets = torch.zeros(d_model + 1, dtype=torch.int32)

@@ -43,7 +43,12 @@ def transposed_supports(layer: HFFNLayer) -> dict[str, torch.Tensor]:
     """Up slots input-major and down edges hidden-major, as positions into the runtime's arrays (host, once).
 
     Stable sorts, so the up slots of one input keep ascending neuron order and the down edges of one neuron ascending
-    output order: the summation orders of ``gx`` and ``gz`` (``train_runtime.py:39-56`` of the reference)."""
+    output order: the summation orders of ``gx`` and ``gz`` (``train_runtime.py:39-56`` of the reference). A layer
+    whose arrays are CUDA tensors is sorted on its device (``layout_device.supports``, the same bits)."""
+    if layer.out_hidden.is_cuda:
+        from . import layout_device
+        return layout_device.supports(layer.d_model, layer.d_ff, layer.up_offsets, layer.up_idx, layer.out_offsets,
+                                      layer.out_hidden)
     up_offsets, up_idx = layer.up_offsets.cpu().long(), layer.up_idx.cpu().long()
     out_offsets, out_hidden = layer.out_offsets.cpu().long(), layer.out_hidden.cpu().long()
     up_owner = torch.repeat_interleave(torch.arange(layer.d_ff), up_offsets.diff())

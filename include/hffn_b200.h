@@ -145,6 +145,29 @@ int hffn_decode_error(int32_t* value, int clear);
  * (runtime/common/pythia/hffn_pythia/export.py:37-45) on device-resident arrays. */
 int hffn_validate_layout(const hffn_layer* layer, int32_t* flag, void* stream);
 
+/* Device-side layout build (no host sort): bytes of the workspace of hffn_build_out_major / hffn_build_supports. */
+int64_t hffn_build_layout_workspace(int32_t d_model, int32_t d_ff, int64_t nnz_up, int64_t nnz_down);
+
+/* The down edges of one layer in output-major order from its hidden-major storage: out_offsets [d_model + 1] (edges
+ * per output, prefix-summed), out_hidden [nnz_down] (the neuron of each edge) and out_val [nnz_down] (its value, in
+ * the storage type `dtype`), by a stable counting sort of down_idx on the device: the edges of one output keep
+ * ascending neuron order. Equal bit for bit to the host form, HFFNLayer.from_hidden_major
+ * (runtime/gpu/nvidia/common/kernels/hffn_cuda/runtime.py:55-67). *flag (device int32) is set to 1 if an offset or
+ * an index is out of range (those entries are skipped; the outputs are then undefined). */
+int hffn_build_out_major(int dtype, int32_t d_model, int32_t d_ff, const int32_t* down_offsets,
+                         const int16_t* down_idx, const void* down_val, int64_t nnz_down, int32_t* out_offsets,
+                         int16_t* out_hidden, void* out_val, void* work, int32_t* flag, void* stream);
+
+/* The transposed supports of the training step on the device: up slots input-major (in_offsets [d_model + 1], in_pos
+ * [nnz_up] positions into the up arrays, in_hidden [nnz_up] their neurons) and down edges hidden-major (hid_offsets
+ * [d_ff + 1], hid_pos [nnz_down] positions into the output-major arrays, hid_output [nnz_down] their outputs), by
+ * stable counting sorts: equal bit for bit to transposed_supports (runtime/gpu/nvidia/ffn/training/
+ * train_runtime.py:39-56). *flag as for hffn_build_out_major. */
+int hffn_build_supports(int32_t d_model, int32_t d_ff, const int32_t* up_offsets, const int16_t* up_idx,
+                        int64_t nnz_up, const int32_t* out_offsets, const int16_t* out_hidden, int64_t nnz_down,
+                        int32_t* in_offsets, int32_t* in_pos, int16_t* in_hidden, int32_t* hid_offsets,
+                        int32_t* hid_pos, int16_t* hid_output, void* work, int32_t* flag, void* stream);
+
 /* Dense tensor-core operands of one layer, built by hffn_densify: W_up [d_ff, d_model] and W_down [d_model, d_ff] with
  * zeros off the support. float32: the tf32 hi and lo parts of the 3xTF32 split; bfloat16: hi only (lo NULL). */
 typedef struct hffn_dense {
