@@ -85,9 +85,14 @@ def from_compact(compact) -> dict:
             "group_hidden_offsets": t(compact.groups)}
 
 
-def kernel_layer(layer: dict):
-    """The runtime's ``HFFNLayer`` of one export layer (output-major down edges)."""
+def kernel_layer(layer: dict, device=None):
+    """The runtime's ``HFFNLayer`` of one export layer (output-major down edges). With a CUDA ``device`` the arrays
+    are moved there first and the output-major order is built on the device (no host sort)."""
     from .runtime import HFFNLayer
-    return HFFNLayer.from_hidden_major(layer["d_model"], layer["d_ff"], layer["b_up"], layer["up_row_offsets"],
-                                       layer["up_idx"], layer["up_val"], layer["b_down"], layer["down_row_offsets"],
-                                       layer["down_idx"], layer["down_val"])
+    names = ("b_up", "up_row_offsets", "up_idx", "up_val", "b_down", "down_row_offsets", "down_idx", "down_val")
+    arrays = {k: layer[k] for k in names}
+    if device is not None and torch.device(device).type == "cuda":
+        arrays = {k: v.to(device) for k, v in arrays.items()}
+    return HFFNLayer.from_hidden_major(layer["d_model"], layer["d_ff"], arrays["b_up"], arrays["up_row_offsets"],
+                                       arrays["up_idx"], arrays["up_val"], arrays["b_down"], arrays["down_row_offsets"],
+                                       arrays["down_idx"], arrays["down_val"])

@@ -64,6 +64,22 @@ class ShardedHFFNMLP(nn.Module):
         return y.view(shape)
 
 
+class TrainableHFFNMLP(nn.Module):
+    """Replacement of ``block.mlp`` for training: the layer ``index`` of an ``HFFNTrainRuntime`` as a torch autograd
+    function (``HFFNFunction``): gradients flow to the model's other parameters through gx, the FFN's compact
+    gradients stay in the training runtime (``model.hffn_train``), whose ``adamw`` updates them."""
+
+    def __init__(self, train, index: int) -> None:
+        super().__init__()
+        self.train_runtime, self.index = train, index
+
+    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        from .train_runtime import HFFNFunction
+        shape = hidden_states.shape
+        y = HFFNFunction.apply(hidden_states.reshape(-1, shape[-1]).contiguous(), self.train_runtime, self.index)
+        return y.view(shape)
+
+
 def shard_layers(layers: list[dict], rank: int, world: int) -> list[dict]:
     """This rank's neuron shard of every export layer (hidden ranges balanced by edge count, multiples of 8; down
     edges restricted to the shard; ``b_down`` kept on rank 0 only): canonical hidden-major arrays."""
@@ -126,12 +142,19 @@ def _load_non_ffn(model: nn.Module, checkpoint: Path) -> None:
 
 
 def load_pythia(model_dir: str | Path, export_dir: str | Path, ffn: str, device: str | torch.device = "cuda",
-                dtype: torch.dtype = torch.float32, tensor_cores: bool | None = None, group=None) -> nn.Module:
+                dtype: torch.dtype = torch.float32, tensor_cores: bool | None = None, group=None,
+                trainable: bool = False, **train_options) -> nn.Module:
     """Pythia in eval mode (``dtype``, on ``device``) with its FFNs from ``export_dir``, executed dense or by HFFN.
 
     ``group`` (a process group of more than one rank, HFFN arm): every FFN neuron-sharded over the group's ranks
     (``ShardedHFFNMLP``), the rest of the model replicated; every rank runs the same tokens and gets the whole
-    model's output. ``model.hffn_runtimes`` holds the rank's runtimes (one per distinct shard width)."""
+    model's output. ``model.hffn_runtimes`` holds the rank's runtimes (one per distinct shard width).
+
+    ``trainable=True`` (HFFN arm, float32, one GPU): every FFN is a ``TrainableHFFNMLP`` over one
+    ``HFFNTrainRuntime`` (``model.hffn_train``; ``train_options``: its lr, betas, eps, weight_decay), the model is in
+    train mode and its other parameters require gradients: ``loss.backward()`` leaves the FFNs' compact gradients in
+    ``model.hffn_train.gradients(index)``, and ``model.hffn_train.adamw(index)`` applies them. The layers' layouts
+    are built on the device."""
     from transformers import AutoConfig, AutoModelForCausalLM
     if ffn not in ("dense", "hffn"):
         raise ValueError("ffn must be 'dense' or 'hffn'")
@@ -150,9 +173,19 @@ def load_pythia(model_dir: str | Path, export_dir: str | Path, ffn: str, device:
     if ffn == "dense":
         for block, layer in zip(blocks, layers):
             set_dense_mlp(block.mlp, layer)
+    elif trainable:
+        if dtype != torch.float32 or (group is not None and _world(group) > 1):
+            raise ValueError("trainable HFFN Pythia: float32 on one GPU")
+        from .runtime import HFFNRuntime
+        from .train_runtime import HFFNTrainRuntime
+        runtime = HFFNRuntime([export.kernel_layer(layer, device) for layer in layers], device, dtype,
+                              tensor_cores=tensor_cores)
+        model.hffn_train = HFFNTrainRuntime(runtime, **train_options)
+        for index, block in enumerate(blocks):
+            block.mlp = TrainableHFFNMLP(model.hffn_train, index)
     elif group is None or _world(group) == 1:
         from .runtime import PreparedRuntime
-        runtime = PreparedRuntime([export.kernel_layer(layer) for layer in layers], device, dtype,
+        runtime = PreparedRuntime([export.kernel_layer(layer, device) for layer in layers], device, dtype,
                                   tensor_cores=tensor_cores)
         for index, block in enumerate(blocks):
             block.mlp = HFFNMLP(runtime, index)
@@ -176,7 +209,8 @@ def load_pythia(model_dir: str | Path, export_dir: str | Path, ffn: str, device:
                 blocks[index].mlp = ShardedHFFNMLP(shard_runtime, local, group)
         runtime = runtimes[0]
         model.hffn_runtimes = runtimes
-    model = model.to(device=device, dtype=dtype).eval().requires_grad_(False)
+    model = model.to(device=device, dtype=dtype)
+    model = model.train().requires_grad_(True) if trainable else model.eval().requires_grad_(False)
     model.hffn_runtime = runtime
     if runtime is not None and not hasattr(model, "hffn_runtimes"):
         model.hffn_runtimes = [runtime]

@@ -311,6 +311,46 @@ class HFFNTrainRuntime:
         """AdamW from the stored gradients (after a data-parallel exchange); the dense operands are rebuilt lazily."""
         self.adamw(index)
 
+    # -- stacks of layers: every call keeps its own activations ---------------------------------------------------
+    def forward_saved(self, index: int, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """``(y, z, act)`` of layer ``index`` for x[N, d_model], each a new tensor (z and act hidden-major
+        ``[d_ff * N]``): the state its ``backward_saved`` needs, kept by the caller, so that a stack of layers can run
+        all its forwards first and its backwards later in reverse order (the runtime's shared work buffers serve one
+        layer at a time). The CUDA-core kernels (hidden-major activations); allocates through torch's caching
+        allocator."""
+        runtime = self.runtime
+        n = self._check_tokens(x, "x")
+        up, down = runtime.modes(n, hidden_major=True)
+        device = runtime.device
+        y = torch.empty(n, self.d_model, device=device)
+        z = torch.empty(self.d_ff * n, device=device)
+        act = torch.empty(self.d_ff * n, device=device)
+        native.check(native.lib.hffn_forward(runtime._code, runtime._structs[index], x.data_ptr(), y.data_ptr(),
+                                             act.data_ptr(), z.data_ptr(), n, native.UP_CODES[up],
+                                             native.DOWN_CODES[down], native.stream_handle(device)), "hffn_forward")
+        runtime.calls[up, down] += 1
+        self.calls[up, down] += 1
+        return y, z, act
+
+    def backward_saved(self, index: int, x: torch.Tensor, gy: torch.Tensor, z: torch.Tensor,
+                       act: torch.Tensor) -> torch.Tensor:
+        """gx[N, d_model] (a new tensor) for the upstream gradient gy of a ``forward_saved`` call (its x, z, act);
+        the layer's compact gradients (``gradients(index)``) are overwritten with this call's. ``adamw(index)``
+        applies them."""
+        runtime = self.runtime
+        n = self._check_tokens(gy, "gy")
+        if self._check_tokens(x, "x") != n or z.numel() < self.d_ff * n or act.numel() < self.d_ff * n:
+            raise ValueError("x, z and act must come from the forward of the same N tokens")
+        self._reserve_partials(n)
+        device = runtime.device
+        gz = torch.empty(self.d_ff * n, device=device)
+        gx = torch.empty(n, self.d_model, device=device)
+        native.check(native.lib.hffn_backward(runtime._structs[index], self._support_structs[index], x.data_ptr(),
+                                              gy.data_ptr(), z.data_ptr(), act.data_ptr(), gz.data_ptr(), gx.data_ptr(),
+                                              self._param_structs[index], None, self._work.data_ptr(), n,
+                                              native.stream_handle(device)), "hffn_backward")
+        return gx
+
     # -- read access for the checks (views, no copy) -------------------------------------------------------------
     def parameters(self, index: int) -> dict[str, torch.Tensor]:
         """The compact values of layer ``index`` (views: a caller may write through them, as the reference's checks
@@ -347,3 +387,22 @@ class HFFNTrainRuntime:
                                  self._supports[index].values()),
                 "workspace": self.runtime.workspace_bytes() + total((self._z, self._gz, self._gx, self._gy)),
                 "partials": total((self._work,))}
+
+
+class HFFNFunction(torch.autograd.Function):
+    """One HFFN layer as a torch autograd function: ``HFFNFunction.apply(x, train, index)`` -> y. The forward keeps
+    the call's x, z and activations for its backward (``forward_saved`` / ``backward_saved``), so stacks of layers and
+    whole models train through torch autograd; the backward returns gx and leaves the layer's compact gradients in
+    ``train.gradients(index)`` (one backward per layer between two ``train.adamw(index)``)."""
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, train: "HFFNTrainRuntime", index: int) -> torch.Tensor:
+        y, z, act = train.forward_saved(index, x.contiguous())
+        ctx.save_for_backward(x, z, act)
+        ctx.train, ctx.index = train, index
+        return y
+
+    @staticmethod
+    def backward(ctx, gy: torch.Tensor):
+        x, z, act = ctx.saved_tensors
+        return ctx.train.backward_saved(ctx.index, x.contiguous(), gy.contiguous(), z, act), None, None
