@@ -11,7 +11,8 @@ line's own fields are the headline record, the others sit under ``workloads``:
   GPU, MSE loss, backward and AdamW (data parallel over the GPUs, gradient all-reduce);
 - ``c4_decode_bf16``: 24 Pythia-410M-shape FFN layers x 8 tokens per step, the prepared decode path in a CUDA graph
   (HBM-bound; replicas when N > 1).
-Single workloads: ``--workload fwd | fwd_bf16 | c1 | train | train_small | decode | pythia410m``.
+Single workloads: ``--workload fwd | fwd_bf16 | c1 | train | train_small | decode | pythia410m | c5`` (c5: Pythia-1B
+bf16 prefill of 64 x 2048 tokens with every FFN neuron-sharded over the GPUs, the plan's 8-GPU configuration).
 
 Every record carries: ``value`` (tokens/s of the whole job, inputs resident in HBM), ``roofline`` (the dominant kernel
 against the measured peaks of ``MEASURED_PEAKS.json``), ``e2e`` (the same metric through the public API with host
@@ -63,6 +64,7 @@ WORKLOADS = {
     "pythia410m": {"case": "c4_1024_4096_k512", "n": 8 * 512, "dtype": "bf16", "batch": 8, "prompt": 512,
                    "decode": 128},
     "decode": {"case": "c4_1024_4096_k512", "n": 8, "dtype": "bf16", "layers": 24},
+    "c5": {"case": "c5_2048_8192_k410", "dtype": "bf16", "batch": 64, "prompt": 2048, "support": 410, "seed": 3005},
 }
 COMPOSITE = (("c2_fwd_fp32", "fwd"), ("c2_fwd_bf16", "fwd_bf16"), ("c1_fwd_fp32", "c1"), ("c3_train_fp32", "train"),
              ("c4_decode_bf16", "decode"))
@@ -944,6 +946,120 @@ def pythia_record(ctx: Context, name: str) -> dict | None:
             "arms_ms": results} if ctx.rank == 0 else None
 
 
+def c5_record(ctx: Context, name: str) -> dict | None:
+    """Pythia-1B architecture (random init, 20 % HFFN FFNs, bfloat16), prefill of 64 x 2048 tokens; with N ranks every
+    FFN is neuron-sharded 1/N per GPU (``load_pythia(group=...)``: the rank's shard on the tensor cores, the partial
+    outputs all-reduced over NCCL) and the rest of the model replicated, every rank running the same batch (strong
+    scaling: the job's throughput is the batch over the step). Beside the step: the shard's two FFN kernels timed alone
+    on the step's FFN input shape (the roofline), one all-reduce of an FFN output, and the parity of the sharded layer-0
+    FFN on 64 token rows against the float64 oracle of the layer as held in bf16."""
+    import tempfile
+    torch, args = ctx.torch, ctx.args
+    from hffn_b200 import pythia, synth
+    from oracle import forward64
+    workload = WORKLOADS[name]
+    rank, world, device, stream = ctx.rank, ctx.world, ctx.device, ctx.stream
+    b, t = workload["batch"], workload["prompt"]
+    arch = pythia.PYTHIA_1B
+    root = Path(tempfile.gettempdir()) / "hffn_bench_pythia1b"
+    if rank == 0 and not (root / "model" / "hffn_random_init.json").exists():
+        pythia.make_random_pythia(root / "model", root / "export", arch, support=workload["support"],
+                                  seed=workload["seed"])
+    ctx.barrier()
+    group = ctx.dist.group.WORLD if world > 1 else None
+    model = pythia.load_pythia(root / "model", root / "export", "hffn", device, torch.bfloat16, group=group)
+    prompt_host = torch.randint(0, 50277, (b, t), generator=torch.Generator().manual_seed(workload["seed"])).pin_memory()
+    prompt = prompt_host.to(device)
+    logits_host = torch.empty(b, 1, arch["vocab_size"], dtype=torch.bfloat16).pin_memory()
+
+    @torch.inference_mode()
+    def step(ids):
+        return model(input_ids=ids, use_cache=False, logits_to_keep=1).logits
+
+    for _ in range(args.warmup):
+        step(prompt)
+    marks = ctx.events(args.steps)
+    ctx.barrier()
+    with ClockSampler(ctx.local) as clocks:
+        for a, e in marks:
+            a.record(stream)
+            step(prompt)
+            e.record(stream)
+        torch.cuda.synchronize(device)
+    step_ms = [a.elapsed_time(e) for a, e in marks]
+    e2e = []
+    for _ in range(args.steps):               # token ids in from pinned host memory, last-position logits back
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        prompt.copy_(prompt_host, non_blocking=True)
+        logits_host.copy_(step(prompt), non_blocking=True)
+        e.record(stream)
+        e.synchronize()
+        e2e.append(a.elapsed_time(e))
+    # the rank's FFN kernels alone (layer 0's runtime, the step's FFN input shape), and one all-reduce of its output
+    runtime = model.hffn_runtime
+    x = torch.randn(b * t, arch["hidden_size"], generator=torch.Generator().manual_seed(7)).to(device, torch.bfloat16)
+    runtime.forward(0, x)
+    kernel_ms, reduce_ms = [], []
+    for _ in range(3):
+        a, m, e = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        a.record(stream)
+        y = runtime.forward(0, x)
+        m.record(stream)
+        if world > 1:
+            ctx.dist.all_reduce(y, op=ctx.dist.ReduceOp.SUM)
+        e.record(stream)
+        e.synchronize()
+        kernel_ms.append(a.elapsed_time(m))
+        reduce_ms.append(m.elapsed_time(e))
+    # parity: the (sharded) layer-0 FFN on 64 rows against the float64 oracle of the layer as held in bf16
+    case0 = synth.Case("pythia_layer0", arch["hidden_size"], arch["intermediate_size"], workload["support"],
+                       workload["support"], False, workload["seed"], 0.02)
+    rows = torch.randn(PARITY_ROWS, arch["hidden_size"], generator=torch.Generator().manual_seed(11)).to(torch.bfloat16)
+    with torch.inference_mode():
+        y_rows = model.gpt_neox.layers[0].mlp(rows.to(device).unsqueeze(0)).squeeze(0).float().cpu().numpy()
+    error = relative_error(y_rows, forward64.forward(bf16_held(synth.make_layer(case0), torch), rows.float().numpy())) \
+        if rank == 0 else 0.0
+    total_s, e2e_s, kernel_s, reduce_s, error = ctx.max_over_ranks(
+        [sum(step_ms) / 1e3, statistics.median(e2e) / 1e3, statistics.median(kernel_ms) / 1e3,
+         statistics.median(reduce_ms) / 1e3, error])
+    errors = runtime.device_errors()
+    ctx.barrier()
+    if rank != 0:
+        return None
+    pk, pk_source = peaks()
+    shard_edges = sum(int(s.numel()) for s in (runtime._tensors[0]["up_val"], runtime._tensors[0]["out_val"]))
+    flops = 2.0 * shard_edges * b * t                       # useful: 2 per edge per token, both projections
+    achieved = flops / kernel_s / 1e12
+    tokens = b * t
+    return {
+        "metric": "Pythia-1B (20 % HFFN FFNs, bf16) prefill tokens/s: 64 x 2048 tokens, FFNs neuron-sharded over the GPUs",
+        "value": tokens * args.steps / total_s, "unit": "tokens/s", "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total_s / args.steps, "dtype": "bf16", "scaling": "strong",
+        "config": {"workload": f"pythia-1b architecture (random init), {arch['num_hidden_layers']} layers, d_model "
+                               f"{arch['hidden_size']}, d_ff {arch['intermediate_size']}, {workload['support']}-of-"
+                               f"{arch['hidden_size']} supports; prefill {b} x {t}, last-position logits",
+                   "parallelism": "single" if world == 1 else
+                   f"every FFN neuron-sharded 1/{world} per GPU, partial outputs all-reduced over NCCL; attention, "
+                   f"embeddings and head replicated", "l2": "inputs larger than L2 (hidden states 537 MB per layer)"},
+        "roofline": {"bound": "tensor", "kernel": "the rank's FFN shard (tc_gemm up + down, layer 0, the step's shape)",
+                     "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / pk["bf16_tflops"], "traffic": None, "launch_ms": kernel_s * 1e3,
+                     "peak_source": pk_source, "note": "useful sparse FLOPs (2 per edge per token) of measured dense "
+                                                       "bf16 burst; the dense tiles execute 1 / density of that"},
+        "all_reduce": {"ms": reduce_s * 1e3, "bytes": tokens * arch["hidden_size"] * 2,
+                       "bus_gbs": (2 * (world - 1) / world * tokens * arch["hidden_size"] * 2 / reduce_s / 1e9)
+                       if world > 1 else None},
+        "ffn_ms_per_step": (kernel_s + reduce_s) * 1e3 * arch["num_hidden_layers"],
+        "e2e": {"value": tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": prompt_host.numel() * 8,
+                "d2h_bytes_per_step": logits_host.numel() * 2},
+        "parity": {"max_rel": error, "bound": BF16_RELATIVE, "ok": error <= BF16_RELATIVE,
+                   "against": "float64 oracle of layer 0 (as held in bf16) on 64 token rows, through the sharded FFN"},
+        "gpu_launches": 2 * arch["num_hidden_layers"] * args.steps, "device_errors": errors,
+        "clocks": clocks.summary(),
+    }
+
+
 # -- driver ------------------------------------------------------------------------------------------------------------
 def single(ctx: Context, name: str) -> dict | None:
     args = ctx.args
@@ -953,6 +1069,8 @@ def single(ctx: Context, name: str) -> dict | None:
         return decode_record(ctx, name, 0 if args.no_cpu_baseline else args.cpu_seconds / 2)
     if name == "pythia410m":
         return pythia_record(ctx, name)
+    if name == "c5":
+        return c5_record(ctx, name)
     return forward_record(ctx, name, 0 if args.no_cpu_baseline else args.cpu_seconds)
 
 
@@ -960,7 +1078,8 @@ def finish(ctx: Context, record: dict) -> dict:
     """The line's contract fields around a record."""
     line = {"metric": record["metric"], "value": record["value"], "unit": record["unit"], "n_gpus": ctx.world,
             "steps": record["steps"], "warmup": record["warmup"], "ms_per_step": record.get("ms_per_step"),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": record["dtype"],
+            "higher_is_better": True, "scaling": record.get("scaling", "weak"), "vs_baseline": None,
+            "dtype": record["dtype"],
             "data": "synthetic (seeded supports, weights and inputs of the benchmark plan's shapes)"}
     line.update({k: v for k, v in record.items() if k not in line})
     return line
