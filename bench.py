@@ -10,7 +10,9 @@ line's own fields are the headline record, the others sit under ``workloads``:
 - ``c3_train_fp32``: the training step, d_model 2048, d_ff 8192, 1638-of-2048 supports (80 %), N = 8192 tokens per
   GPU, MSE loss, backward and AdamW (data parallel over the GPUs, gradient all-reduce);
 - ``c4_decode_bf16``: 24 Pythia-410M-shape FFN layers x 8 tokens per step, the prepared decode path in a CUDA graph
-  (HBM-bound; replicas when N > 1).
+  (HBM-bound; replicas when N > 1);
+- ``c5_pythia1b_bf16``: the Pythia-1B architecture (random init, 20 % HFFN FFNs, bf16), prefill of 64 x 2048 tokens,
+  every FFN neuron-sharded over the N GPUs (strong scaling: the same batch at every N).
 Single workloads: ``--workload fwd | fwd_bf16 | c1 | train | train_small | decode | pythia410m | c5`` (c5: Pythia-1B
 bf16 prefill of 64 x 2048 tokens with every FFN neuron-sharded over the GPUs, the plan's 8-GPU configuration).
 
@@ -67,7 +69,7 @@ WORKLOADS = {
     "c5": {"case": "c5_2048_8192_k410", "dtype": "bf16", "batch": 64, "prompt": 2048, "support": 410, "seed": 3005},
 }
 COMPOSITE = (("c2_fwd_fp32", "fwd"), ("c2_fwd_bf16", "fwd_bf16"), ("c1_fwd_fp32", "c1"), ("c3_train_fp32", "train"),
-             ("c4_decode_bf16", "decode"))
+             ("c4_decode_bf16", "decode"), ("c5_pythia1b_bf16", "c5"))
 # DRAM bytes (read + write) per launch of the dominant kernel from one `ncu --set full` capture of the same workload
 # on a B200 (dram__bytes_read.sum + dram__bytes_write.sum); the command and the figures are in the named summary under
 # profiles/. Keyed by (workload, kernel); a kernel without a capture reports null.
