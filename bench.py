@@ -72,10 +72,10 @@ COMPOSITE = (("c2_fwd_fp32", "fwd"), ("c2_fwd_bf16", "fwd_bf16"), ("c1_fwd_fp32"
              ("c4_decode_bf16", "decode"), ("c5_pythia1b_bf16", "c5"))
 # DRAM bytes (read + write) per launch of the dominant kernel from one `ncu --set full` capture of the same workload
 # on a B200 (dram__bytes_read.sum + dram__bytes_write.sum); the command and the figures are in the named summary under
-# profiles/. Keyed by (workload, kernel); a kernel without a capture reports null.
+# profiles/. Keyed by (workload, kernel, operand format); a kernel without a capture reports null.
 NCU_TRAFFIC = {
-    ("fwd", "tc_gemm_up"): (142.489e6 + 96.618e6, "profiles/fwd_tensor_cores_c2_fp32.md"),
-    ("fwd_bf16", "tc_gemm_up"): (16.834e6 + 0.433e6, "profiles/fwd_tensor_cores_c2_bf16.md"),
+    ("fwd", "tc_gemm_up", "tf32x3"): (142.489e6 + 96.618e6, "profiles/fwd_tensor_cores_c2_fp32.md"),
+    ("fwd_bf16", "tc_gemm_up", "bf16"): (16.834e6 + 0.433e6, "profiles/fwd_tensor_cores_c2_bf16.md"),
 }
 CLOCK_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
                "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -376,12 +376,14 @@ def forward_record(ctx: Context, name: str, cpu_seconds: float) -> dict | None:
     layer = synth.make_layer(case)
     tensor_cores = False if args.path == "cuda_cores" else None
     if world == 1:
-        runtime = HFFNRuntime([kernel_layer(layer, torch)], device, dtype, tensor_cores=tensor_cores)
+        runtime = HFFNRuntime([kernel_layer(layer, torch)], device, dtype, tensor_cores=tensor_cores,
+                              tc_format=args.tc_format if dtype == torch.float32 else None)
         shard, (lo, hi) = None, (0, case.d_ff)
     else:
         runtime, shard, (lo, hi) = sharded_runtime(case.d_model, canonical(layer, torch), device, dtype,
                                                    tensor_cores=tensor_cores, segments=args.segments,
-                                                   comm_sms=args.comm_sms, transport=args.transport, push=args.push)
+                                                   comm_sms=args.comm_sms, transport=args.transport, push=args.push,
+                                                   tc_format=args.tc_format if dtype == torch.float32 else None)
     if args.path == "tensor_cores":
         runtime.force("tc", "tc")
     d, f_local = case.d_model, hi - lo
@@ -397,8 +399,9 @@ def forward_record(ctx: Context, name: str, cpu_seconds: float) -> dict | None:
     tc = up == "tc"
     ptr = lambda v: None if v is None else v.data_ptr()  # noqa: E731
     if tc:
+        tc_format, dense_struct = runtime.forward_operands(0)
         dense, work, err = runtime._dense[0], runtime._tc_work.data_ptr(), runtime._err.data_ptr()
-        if dtype == torch.float32:
+        if tc_format == "tf32x3":
             x_split, act_hi = work, work + 2 * n_kernel * d * 4
             act_lo = act_hi + n_kernel * f_local * 4
         else:
@@ -406,6 +409,13 @@ def forward_record(ctx: Context, name: str, cpu_seconds: float) -> dict | None:
 
     def kernels(marks):
         """The two kernels of one forward of the local runtime over x_all, an event between them."""
+        if tc and tc_format == "f16x3":
+            native.check(native.lib.hffn_up_f16x3(x_all.data_ptr(), dense_struct, struct.b_up, None, work, err, d,
+                                                  f_local, n_kernel, handle), "hffn_up_f16x3")
+            marks[1].record(stream)
+            native.check(native.lib.hffn_down_f16x3(work, dense_struct, struct.b_down, runtime._y.data_ptr(), err, d,
+                                                    f_local, n_kernel, handle), "hffn_down_f16x3")
+            return
         if tc:
             native.check(native.lib.hffn_up_tc(code, x_all.data_ptr(), ptr(dense["up_hi"]), ptr(dense["up_lo"]),
                                                struct.b_up, act_hi, act_lo, None, x_split, err, d, f_local,
@@ -544,18 +554,21 @@ def forward_record(ctx: Context, name: str, cpu_seconds: float) -> dict | None:
     if tc:
         passes = 3 if elem == 4 else 1
         dense_flops = 2.0 * n_kernel * f_local * d * passes
-        pipe_peak = gemm["tf32_tflops"] if elem == 4 else pk["bf16_tflops"]
-        traffic, traffic_source = NCU_TRAFFIC.get((name, f"tc_gemm_{top}"), (None, None)) \
+        tf32 = tc_format == "tf32x3"
+        pipe_peak = gemm["tf32_tflops"] if tf32 else pk["bf16_tflops"]
+        traffic, traffic_source = NCU_TRAFFIC.get((name, f"tc_gemm_{top}", tc_format), (None, None)) \
             if world == 1 else (None, None)
         roofline = {"bound": "tensor", "kernel": f"tc_gemm_{top}", "achieved": achieved_tflops,
                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved_tflops / pk["bf16_tflops"],
                     "traffic": traffic, "traffic_source": traffic_source,
                     "algorithmic_flops": alg[top]["flops"], "launch_ms": kernel_ms[top], "peak_source": pk_source,
                     "note": "useful sparse FLOPs (2 per edge per token) of measured dense bf16 burst",
-                    "tensor_pipe": {"kind": "tf32 x3 (3xTF32 split)" if elem == 4 else "bf16",
+                    "tensor_pipe": {"kind": {"tf32x3": "tf32 x3 (3xTF32 split)",
+                                             "f16x3": "f16 x3 (scaled fp16 hi / lo split, three products)",
+                                             "bf16": "bf16"}[tc_format],
                                     "executed_tflops": dense_flops / seconds / 1e12, "peak_tflops": pipe_peak,
-                                    "peak_source": gemm["source"] + ", TF32 on" if elem == 4 else
-                                    "MEASURED_PEAKS.json bf16 burst",
+                                    "peak_source": gemm["source"] + ", TF32 on" if tf32 else
+                                    "MEASURED_PEAKS.json dense bf16 burst (the f16 rate)",
                                     "frac": dense_flops / seconds / 1e12 / pipe_peak},
                     "hbm": hbm}
         launches = 3 if elem == 4 else 2
@@ -1103,6 +1116,8 @@ def main() -> int:
                         help="sharded forward: NCCL collectives or NVLink peer memory (tensor cores)")
     parser.add_argument("--push", choices=("copy", "store"), default="copy",
                         help="peer sharded forward: partial outputs pushed by copy engines or by the GEMM epilogue")
+    parser.add_argument("--tc-format", choices=("f16x3", "tf32x3"), default=None,
+                        help="operand format of the float32 tensor-core forward (default: f16x3)")
     parser.add_argument("--path", choices=("auto", "cuda_cores", "tensor_cores"), default="auto",
                         help="forward kernels: the runtime policy, the CUDA-core gather kernels, or the tcgen05 path")
     args = parser.parse_args()

@@ -50,6 +50,11 @@ class Dense(ctypes.Structure):
     _fields_ = [("up_hi", _P), ("up_lo", _P), ("down_hi", _P), ("down_lo", _P)]
 
 
+class DenseF16x3(ctypes.Structure):
+    _fields_ = [("up_hi", _P), ("up_lo", _P), ("up_scale", _P), ("down_hi", _P), ("down_lo", _P), ("down_scale", _P),
+                ("up_bound", _P)]
+
+
 class AdamWStep(ctypes.Structure):
     _fields_ = [(name, ctypes.c_float) for name in
                 ("lr_decay", "beta1", "one_minus_beta1", "beta2", "one_minus_beta2", "step_size", "bias2_sqrt", "eps")]
@@ -97,6 +102,12 @@ SIGNATURES = {
                                           _I64, _P]),
     "hffn_forward_noalloc_max_bytes": (_I64, []),
     "hffn_forward_noalloc": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(Layer), _P, _P, _I64, _P]),
+    "hffn_densify_f16x3": (ctypes.c_int, [_P, _P, _P, _P, _I32, _I32, _P, _P, _P, _P, _P]),
+    "hffn_forward_f16x3_workspace": (_I64, [ctypes.POINTER(Layer), _I64]),
+    "hffn_forward_f16x3": (ctypes.c_int, [ctypes.POINTER(Layer), ctypes.POINTER(DenseF16x3), _P, _P, _P, _P, _P, _I64,
+                                          _P]),
+    "hffn_up_f16x3": (ctypes.c_int, [_P, ctypes.POINTER(DenseF16x3), _P, _P, _P, _P, _I32, _I32, _I64, _P]),
+    "hffn_down_f16x3": (ctypes.c_int, [_P, ctypes.POINTER(DenseF16x3), _P, _P, _P, _I32, _I32, _I64, _P]),
     "hffn_forward_tc_workspace": (_I64, [ctypes.c_int, ctypes.POINTER(Layer), _I64]),
     "hffn_forward_tc": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(Layer), ctypes.POINTER(Dense), _P, _P, _P, _P, _P,
                                        _I64, _P]),

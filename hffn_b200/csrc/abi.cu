@@ -43,6 +43,13 @@ int tc_down(int dtype, const void* act_hi, const void* act_lo, const void* w_hi,
             void* y, int* err, int d, int H, int64_t n, cudaStream_t s);
 int tc_densify(int dtype, const int32_t* off, const int16_t* idx, const void* val, int rows, int cols, void* hi,
                void* lo, cudaStream_t s);
+int64_t tc_f16_workspace(int d, int H, int64_t n);
+int tc_up_f16(const float* x, const hffn_dense_f16x3* D, const float* b, float* z, void* work, int* err, int d, int H,
+              int64_t n, cudaStream_t s);
+int tc_down_f16(const void* work, const hffn_dense_f16x3* D, const float* b, float* y, int* err, int d, int H,
+                int64_t n, cudaStream_t s);
+int tc_densify_f16(const int32_t* off, const int16_t* idx, const float* val, const float* bias, int rows, int cols,
+                   void* hi, void* lo, float* scale, float* bound, cudaStream_t s);
 
 static thread_local char g_error[512] = "";
 
@@ -248,6 +255,64 @@ static int check_tc(int dtype, int32_t d_model, int32_t d_ff, int64_t n) {
   HFFN_REQUIRE(n <= (int64_t(1) << 31) - 1, "token count beyond 2^31 - 1");
   HFFN_REQUIRE(d_model % 8 == 0 && d_ff % 8 == 0, "tensor-core path: d_model and d_ff multiples of 8");
   return HFFN_OK;
+}
+
+int hffn_densify_f16x3(const int32_t* offsets, const int16_t* idx, const float* val, const float* bias, int32_t rows,
+                       int32_t cols, void* hi, void* lo, float* scale, float* bound, void* stream) {
+  HFFN_REQUIRE(rows >= 1 && cols >= 1 && rows <= 32767 && cols <= 32767, "dense shape out of range");
+  HFFN_REQUIRE(offsets && idx && val && hi && lo && scale, "null pointer argument");
+  HFFN_REQUIRE(bias == nullptr || bound != nullptr, "a bias needs the bound it feeds");
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_densify_f16(offsets, idx, val, bias, rows, cols, hi, lo, scale, bound, static_cast<cudaStream_t>(stream));
+}
+
+int64_t hffn_forward_f16x3_workspace(const hffn_layer* layer, int64_t n) {
+  if (layer == nullptr || n < 1) return -1;
+  return tc_f16_workspace(layer->d_model, layer->d_ff, n);
+}
+
+static int check_dense_f16(const hffn_dense_f16x3* D, bool up, bool down) {
+  HFFN_REQUIRE(D != nullptr, "null dense operands");
+  HFFN_REQUIRE(!up || (D->up_hi && D->up_lo && D->up_scale && D->up_bound), "null up operand");
+  HFFN_REQUIRE(!down || (D->down_hi && D->down_lo && D->down_scale), "null down operand");
+  HFFN_REQUIRE((!up || (aligned16(D->up_hi) && aligned16(D->up_lo))) &&
+                   (!down || (aligned16(D->down_hi) && aligned16(D->down_lo))),
+               "tensor-core operands must be 16-byte aligned");
+  return HFFN_OK;
+}
+
+int hffn_up_f16x3(const float* x, const hffn_dense_f16x3* dense, const float* b_up, float* z, void* work, int32_t* err,
+                  int32_t d_model, int32_t d_ff, int64_t n, void* stream) {
+  HFFN_TRY(check_tc(HFFN_F32, d_model, d_ff, n));
+  HFFN_TRY(check_dense_f16(dense, true, false));
+  HFFN_REQUIRE(x && b_up && work && err, "null pointer argument");
+  HFFN_REQUIRE(aligned16(x) && aligned16(work), "x and work must be 16-byte aligned");
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_up_f16(x, dense, b_up, z, work, err, d_model, d_ff, n, static_cast<cudaStream_t>(stream));
+}
+
+int hffn_down_f16x3(const void* work, const hffn_dense_f16x3* dense, const float* b_down, float* y, int32_t* err,
+                    int32_t d_model, int32_t d_ff, int64_t n, void* stream) {
+  HFFN_TRY(check_tc(HFFN_F32, d_model, d_ff, n));
+  HFFN_TRY(check_dense_f16(dense, false, true));
+  HFFN_REQUIRE(work && b_down && y && err, "null pointer argument");
+  HFFN_REQUIRE(aligned16(work), "work must be 16-byte aligned");
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_down_f16(work, dense, b_down, y, err, d_model, d_ff, n, static_cast<cudaStream_t>(stream));
+}
+
+int hffn_forward_f16x3(const hffn_layer* layer, const hffn_dense_f16x3* dense, const float* x, float* y, float* z,
+                       void* work, int32_t* err, int64_t n, void* stream) {
+  HFFN_TRY(check_layer(layer));
+  HFFN_TRY(check_tc(HFFN_F32, layer->d_model, layer->d_ff, n));
+  HFFN_TRY(check_dense_f16(dense, true, true));
+  HFFN_REQUIRE(x && y && work && err, "null pointer argument");
+  HFFN_REQUIRE(aligned16(x) && aligned16(work), "x and work must be 16-byte aligned");
+  HFFN_TRY(bind_stream_device(stream));
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  HFFN_TRY(tc_up_f16(x, dense, static_cast<const float*>(layer->b_up), z, work, err, layer->d_model, layer->d_ff, n,
+                     s));
+  return tc_down_f16(work, dense, static_cast<const float*>(layer->b_down), y, err, layer->d_model, layer->d_ff, n, s);
 }
 
 int hffn_up_tc(int dtype, const void* x, const void* w_hi, const void* w_lo, const void* b_up, void* act_hi,

@@ -12,6 +12,15 @@
 // ~2^-22 relative, is dropped), with fp32 accumulation in TMEM: products carry ~2^-21 relative error instead of tf32's
 // 2^-11. The conversions are the PTX instruction cvt.rna.tf32.f32.
 //
+// float32 storage, fp16x3 format (the float32 forward's default): the same three-product split with fp16 parts, which
+// carry the same 11-bit significand as tf32 but run at the f16 MMA rate (twice tf32's) and take half the bytes. fp16's
+// 5-bit exponent is met by power-of-two scales that leave every product exact: each weight row r is stored scaled by
+// 2^e_r (its largest |value| into [2^14, 2^15)), each token's x row by 2^e_t likewise, and each token's act row by a
+// power of two that maps a bound of |act| below 2^15 (|gelu(z)| <= max(|z|, 0.17), |z| <= max_r ||W_up[r]||_1 max|x_t|
+// + max|b_up|). The epilogues multiply the accumulator by 2^-(e_r + e_t) before the bias. An element far below its
+// row's largest loses significand bits to fp16's subnormal range only where its error is below 2^-40 of that row's
+// largest, far under float32's own rounding of the dot product.
+//
 // float32 accumulation runs in K chunks of 128 values (48 MMAs) into fresh TMEM accumulators that the epilogue adds
 // into float32 registers with round-to-nearest: the accumulation bias of the tensor core stays bounded by one chunk.
 //
@@ -24,6 +33,7 @@
 // own copies in flight, frees its TMEM and returns. No TMA multicast is used.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_fp16.h>
 
 #include <atomic>
 #include <climits>
@@ -217,6 +227,11 @@ struct EpilogueArgs {
   void* peers[kMaxPeers];
   int64_t tokens_per_owner;
   int64_t rows;          // M
+  // fp16x3 (kUp, kDown): the accumulator of (row, token t) is scaled back by row_inv[row] tok_inv[t];
+  // kUp stores act 2^e_t (act_mul[t] = 2^e_t) as fp16 hi / lo parts into out_hi / out_lo
+  const float* row_inv;
+  const float* tok_inv;
+  const float* act_mul;
 };
 
 // One value of the output tile: bias added, then (up) GELU and the stores of act (float32: tf32 hi and lo parts) and
@@ -349,6 +364,49 @@ __device__ __forceinline__ float2 emit4_at(const EpilogueArgs* e, int row, int t
   }
 }
 
+// fp16x3: one value of the output tile, token t: the accumulator scaled back by row_inv tok_inv[t] (powers of two: exact,
+// so a fused multiply-add rounds once like the separate add), + bias; then (up) z, GELU and act 2^e_t split into fp16
+// hi / lo, or (down) the y store.
+template <int EPI>
+__device__ __forceinline__ void emit_f16_one(const EpilogueArgs* e, int64_t at, float acc, float row_inv, float tok_inv,
+                                             float act_mul, float bias) {
+  const float s = acc * row_inv * tok_inv + bias;
+  if constexpr (EPI == kUp) {
+    if (e->z) e->z[at] = s;
+    const float h = gelu(s) * act_mul;
+    const __half hi = __float2half_rn(h);
+    reinterpret_cast<__half*>(e->out_hi)[at] = hi;
+    reinterpret_cast<__half*>(e->out_lo)[at] = __float2half_rn(h - __half2float(hi));
+  } else {
+    static_assert(EPI == kDown, "fp16x3 epilogues: up and down");
+    reinterpret_cast<float*>(e->out_hi)[at] = s;
+  }
+}
+
+// fp16x3: four values of one output row, tokens t0 .. t0 + 3 (t0 a multiple of 4; the token tables 16-byte aligned).
+template <int EPI>
+__device__ __forceinline__ void emit4_f16(const EpilogueArgs* e, int row, int t0, int M, int N, float row_inv,
+                                          float bias, float v0, float v1, float v2, float v3) {
+  const int64_t at = (int64_t)t0 * M + row;
+  const int count = N - t0;
+  if (count >= 4) {
+    const float4 ti = *reinterpret_cast<const float4*>(e->tok_inv + t0);
+    float4 am = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (EPI == kUp) am = *reinterpret_cast<const float4*>(e->act_mul + t0);
+    emit_f16_one<EPI>(e, at, v0, row_inv, ti.x, am.x, bias);
+    emit_f16_one<EPI>(e, at + M, v1, row_inv, ti.y, am.y, bias);
+    emit_f16_one<EPI>(e, at + 2 * (int64_t)M, v2, row_inv, ti.z, am.z, bias);
+    emit_f16_one<EPI>(e, at + 3 * (int64_t)M, v3, row_inv, ti.w, am.w, bias);
+    return;
+  }
+  const float v[3] = {v0, v1, v2};
+#pragma unroll
+  for (int j = 0; j < 3; ++j)
+    if (j < count)
+      emit_f16_one<EPI>(e, at + (int64_t)j * M, v[j], row_inv, e->tok_inv[t0 + j],
+                        EPI == kUp ? e->act_mul[t0 + j] : 0.f, bias);
+}
+
 // One support entry q of row `row`, column `col`, gradient g: stored and / or applied by AdamW (PyTorch's fused order),
 // and the dense operand [row, col] refreshed with the new value as tf32 hi / lo.
 __device__ __noinline__ void sampled_entry(const EpilogueArgs* e, int q, int64_t dense_at, float g) {
@@ -381,7 +439,7 @@ struct Layout {
   static constexpr int kTmemCols = 2 * BN;
 };
 
-template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK, int RB, int EW, bool A_MN, bool B_MN>
+template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK, int RB, int EW, bool A_MN, bool B_MN, bool kF16>
 __global__ void __launch_bounds__(threads_for(EW), 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_a_lo,
                const __grid_constant__ CUtensorMap map_b_hi, const __grid_constant__ CUtensorMap map_b_lo, int M,
@@ -402,8 +460,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN, num_tiles = num_m * num_n;
-  const int num_kb = (K * (kBf16 ? 2 : 4) + kRowBytes - 1) / kRowBytes;
-  const int k_elems = kRowBytes / (kBf16 ? 2 : 4);
+  static_assert(!(kBf16 && kF16), "fp16x3 operands are a float32 format");
+  constexpr int kElem = kBf16 || kF16 ? 2 : 4;
+  const int num_kb = (K * kElem + kRowBytes - 1) / kRowBytes;
+  const int k_elems = kRowBytes / kElem;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -506,7 +566,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
     // The K loop of a tile runs in chunks of chunk_kb k-blocks, each into a fresh accumulator buffer that the
     // epilogue drains (float32: the chunk sums are added in registers with round-to-nearest; see the epilogue).
     if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(kBf16 ? 1 : 2, BN, A_MN, B_MN);
+      constexpr uint32_t idesc = instr_desc(kBf16 ? 1 : (kF16 ? 0 : 2), BN, A_MN, B_MN);
       const uint32_t mn_lbo = (uint32_t)(k_elems * 128);    // bytes between 32-element MN blocks of a stage
       const int chunk_kb = KCHUNK > 0 ? KCHUNK : num_kb;
       int stage = 0, acc = 0;
@@ -534,12 +594,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
               const uint32_t acc_in = (kb != kc || k != 0) ? 1u : 0u;
               const uint64_t ah = A_MN ? smem_desc_mn(a + 1024 * k, mn_lbo) : smem_desc<RB>(a + 32 * k);
               const uint64_t bh = B_MN ? smem_desc_mn(b + 1024 * k, mn_lbo) : smem_desc<RB>(b + 32 * k);
-              mma<kBf16>(d_tmem, ah, bh, idesc, acc_in);
+              mma<kBf16 || kF16>(d_tmem, ah, bh, idesc, acc_in);
               if (!kBf16) {
                 const uint64_t al = A_MN ? smem_desc_mn(a + L::kA + 1024 * k, mn_lbo) : smem_desc<RB>(a + L::kA + 32 * k);
                 const uint64_t bl = B_MN ? smem_desc_mn(b + L::kB + 1024 * k, mn_lbo) : smem_desc<RB>(b + L::kB + 32 * k);
-                mma<kBf16>(d_tmem, ah, bl, idesc, 1);
-                mma<kBf16>(d_tmem, al, bh, idesc, 1);
+                mma<kBf16 || kF16>(d_tmem, ah, bl, idesc, 1);
+                mma<kBf16 || kF16>(d_tmem, al, bh, idesc, 1);
               }
             }
             mma_commit(&empty[stage]);
@@ -585,6 +645,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
         if constexpr (kBf16) bias = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(e->bias)[row]);
         else bias = reinterpret_cast<const float*>(e->bias)[row];
       }
+      float row_inv = 1.f;
+      if constexpr (kF16)
+        if (row < M) row_inv = e->row_inv[row];
       float2 partial = make_float2(0.f, 0.f);
       if constexpr (KCHUNK > 0) {
         // chunk partials summed in registers, chunk after chunk, round-to-nearest
@@ -635,10 +698,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
 #pragma unroll
           for (int i = 0; i < HALF; i += 4)
             if (n0 + i < N) {
-              const float2 r = emit4_at<kBf16, EPI, HALF>(e, row, n0 + i, M, N, bias, sum[i], sum[i + 1], sum[i + 2],
-                                                          sum[i + 3]);
-              partial.x += r.x;
-              partial.y += r.y;
+              if constexpr (kF16) {
+                emit4_f16<EPI>(e, row, n0 + i, M, N, row_inv, bias, sum[i], sum[i + 1], sum[i + 2], sum[i + 3]);
+              } else {
+                const float2 r = emit4_at<kBf16, EPI, HALF>(e, row, n0 + i, M, N, bias, sum[i], sum[i + 1],
+                                                            sum[i + 2], sum[i + 3]);
+                partial.x += r.x;
+                partial.y += r.y;
+              }
             }
         }
       } else {
@@ -655,10 +722,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
             for (int j = 0; j < 32; j += 4) {
               const int t = n0 + c * 32 + j;
               if (t < N) {
-                const float2 r = emit4_at<kBf16, EPI, HALF>(e, row, t, M, N, bias, v[j], v[j + 1], v[j + 2],
-                                                            v[j + 3]);
-                partial.x += r.x;
-                partial.y += r.y;
+                if constexpr (kF16) {
+                  emit4_f16<EPI>(e, row, t, M, N, row_inv, bias, v[j], v[j + 1], v[j + 2], v[j + 3]);
+                } else {
+                  const float2 r = emit4_at<kBf16, EPI, HALF>(e, row, t, M, N, bias, v[j], v[j + 1], v[j + 2],
+                                                              v[j + 3]);
+                  partial.x += r.x;
+                  partial.y += r.y;
+                }
               }
             }
           }
@@ -752,6 +823,115 @@ __global__ void split_transpose_kernel(const float* __restrict__ x, int64_t n, i
   }
 }
 
+// fp16x3 scales. 2^e as a float (e in [-126, 127]).
+__device__ __forceinline__ float exp2i(int e) { return __int_as_float((127 + e) << 23); }
+
+// The exponent e that maps the largest magnitude m of a row into [2^14, 2^15) (m = f 2^k, f in [0.5, 1): e = 15 - k),
+// clamped to [-63, 63] so that the product of two scales stays a normal float; 0 for an all-zero row.
+__device__ __forceinline__ int row_exponent(float m) {
+  if (!(m > 0.f)) return 0;
+  const int k = (int)((__float_as_uint(m) >> 23) & 0xFF) - 126;
+  const int e = 15 - k;
+  return e < -63 ? -63 : (e > 63 ? 63 : e);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_add(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// fp16x3 operands of a CSR-by-row support [rows, cols] (zeroed beforehand): one warp per row; the row's values scaled by
+// 2^e (row_exponent of its largest |value|) and split into fp16 hi / lo at their dense positions, inv[row] = 2^-e; with
+// `bound`, bound[0] = the largest row L1 norm and bound[1] = the largest |bias| (atomicMax on the bits of non-negative
+// floats, which order as integers).
+__global__ void densify_f16_kernel(const int32_t* __restrict__ off, const int16_t* __restrict__ idx,
+                                   const float* __restrict__ val, const float* __restrict__ bias, int rows, int cols,
+                                   __half* __restrict__ hi, __half* __restrict__ lo, float* __restrict__ inv,
+                                   float* bound) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int begin = off[row], end = off[row + 1];
+  float m = 0.f, l1 = 0.f;
+  for (int q = begin + lane; q < end; q += 32) {
+    const float a = fabsf(val[q]);
+    m = fmaxf(m, a);
+    l1 += a;
+  }
+  m = warp_max(m);
+  l1 = warp_add(l1);
+  const int e = row_exponent(m);
+  if (lane == 0) {
+    inv[row] = exp2i(-e);
+    if (bound != nullptr) {
+      atomicMax(reinterpret_cast<int*>(bound), __float_as_int(l1));
+      if (bias != nullptr) atomicMax(reinterpret_cast<int*>(bound) + 1, __float_as_int(fabsf(bias[row])));
+    }
+  }
+  const float scale = exp2i(e);
+  const int64_t base = (int64_t)row * cols;
+  for (int q = begin + lane; q < end; q += 32) {
+    const float v = val[q] * scale;
+    const __half h = __float2half_rn(v);
+    hi[base + idx[q]] = h;
+    lo[base + idx[q]] = __float2half_rn(v - __half2float(h));
+  }
+}
+
+// fp16x3 x operand and token scales: one warp per token row t of x [n, d] (d a multiple of 4, rows 16-byte aligned).
+// x_t 2^e_t (row_exponent of max |x_t|) split into fp16 hi / lo, x_inv[t] = 2^-e_t; act_mul[t] = 2^a_t and
+// act_inv[t] = 2^-a_t with a_t = row_exponent of the bound max(bound[0] max|x_t| + bound[1], 0.17) of |act_t|
+// (|z| <= ||W_up[r]||_1 max|x_t| + |b_up[r]|, and |gelu(z)| <= max(|z|, 0.17)): act 2^a_t stays below 2^15, half of
+// fp16's largest finite value, which leaves room for the rounding of the bound and of z.
+__global__ void split_f16_kernel(const float* __restrict__ x, int64_t n, int d, const float* __restrict__ bound,
+                                 __half* __restrict__ hi, __half* __restrict__ lo, float* __restrict__ x_inv,
+                                 float* __restrict__ act_mul, float* __restrict__ act_inv) {
+  const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= n) return;
+  const float4* row = reinterpret_cast<const float4*>(x + t * d);
+  const int d4 = d >> 2;
+  float m = 0.f;
+  for (int i = lane; i < d4; i += 32) {
+    const float4 v = row[i];
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+  m = warp_max(m);
+  const int e = row_exponent(m);
+  const float scale = exp2i(e);
+  uint2* h_row = reinterpret_cast<uint2*>(hi + t * d);
+  uint2* l_row = reinterpret_cast<uint2*>(lo + t * d);
+  for (int i = lane; i < d4; i += 32) {
+    const float4 v = row[i];
+    const float s[4] = {v.x * scale, v.y * scale, v.z * scale, v.w * scale};
+    __half h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      h[j] = __float2half_rn(s[j]);
+      l[j] = __float2half_rn(s[j] - __half2float(h[j]));
+    }
+    uint2 ph, pl;
+    ph.x = (uint32_t)__half_as_ushort(h[0]) | ((uint32_t)__half_as_ushort(h[1]) << 16);
+    ph.y = (uint32_t)__half_as_ushort(h[2]) | ((uint32_t)__half_as_ushort(h[3]) << 16);
+    pl.x = (uint32_t)__half_as_ushort(l[0]) | ((uint32_t)__half_as_ushort(l[1]) << 16);
+    pl.y = (uint32_t)__half_as_ushort(l[2]) | ((uint32_t)__half_as_ushort(l[3]) << 16);
+    h_row[i] = ph;
+    l_row[i] = pl;
+  }
+  if (lane == 0) {
+    x_inv[t] = exp2i(-e);
+    const int a = row_exponent(fmaxf(bound[0] * m + bound[1], 0.17f));
+    act_mul[t] = exp2i(a);
+    act_inv[t] = exp2i(-a);
+  }
+}
+
 // The support of each row (CSR: offsets [rows + 1], columns) as a bitmask over 32-column words (ld words per row,
 // zero past the last column) and, per word, the compact index of the row's first entry at or after the word's first
 // column. One warp per row, the row's mask assembled in shared memory (ld <= kMaxMaskWords).
@@ -805,21 +985,26 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [rows, k] K-major operand, box = (128 bytes of K) x box_rows, 128-byte swizzle, zero fill outside.
-static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, bool bf16, int box_rows,
+// Element types of the operands: float32 (tf32 parts), bfloat16, fp16 (fp16x3 parts).
+enum Elem { kElemF32 = 0, kElemBf16 = 1, kElemF16 = 2 };
+
+// [rows, k] K-major operand, box = (row_bytes bytes of K) x box_rows, 128- or 64-byte swizzle, zero fill outside.
+static int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int elem_type, int box_rows,
                     int row_bytes, int64_t ld = 0) {
   auto fn = encode_fn();
   if (fn == nullptr) {
     set_error("cuTensorMapEncodeTiled unavailable");
     return HFFN_ERR_CUDA;
   }
-  const int elem = bf16 ? 2 : 4;
+  const int elem = elem_type == kElemF32 ? 4 : 2;
+  const CUtensorMapDataType type = elem_type == kElemF32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : elem_type == kElemBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)((ld > 0 ? ld : k) * elem)};
   cuuint32_t box[2] = {(cuuint32_t)(row_bytes / elem), (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
-                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  CUresult r = fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -870,15 +1055,17 @@ static int make_map_mn(CUtensorMap* map, const void* base, int64_t mn, int64_t k
 
 // D[M, N] = A[M, K] B[N, K]^T. K-major operands are [rows, K] with K contiguous; an MN-major operand A (B) is stored
 // [K, M] ([K, N]), its leading dimension lda (ldb) elements.
-template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK, int RB, int EW, bool A_MN = false, bool B_MN = false>
+template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK, int RB, int EW, bool A_MN = false, bool B_MN = false,
+          bool kF16 = false>
 static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N, int K,
                        const EpilogueArgs& epi, int* err, cudaStream_t s, int64_t lda = 0, int64_t ldb = 0) {
   using L = Layout<kBf16, BN, STAGES, RB>;
-  static_assert(!(kBf16 && (A_MN || B_MN)), "MN-major operands are float32 only");
+  static_assert(!((kBf16 || kF16) && (A_MN || B_MN)), "MN-major operands are tf32 parts only");
+  constexpr int kElemType = kBf16 ? kElemBf16 : (kF16 ? kElemF16 : kElemF32);
   constexpr int k_box = RB / 4;
   CUtensorMap ma_hi, ma_lo, mb_hi, mb_lo;
   auto map = [&](CUtensorMap* m, const void* base, int rows, int box_rows, bool mn, int64_t ld) {
-    return mn ? make_map_mn(m, base, rows, K, ld, k_box) : make_map(m, base, rows, K, kBf16, box_rows, RB, ld);
+    return mn ? make_map_mn(m, base, rows, K, ld, k_box) : make_map(m, base, rows, K, kElemType, box_rows, RB, ld);
   };
   HFFN_TRY(map(&ma_hi, a_hi, M, BM, A_MN, lda));
   HFFN_TRY(map(&mb_hi, b_hi, N, BN, B_MN, ldb));
@@ -889,7 +1076,7 @@ static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, con
     ma_lo = ma_hi;
     mb_lo = mb_hi;
   }
-  auto kernel = tc_gemm_kernel<kBf16, BN, STAGES, EPI, KCHUNK, RB, EW, A_MN, B_MN>;
+  auto kernel = tc_gemm_kernel<kBf16, BN, STAGES, EPI, KCHUNK, RB, EW, A_MN, B_MN, kF16>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
@@ -939,7 +1126,102 @@ static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b
   }
 }
 
+// fp16x3: 128 K values per accumulation chunk, as for 3xTF32 (4 k-blocks of 32 fp16 values, 24 MMAs).
+constexpr int kF16Chunk = 4;
+
+// One fp16x3 forward GEMM: 64-byte rows of fp16 (32 K values a stage, 48 KB: A hi / lo + B hi / lo), the tile widths
+// and stage counts of the 3xTF32 GEMMs, 16 epilogue warps for up (GELU and the split), 8 for down.
+template <int EPI>
+static int launch_forward_gemm_f16(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N,
+                                   int K, const EpilogueArgs& epi, int* err, cudaStream_t s) {
+  constexpr int kWarps = EPI == kUp ? 16 : 8;
+  switch (pick_tile_tokens()) {
+    case 64:
+      return launch_gemm<false, 64, 6, EPI, kF16Chunk, 64, 8, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi,
+                                                                                  err, s);
+    case 128:
+      return launch_gemm<false, 128, 5, EPI, kF16Chunk, 64, kWarps, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K,
+                                                                                       epi, err, s);
+    default:
+      return launch_gemm<false, 256, 4, EPI, kF16Chunk, 64, kWarps, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K,
+                                                                                       epi, err, s);
+  }
+}
+
+// The fp16x3 forward's workspace: x parts [n, d] and act parts [n, H] (fp16 hi, lo), the token tables x_inv, act_mul,
+// act_inv [n] (float32), each piece 256-byte aligned.
+struct F16Work {
+  __half *x_hi, *x_lo, *act_hi, *act_lo;
+  float *x_inv, *act_mul, *act_inv;
+};
+
+static int64_t f16_work(int64_t d, int64_t H, int64_t n, F16Work* w, uint8_t* base) {
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    uint8_t* p = base ? base + off : nullptr;
+    off += (bytes + 255) / 256 * 256;
+    return p;
+  };
+  F16Work dummy;
+  F16Work* t = w ? w : &dummy;
+  t->x_hi = reinterpret_cast<__half*>(take(2 * n * d));
+  t->x_lo = reinterpret_cast<__half*>(take(2 * n * d));
+  t->act_hi = reinterpret_cast<__half*>(take(2 * n * H));
+  t->act_lo = reinterpret_cast<__half*>(take(2 * n * H));
+  t->x_inv = reinterpret_cast<float*>(take(4 * n));
+  t->act_mul = reinterpret_cast<float*>(take(4 * n));
+  t->act_inv = reinterpret_cast<float*>(take(4 * n));
+  return off;
+}
+
 }  // namespace tc
+
+int64_t tc_f16_workspace(int d, int H, int64_t n) { return tc::f16_work(d, H, n, nullptr, nullptr); }
+
+// fp16x3 up: x [n, d] float32 -> act parts and token tables in `work` (z: float32 [n, H] token-major, or NULL).
+int tc_up_f16(const float* x, const hffn_dense_f16x3* D, const float* b, float* z, void* work, int* err, int d, int H,
+              int64_t n, cudaStream_t s) {
+  tc::F16Work w;
+  tc::f16_work(d, H, n, &w, reinterpret_cast<uint8_t*>(work));
+  const int64_t threads = n * 32;
+  tc::split_f16_kernel<<<(unsigned)ceil_div(threads, 256), 256, 0, s>>>(x, n, d, D->up_bound, w.x_hi, w.x_lo, w.x_inv,
+                                                                       w.act_mul, w.act_inv);
+  HFFN_TRY(launch_status("tc_split_f16"));
+  tc::EpilogueArgs up{};
+  up.bias = b;
+  up.out_hi = w.act_hi;
+  up.out_lo = w.act_lo;
+  up.z = z;
+  up.row_inv = D->up_scale;
+  up.tok_inv = w.x_inv;
+  up.act_mul = w.act_mul;
+  return tc::launch_forward_gemm_f16<tc::kUp>(D->up_hi, D->up_lo, w.x_hi, w.x_lo, H, (int)n, d, up, err, s);
+}
+
+// fp16x3 down: the act parts and token tables of tc_up_f16 in `work` -> y [n, d] float32.
+int tc_down_f16(const void* work, const hffn_dense_f16x3* D, const float* b, float* y, int* err, int d, int H,
+                int64_t n, cudaStream_t s) {
+  tc::F16Work w;
+  tc::f16_work(d, H, n, &w, reinterpret_cast<uint8_t*>(const_cast<void*>(work)));
+  tc::EpilogueArgs dn{};
+  dn.bias = b;
+  dn.out_hi = y;
+  dn.row_inv = D->down_scale;
+  dn.tok_inv = w.act_inv;
+  return tc::launch_forward_gemm_f16<tc::kDown>(D->down_hi, D->down_lo, w.act_hi, w.act_lo, d, (int)n, H, dn, err, s);
+}
+
+int tc_densify_f16(const int32_t* off, const int16_t* idx, const float* val, const float* bias, int rows, int cols,
+                   void* hi, void* lo, float* scale, float* bound, cudaStream_t s) {
+  const size_t bytes = (size_t)rows * cols * 2;
+  if (cudaMemsetAsync(hi, 0, bytes, s) != cudaSuccess || cudaMemsetAsync(lo, 0, bytes, s) != cudaSuccess ||
+      (bound != nullptr && cudaMemsetAsync(bound, 0, 2 * sizeof(float), s) != cudaSuccess))
+    return launch_status("densify memset");
+  const int blocks = (int)ceil_div((int64_t)rows * 32, 256);
+  tc::densify_f16_kernel<<<blocks, 256, 0, s>>>(off, idx, val, bias, rows, cols, reinterpret_cast<__half*>(hi),
+                                                reinterpret_cast<__half*>(lo), scale, bound);
+  return launch_status("densify f16x3");
+}
 
 // Tile shapes: float32 (3xTF32) 128 x 256 tiles, stages of 16 K values (64-byte rows, 48 KB: A hi/lo + B hi/lo), 4
 // stages, 16 epilogue warps for up and 8 for down; bfloat16 128 x 256 tiles, stages of 64 K values (128-byte rows,

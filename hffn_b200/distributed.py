@@ -154,7 +154,8 @@ def x_is_cuda(ffn: "ShardedFFN") -> bool:
 
 
 def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, tensor_cores=None, group=None,
-                    segments: int | None = None, comm_sms: int = 0, transport: str = "nccl", push: str = "copy"):
+                    segments: int | None = None, comm_sms: int = 0, transport: str = "nccl", push: str = "copy",
+                    tc_format: str | None = None):
     """The rank's ``HFFNRuntime`` over its neuron shard and the sharded forward around it: ``transport="nccl"`` a
     ``ShardedFFN`` (collective kernels), ``"peer"`` a ``PeerShardedFFN`` (NVLink peer memory and copy engines,
     pipelined over batches, tensor cores only, ``push`` its delivery mode)."""
@@ -170,7 +171,9 @@ def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, ten
     layer = HFFNLayer.from_hidden_major(shard["d_model"], shard["d_ff"], shard["b_up"], shard["up_offsets"],
                                         shard["up_idx"], shard["up_val"], shard["b_down"], shard["down_offsets"],
                                         shard["down_idx"], shard["down_val"])
-    runtime = HFFNRuntime([layer], device, dtype, tensor_cores=tensor_cores)
+    if transport == "peer" and dtype == torch.float32:
+        tc_format = "tf32x3"          # the peer pipeline's GEMMs run on the tf32 pairs
+    runtime = HFFNRuntime([layer], device, dtype, tensor_cores=tensor_cores, tc_format=tc_format)
     if transport == "peer":
         return runtime, PeerShardedFFN(runtime, d_model, group, push=push), (lo, hi)
     ffn = ShardedFFN(lambda x, out: runtime.forward(0, x, out=out), d_model, group, segments=segments,

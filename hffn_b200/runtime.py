@@ -113,7 +113,8 @@ def layer_struct(tensors: dict, d_model: int, d_ff: int) -> native.Layer:
 
 class HFFNRuntime:
     def __init__(self, layers: list[HFFNLayer], device: str | torch.device = "cuda",
-                 dtype: torch.dtype = torch.float32, tensor_cores: bool | None = None) -> None:
+                 dtype: torch.dtype = torch.float32, tensor_cores: bool | None = None,
+                 tc_format: str | None = None) -> None:
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("the HFFN runtime runs on a CUDA device")
@@ -135,22 +136,31 @@ class HFFNRuntime:
                                  else getattr(layer, name).to(self.device)).contiguous() for name in ARRAYS}
                          for layer in layers]
         self._structs = [layer_struct(t, self.d_model, self.d_ff) for t in self._tensors]
-        # Tensor-core operands: the supports densified once (W_up [d_ff, d_model], W_down [d_model, d_ff], zeros off
-        # the support; float32 as tf32 hi/lo pairs). Built when the shape allows it unless tensor_cores=False.
+        # Tensor-core operands: the supports densified (W_up [d_ff, d_model], W_down [d_model, d_ff], zeros off the
+        # support), built on first use and rebuilt after the compact values change. Two formats: ``_dense`` (bfloat16;
+        # float32 as tf32 hi / lo pairs, the operands of the tensor-core training step and of the peer pipeline) and
+        # ``_dense16`` (float32 as scaled fp16 hi / lo pairs, the fp16x3 format of the float32 forward, the default;
+        # ``tc_format="tf32x3"`` runs the float32 forward on the tf32 pairs instead).
         compatible = self.d_model % 8 == 0 and self.d_ff % 8 == 0
         if tensor_cores and not compatible:
             raise ValueError("the tensor-core path needs d_model and d_ff multiples of 8")
         self.tensor_cores = compatible if tensor_cores is None else bool(tensor_cores)
-        self._dense: list[dict] = []
-        self._dense_structs: list = []
-        self._dense_stale: list[bool] = []
+        if dtype == torch.bfloat16:
+            if tc_format not in (None, "bf16"):
+                raise ValueError("bfloat16 layers have one tensor-core format")
+            self.tc_format = "bf16"
+        else:
+            if tc_format not in (None, "f16x3", "tf32x3"):
+                raise ValueError("tc_format must be 'f16x3' or 'tf32x3'")
+            self.tc_format = tc_format or "f16x3"
+        count = len(layers)
+        self._dense: list[dict | None] = [None] * count
+        self._dense_structs: list = [None] * count
+        self._dense_stale: list[bool] = [True] * count
+        self._dense16: list[dict | None] = [None] * count
+        self._dense16_structs: list = [None] * count
+        self._dense16_stale: list[bool] = [True] * count
         self._err = torch.zeros(1, dtype=torch.int32, device=self.device)
-        if self.tensor_cores:
-            for index in range(len(layers)):
-                self._dense.append(self._alloc_dense())
-                self._dense_structs.append(native.Dense(*(self._dense[index][k].data_ptr() if self._dense[index][k] is not None
-                                                          else None for k in ("up_hi", "up_lo", "down_hi", "down_lo"))))
-                self._dense_stale.append(True)
         self.forced_up: str | None = None
         self.forced_down: str | None = None
         self.calls: Counter = Counter()
@@ -165,7 +175,12 @@ class HFFNRuntime:
                 "down_hi": make(d, f), "down_lo": make(d, f) if split else None}
 
     def _densify(self, index: int) -> None:
-        """(Re)build the dense tensor-core operands of layer ``index`` from its compact arrays."""
+        """(Re)build the tf32-pair (float32) or bfloat16 tensor-core operands of layer ``index`` from its compact
+        arrays."""
+        if self._dense[index] is None:
+            dense = self._dense[index] = self._alloc_dense()
+            self._dense_structs[index] = native.Dense(*(None if dense[k] is None else dense[k].data_ptr()
+                                                        for k in ("up_hi", "up_lo", "down_hi", "down_lo")))
         t, dense, stream = self._tensors[index], self._dense[index], native.stream_handle(self.device)
         ptr = lambda v: None if v is None else v.data_ptr()  # noqa: E731
         native.check(native.lib.hffn_densify(self._code, t["up_offsets"].data_ptr(), t["up_idx"].data_ptr(),
@@ -176,10 +191,48 @@ class HFFNRuntime:
                                              ptr(dense["down_lo"]), stream), "hffn_densify down")
         self._dense_stale[index] = False
 
-    def mark_updated(self, index: int) -> None:
-        """The compact values of layer ``index`` changed (an optimiser step): the dense operands are rebuilt lazily."""
+    def _densify16(self, index: int) -> None:
+        """(Re)build the fp16x3 operands of float32 layer ``index``: per projection the scaled fp16 hi / lo parts, the
+        rows' inverse scales and, for up, the bound of |z| per unit of max|x| (``hffn_densify_f16x3``)."""
+        f, d, device = self.d_ff, self.d_model, self.device
+        if self._dense16[index] is None:
+            half = lambda rows, cols: torch.empty(rows, cols, device=device, dtype=torch.float16)  # noqa: E731
+            dense = self._dense16[index] = {
+                "up_hi": half(f, d), "up_lo": half(f, d), "up_scale": torch.empty(f, device=device),
+                "down_hi": half(d, f), "down_lo": half(d, f), "down_scale": torch.empty(d, device=device),
+                "up_bound": torch.empty(2, device=device)}
+            self._dense16_structs[index] = native.DenseF16x3(*(dense[k].data_ptr() for k in (
+                "up_hi", "up_lo", "up_scale", "down_hi", "down_lo", "down_scale", "up_bound")))
+        t, dense, stream = self._tensors[index], self._dense16[index], native.stream_handle(device)
+        native.check(native.lib.hffn_densify_f16x3(t["up_offsets"].data_ptr(), t["up_idx"].data_ptr(),
+                                                   t["up_val"].data_ptr(), t["b_up"].data_ptr(), f, d,
+                                                   dense["up_hi"].data_ptr(), dense["up_lo"].data_ptr(),
+                                                   dense["up_scale"].data_ptr(), dense["up_bound"].data_ptr(), stream),
+                     "hffn_densify_f16x3 up")
+        native.check(native.lib.hffn_densify_f16x3(t["out_offsets"].data_ptr(), t["out_hidden"].data_ptr(),
+                                                   t["out_val"].data_ptr(), None, d, f, dense["down_hi"].data_ptr(),
+                                                   dense["down_lo"].data_ptr(), dense["down_scale"].data_ptr(), None,
+                                                   stream), "hffn_densify_f16x3 down")
+        self._dense16_stale[index] = False
+
+    def forward_operands(self, index: int):
+        """The ``(format, struct)`` of the dense operands the tensor-core forward of layer ``index`` runs on, built or
+        rebuilt first if needed: ``("f16x3", DenseF16x3)`` or ``("tf32x3" / "bf16", Dense)``."""
+        if self.tc_format == "f16x3":
+            if self._dense16_stale[index]:
+                self._densify16(index)
+            return self.tc_format, self._dense16_structs[index]
+        if self._dense_stale[index]:
+            self._densify(index)
+        return self.tc_format, self._dense_structs[index]
+
+    def mark_updated(self, index: int, refreshed: str | None = None) -> None:
+        """The compact values of layer ``index`` changed (an optimiser step): the dense operands are rebuilt lazily,
+        except those of format ``refreshed`` (``"tf32x3"``: the tensor-core training step refreshed them in place)."""
         if self.tensor_cores:
-            self._dense_stale[index] = True
+            if refreshed != "tf32x3":
+                self._dense_stale[index] = True
+            self._dense16_stale[index] = True
 
     def force(self, up: str | None, down: str | None) -> None:
         """Diagnostic: fix the up and/or the down kernel regardless of N (None: the policy). ``("tc", "tc")`` forces the
@@ -198,7 +251,10 @@ class HFFNRuntime:
         self._y = torch.empty(n, self.d_model, device=self.device, dtype=self.dtype)
         self._tc_work = None
         if self.tensor_cores:
-            size = int(native.lib.hffn_forward_tc_workspace(self._code, self._structs[0], n))
+            if self.tc_format == "f16x3":
+                size = int(native.lib.hffn_forward_f16x3_workspace(self._structs[0], n))
+            else:
+                size = int(native.lib.hffn_forward_tc_workspace(self._code, self._structs[0], n))
             self._tc_work = torch.empty(size, dtype=torch.uint8, device=self.device)
 
     def workspace_bytes(self) -> int:
@@ -256,11 +312,15 @@ class HFFNRuntime:
         up, down = self.modes(n, hidden_major=z is not None)
         y = self._y if out is None else out
         if up == TC:
-            if self._dense_stale[index]:
-                self._densify(index)
-            status = native.lib.hffn_forward_tc(self._code, self._structs[index], self._dense_structs[index],
-                                                x.data_ptr(), y.data_ptr(), None, self._tc_work.data_ptr(),
-                                                self._err.data_ptr(), n, native.stream_handle(self.device))
+            fmt, dense = self.forward_operands(index)
+            stream = native.stream_handle(self.device)
+            if fmt == "f16x3":
+                status = native.lib.hffn_forward_f16x3(self._structs[index], dense, x.data_ptr(), y.data_ptr(), None,
+                                                       self._tc_work.data_ptr(), self._err.data_ptr(), n, stream)
+            else:
+                status = native.lib.hffn_forward_tc(self._code, self._structs[index], dense, x.data_ptr(),
+                                                    y.data_ptr(), None, self._tc_work.data_ptr(),
+                                                    self._err.data_ptr(), n, stream)
             native.check(status, "hffn_forward_tc")
             return up, down
         status = native.lib.hffn_forward(self._code, self._structs[index], x.data_ptr(), y.data_ptr(),

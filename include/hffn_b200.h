@@ -206,6 +206,46 @@ int64_t hffn_forward_tc_workspace(int dtype, const hffn_layer* layer, int64_t n)
 int hffn_forward_tc(int dtype, const hffn_layer* layer, const hffn_dense* dense, const void* x, void* y, float* z,
                     void* work, int32_t* err, int64_t n, void* stream);
 
+/* Dense tensor-core operands of one float32 layer in the fp16x3 format, built by hffn_densify_f16x3: W_up [d_ff,
+ * d_model] and W_down [d_model, d_ff], zeros off the support, each row r scaled by a power of two 2^e_r (its largest
+ * |value| into [2^14, 2^15)) and stored as fp16 parts hi = rn(w 2^e_r), lo = rn(w 2^e_r - hi); up_scale [d_ff] and
+ * down_scale [d_model] hold 2^-e_r; up_bound [2] = {max_r sum_k |W_up[r, k]|, max_r |b_up[r]|} (the bound of |z| the
+ * activations' scales derive from). A product of fp16 parts is exact and each part holds tf32's 11-bit significand, so
+ * the forward computes the 3xTF32 split's three products (hi hi + hi lo + lo hi) at the f16 tensor-core rate. */
+typedef struct hffn_dense_f16x3 {
+  void* up_hi;
+  void* up_lo;
+  float* up_scale;
+  void* down_hi;
+  void* down_lo;
+  float* down_scale;
+  float* up_bound;
+} hffn_dense_f16x3;
+
+/* Build one projection's fp16x3 operands from its CSR-by-row support (up: rows = d_ff over up_offsets / up_idx /
+ * up_val with bias = b_up and bound = the up_bound of the struct; down: rows = d_model over out_offsets / out_hidden /
+ * out_val, bias and bound NULL). hi, lo: fp16 [rows, cols]; scale: float32 [rows]. */
+int hffn_densify_f16x3(const int32_t* offsets, const int16_t* idx, const float* val, const float* bias, int32_t rows,
+                       int32_t cols, void* hi, void* lo, float* scale, float* bound, void* stream);
+
+/* Bytes of the workspace of the fp16x3 forward for n tokens. */
+int64_t hffn_forward_f16x3_workspace(const hffn_layer* layer, int64_t n);
+
+/* The float32 forward on the tcgen05 tensor cores in the fp16x3 format (the same function as hffn_forward and
+ * hffn_forward_tc, which it replaces for float32 layers, runtime.py:134-163): x split per token into scaled fp16
+ * parts, the up GEMM with a scale + bias + GELU epilogue that stores act as scaled fp16 parts, the down GEMM with a
+ * scale + bias epilogue. y [n, d_model]; z NULL or float32 [n, d_ff] TOKEN-major; work:
+ * hffn_forward_f16x3_workspace bytes; err as for hffn_forward_tc. */
+int hffn_forward_f16x3(const hffn_layer* layer, const hffn_dense_f16x3* dense, const float* x, float* y, float* z,
+                       void* work, int32_t* err, int64_t n, void* stream);
+
+/* The two halves of hffn_forward_f16x3, for callers that run them apart (the neuron-sharded forward, the benchmark's
+ * per-kernel timing): hffn_up_f16x3 leaves act and its token scales in `work` for hffn_down_f16x3 over the same n. */
+int hffn_up_f16x3(const float* x, const hffn_dense_f16x3* dense, const float* b_up, float* z, void* work, int32_t* err,
+                  int32_t d_model, int32_t d_ff, int64_t n, void* stream);
+int hffn_down_f16x3(const void* work, const hffn_dense_f16x3* dense, const float* b_down, float* y, int32_t* err,
+                    int32_t d_model, int32_t d_ff, int64_t n, void* stream);
+
 /* The tensor-core down projection of a rank's neuron shard, fused with the reduction's transfer: the partial output of
  * token t is stored directly into the receive buffer of the rank that owns t (peer memory over NVLink, plain stores,
  * no collective call): peer_y[t / tokens_per_owner] + (t % tokens_per_owner) * d_model. n = world x tokens_per_owner;

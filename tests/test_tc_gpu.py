@@ -1,7 +1,8 @@
 """GPU parity of the tensor-core (tcgen05) forward against the float64 oracle, through the C ABI.
 
-float32 runs the 3xTF32 split and must meet the float32 bar (relative 1e-5 with floor 1, absolute 2e-5); bfloat16
-storage relative 2e-2. The kernels' bounded waits must never fire (error flag 0)."""
+float32 runs in both operand formats, the fp16x3 split (the default) and the 3xTF32 split, and must meet the float32
+bar in each (relative 1e-5 with floor 1, absolute 2e-5); bfloat16 storage relative 2e-2. The kernels' bounded waits
+must never fire (error flag 0)."""
 import numpy as np
 import pytest
 import torch
@@ -20,9 +21,12 @@ def kernel_layer(layer):
                                        t(layer.down_val))
 
 
-def tc_runtime(layer, dtype=torch.float32):
+FORMATS = ("f16x3", "tf32x3")
+
+
+def tc_runtime(layer, dtype=torch.float32, tc_format=None):
     from hffn_b200.runtime import HFFNRuntime
-    runtime = HFFNRuntime([kernel_layer(layer)], "cuda", dtype, tensor_cores=True)
+    runtime = HFFNRuntime([kernel_layer(layer)], "cuda", dtype, tensor_cores=True, tc_format=tc_format)
     runtime.force("tc", "tc")
     return runtime
 
@@ -31,11 +35,12 @@ def relative(y, expected):
     return float(np.max(np.abs(y - expected) / np.maximum(1.0, np.abs(expected))))
 
 
+@pytest.mark.parametrize("tc_format", FORMATS)
 @pytest.mark.parametrize("n", [1, 7, 128, 129, 300])
-def test_small_layer(n):
+def test_small_layer(n, tc_format):
     case = synth.TEST_CASES["homog_256_1024"]
     layer = synth.make_layer(case)
-    runtime = tc_runtime(layer)
+    runtime = tc_runtime(layer, tc_format=tc_format)
     x = synth.make_input(case, n)
     y = runtime.forward(0, torch.from_numpy(x).cuda()).double().cpu().numpy()
     expected = forward64.forward(layer, x)
@@ -44,10 +49,11 @@ def test_small_layer(n):
     assert runtime.calls[("tc", "tc")] == 1
 
 
-def test_irregular_layer_repeatable():
+@pytest.mark.parametrize("tc_format", FORMATS)
+def test_irregular_layer_repeatable(tc_format):
     case = synth.TEST_CASES["irreg_512_2048"]
     layer = synth.make_layer(case)
-    runtime = tc_runtime(layer)
+    runtime = tc_runtime(layer, tc_format=tc_format)
     x = torch.from_numpy(synth.make_input(case, 333)).cuda()
     first = runtime.forward(0, x).clone()
     assert torch.equal(first, runtime.forward(0, x))
@@ -55,12 +61,13 @@ def test_irregular_layer_repeatable():
     assert runtime.device_errors() == 0
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_c1_and_c2(dtype):
+@pytest.mark.parametrize("dtype,tc_format", [(torch.float32, "f16x3"), (torch.float32, "tf32x3"),
+                                             (torch.bfloat16, None)])
+def test_c1_and_c2(dtype, tc_format):
     for name, n in (("c1_512_2048_k128", 256), ("c2_1024_4096_k512", 4096)):
         case = synth.CONFIGS[name]
         layer = synth.make_layer(case)
-        runtime = tc_runtime(layer, dtype)
+        runtime = tc_runtime(layer, dtype, tc_format)
         x = synth.make_input(case, n)
         y = runtime.forward(0, torch.from_numpy(x).cuda().to(dtype)).float().cpu().numpy()
         rows = np.r_[0:16, n - 16:n]
@@ -107,8 +114,9 @@ def bf16_layer(layer):
                                b_down=r(layer.b_down))
 
 
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_forced_tile_widths(dtype):
+@pytest.mark.parametrize("dtype,tc_format", [(torch.float32, "f16x3"), (torch.float32, "tf32x3"),
+                                             (torch.bfloat16, None)])
+def test_forced_tile_widths(dtype, tc_format):
     """Every token width of the forward GEMMs' tiles (forced process-wide, then back to the automatic choice) on ragged
     token counts, irregular supports: the same bits at every width (token columns are independent), within tolerance
     of the oracle on the layer and input the kernel holds (bfloat16: rounded)."""
@@ -116,7 +124,7 @@ def test_forced_tile_widths(dtype):
     case = synth.TEST_CASES["irreg_512_2048"]
     layer = synth.make_layer(case)
     held = layer if dtype == torch.float32 else bf16_layer(layer)
-    runtime = tc_runtime(layer, dtype)
+    runtime = tc_runtime(layer, dtype, tc_format)
     try:
         for n in (1, 65, 200, 777):
             x = torch.from_numpy(synth.make_input(case, n)).to(dtype)
