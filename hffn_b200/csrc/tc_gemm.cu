@@ -372,7 +372,7 @@ __device__ __forceinline__ void emit_f16_one(const EpilogueArgs* e, int64_t at, 
                                              float act_mul, float bias) {
   const float s = acc * row_inv * tok_inv + bias;
   if constexpr (EPI == kUp) {
-    if (e->z) e->z[at] = s;
+    if (e->z != nullptr) e->z[at] = s;
     const float h = gelu(s) * act_mul;
     const __half hi = __float2half_rn(h);
     reinterpret_cast<__half*>(e->out_hi)[at] = hi;
@@ -405,6 +405,41 @@ __device__ __forceinline__ void emit4_f16(const EpilogueArgs* e, int row, int t0
     if (j < count)
       emit_f16_one<EPI>(e, at + (int64_t)j * M, v[j], row_inv, e->tok_inv[t0 + j],
                         EPI == kUp ? e->act_mul[t0 + j] : 0.f, bias);
+}
+
+// fp16x3: the values of one output row over the thread's HALF token columns n0 .. n0 + HALF - 1 (sum: the chunk sums).
+// With the whole column part inside [0, N), the token tables (written by the split kernel, read-only here) are read
+// as float4, each group's ahead of the previous group's stores, so that their latency overlaps the GELU of the
+// previous group instead of following its stores.
+template <int EPI, int HALF>
+__device__ __forceinline__ void emit_row_f16(const EpilogueArgs* e, int row, int n0, int M, int N, float row_inv,
+                                             float bias, const float (&sum)[HALF]) {
+  if (n0 + HALF > N) {
+#pragma unroll
+    for (int i = 0; i < HALF; i += 4)
+      if (n0 + i < N) emit4_f16<EPI>(e, row, n0 + i, M, N, row_inv, bias, sum[i], sum[i + 1], sum[i + 2], sum[i + 3]);
+    return;
+  }
+  const float4* tok = reinterpret_cast<const float4*>(e->tok_inv + n0);
+  const float4* mul = reinterpret_cast<const float4*>(e->act_mul + n0);
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 ti = __ldg(tok), am = EPI == kUp ? __ldg(mul) : zero;
+  int64_t at = (int64_t)n0 * M + row;
+#pragma unroll
+  for (int g = 0; g < HALF / 4; ++g) {
+    float4 ti_next = zero, am_next = zero;
+    if (g + 1 < HALF / 4) {
+      ti_next = __ldg(tok + g + 1);
+      if constexpr (EPI == kUp) am_next = __ldg(mul + g + 1);
+    }
+    emit_f16_one<EPI>(e, at, sum[4 * g], row_inv, ti.x, am.x, bias);
+    emit_f16_one<EPI>(e, at + M, sum[4 * g + 1], row_inv, ti.y, am.y, bias);
+    emit_f16_one<EPI>(e, at + 2 * (int64_t)M, sum[4 * g + 2], row_inv, ti.z, am.z, bias);
+    emit_f16_one<EPI>(e, at + 3 * (int64_t)M, sum[4 * g + 3], row_inv, ti.w, am.w, bias);
+    at += 4 * (int64_t)M;
+    ti = ti_next;
+    am = am_next;
+  }
 }
 
 // One support entry q of row `row`, column `col`, gradient g: stored and / or applied by AdamW (PyTorch's fused order),
@@ -695,18 +730,18 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
             }
           }
         } else if (row < M) {
+          if constexpr (kF16) {
+            emit_row_f16<EPI, HALF>(e, row, n0, M, N, row_inv, bias, sum);
+          } else {
 #pragma unroll
-          for (int i = 0; i < HALF; i += 4)
-            if (n0 + i < N) {
-              if constexpr (kF16) {
-                emit4_f16<EPI>(e, row, n0 + i, M, N, row_inv, bias, sum[i], sum[i + 1], sum[i + 2], sum[i + 3]);
-              } else {
+            for (int i = 0; i < HALF; i += 4)
+              if (n0 + i < N) {
                 const float2 r = emit4_at<kBf16, EPI, HALF>(e, row, n0 + i, M, N, bias, sum[i], sum[i + 1],
                                                             sum[i + 2], sum[i + 3]);
                 partial.x += r.x;
                 partial.y += r.y;
               }
-            }
+          }
         }
       } else {
         if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, kWaitNs)) {
@@ -1126,8 +1161,11 @@ static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b
   }
 }
 
-// fp16x3: 128 K values per accumulation chunk, as for 3xTF32 (4 k-blocks of 32 fp16 values, 24 MMAs).
-constexpr int kF16Chunk = 4;
+// fp16x3 accumulation chunks: up 8 k-blocks (256 K values, 48 MMAs: the MMA count of a 3xTF32 chunk, so the same bound
+// on the accumulation bias; two chunks let the MMAs run a quarter of a C2 tile ahead of the GELU epilogue), down 4
+// (128 K values: its epilogue is light, and shorter chunks keep its error below the up's).
+template <int EPI>
+constexpr int f16_chunk() { return EPI == kUp ? 8 : 4; }
 
 // One fp16x3 forward GEMM: 64-byte rows of fp16 (32 K values a stage, 48 KB: A hi / lo + B hi / lo), the tile widths
 // and stage counts of the 3xTF32 GEMMs, 16 epilogue warps for up (GELU and the split), 8 for down.
@@ -1135,16 +1173,17 @@ template <int EPI>
 static int launch_forward_gemm_f16(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N,
                                    int K, const EpilogueArgs& epi, int* err, cudaStream_t s) {
   constexpr int kWarps = EPI == kUp ? 16 : 8;
+  constexpr int kChunk = f16_chunk<EPI>();
   switch (pick_tile_tokens()) {
     case 64:
-      return launch_gemm<false, 64, 6, EPI, kF16Chunk, 64, 8, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi,
-                                                                                  err, s);
+      return launch_gemm<false, 64, 6, EPI, kChunk, 64, 8, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi,
+                                                                               err, s);
     case 128:
-      return launch_gemm<false, 128, 5, EPI, kF16Chunk, 64, kWarps, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K,
-                                                                                       epi, err, s);
+      return launch_gemm<false, 128, 5, EPI, kChunk, 64, kWarps, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K,
+                                                                                    epi, err, s);
     default:
-      return launch_gemm<false, 256, 4, EPI, kF16Chunk, 64, kWarps, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K,
-                                                                                       epi, err, s);
+      return launch_gemm<false, 256, 4, EPI, kChunk, 64, kWarps, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K,
+                                                                                    epi, err, s);
   }
 }
 
