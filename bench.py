@@ -433,8 +433,10 @@ def forward_record(ctx: Context, name: str, cpu_seconds: float) -> dict | None:
                                           struct.out_hidden, struct.out_val, struct.b_down, runtime._y.data_ptr(), d,
                                           f_local, n_kernel, handle), "hffn_down")
 
-    # kernel loop: the local forward's two kernels with per-kernel events (the roofline's timing); on one GPU it is
-    # also the timed step
+    # kernel loop: the local forward's two kernels with per-kernel events (the roofline's timing). The timed step is
+    # the product call without the middle event (one GPU: runtime.forward, whose float32 tensor-core kernels are
+    # chained by programmatic dependent launches that an event between them would serialise; several GPUs: the
+    # sharded forward)
     for marks in ctx.events(args.warmup, 3):
         ctx.flush.zero_()
         marks[0].record(stream)
@@ -449,7 +451,18 @@ def forward_record(ctx: Context, name: str, cpu_seconds: float) -> dict | None:
             kernels(marks)
             marks[2].record(stream)
         torch.cuda.synchronize(device)
-        if world > 1 and args.transport == "peer":
+        if world == 1:
+            for _ in range(args.warmup):
+                ctx.flush.zero_()
+                runtime.forward(0, x)
+            step_events = ctx.events(args.steps)
+            for marks in step_events:
+                ctx.flush.zero_()
+                marks[0].record(stream)
+                runtime.forward(0, x)
+                marks[1].record(stream)
+            torch.cuda.synchronize(device)
+        elif world > 1 and args.transport == "peer":
             # the sharded steps as one pipelined stream of batches (forward_many): batch k's gathers and batch
             # k - 2's deliveries run on the copy engines during batch k - 1's GEMMs; each step's working set
             # (gathered batches, activations, partial outputs) exceeds L2, which is not flushed inside the stream
@@ -618,8 +631,7 @@ def forward_record(ctx: Context, name: str, cpu_seconds: float) -> dict | None:
     }
     if elem == 2:
         record["parity"]["max_rel_vs_fp32_layer"] = error_fp32_layer
-    if world > 1:
-        record["kernel_loop_ms_per_step"] = statistics.mean(a + b for a, b in zip(up_ms, down_ms))
+    record["kernel_loop_ms_per_step"] = statistics.mean(a + b for a, b in zip(up_ms, down_ms))
     if cpu is not None:
         record["cpu_baseline"] = cpu
     return record

@@ -106,6 +106,10 @@ SIGNATURES = {
     "hffn_forward_f16x3_workspace": (_I64, [ctypes.POINTER(Layer), _I64]),
     "hffn_forward_f16x3": (ctypes.c_int, [ctypes.POINTER(Layer), ctypes.POINTER(DenseF16x3), _P, _P, _P, _P, _P, _I64,
                                           _P]),
+    "hffn_f16x3_packet_bytes": (_I64, [_I32]),
+    "hffn_split_f16x3": (ctypes.c_int, [_P, ctypes.POINTER(DenseF16x3), _P, _I32, _I32, _I64, _P]),
+    "hffn_forward_f16x3_packets": (ctypes.c_int, [ctypes.POINTER(Layer), ctypes.POINTER(DenseF16x3), _P, _P, _P, _P,
+                                                  _P, _I64, _P]),
     "hffn_up_f16x3": (ctypes.c_int, [_P, ctypes.POINTER(DenseF16x3), _P, _P, _P, _P, _I32, _I32, _I64, _P]),
     "hffn_down_f16x3": (ctypes.c_int, [_P, ctypes.POINTER(DenseF16x3), _P, _P, _P, _I32, _I32, _I64, _P]),
     "hffn_forward_tc_workspace": (_I64, [ctypes.c_int, ctypes.POINTER(Layer), _I64]),

@@ -44,6 +44,10 @@ int tc_down(int dtype, const void* act_hi, const void* act_lo, const void* w_hi,
 int tc_densify(int dtype, const int32_t* off, const int16_t* idx, const void* val, int rows, int cols, void* hi,
                void* lo, cudaStream_t s);
 int64_t tc_f16_workspace(int d, int H, int64_t n);
+int64_t tc_f16_packet_bytes(int d);
+int tc_split_f16(const float* x, const hffn_dense_f16x3* D, void* packets, int d, int64_t n, cudaStream_t s);
+int tc_forward_f16_packets(const void* packets, const hffn_dense_f16x3* D, const float* b_up, const float* b_down,
+                           float* y, float* z, void* work, int* err, int d, int H, int64_t n, cudaStream_t s);
 int tc_up_f16(const float* x, const hffn_dense_f16x3* D, const float* b, float* z, void* work, int* err, int d, int H,
               int64_t n, cudaStream_t s);
 int tc_down_f16(const void* work, const hffn_dense_f16x3* D, const float* b, float* y, int* err, int d, int H,
@@ -299,6 +303,34 @@ int hffn_down_f16x3(const void* work, const hffn_dense_f16x3* dense, const float
   HFFN_REQUIRE(aligned16(work), "work must be 16-byte aligned");
   HFFN_TRY(bind_stream_device(stream));
   return tc_down_f16(work, dense, b_down, y, err, d_model, d_ff, n, static_cast<cudaStream_t>(stream));
+}
+
+int64_t hffn_f16x3_packet_bytes(int32_t d_model) {
+  if (d_model < 1) return -1;
+  return tc_f16_packet_bytes(d_model);
+}
+
+int hffn_split_f16x3(const float* x, const hffn_dense_f16x3* dense, void* packets, int32_t d_model, int32_t d_ff,
+                     int64_t n, void* stream) {
+  HFFN_TRY(check_tc(HFFN_F32, d_model, d_ff, n));
+  HFFN_REQUIRE(dense != nullptr && dense->up_bound != nullptr, "null up bound");
+  HFFN_REQUIRE(x && packets, "null pointer argument");
+  HFFN_REQUIRE(aligned16(x) && aligned16(packets), "x and packets must be 16-byte aligned");
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_split_f16(x, dense, packets, d_model, n, static_cast<cudaStream_t>(stream));
+}
+
+int hffn_forward_f16x3_packets(const hffn_layer* layer, const hffn_dense_f16x3* dense, const void* packets, float* y,
+                               float* z, void* work, int32_t* err, int64_t n, void* stream) {
+  HFFN_TRY(check_layer(layer));
+  HFFN_TRY(check_tc(HFFN_F32, layer->d_model, layer->d_ff, n));
+  HFFN_TRY(check_dense_f16(dense, true, true));
+  HFFN_REQUIRE(packets && y && work && err, "null pointer argument");
+  HFFN_REQUIRE(aligned16(packets) && aligned16(work), "packets and work must be 16-byte aligned");
+  HFFN_TRY(bind_stream_device(stream));
+  return tc_forward_f16_packets(packets, dense, static_cast<const float*>(layer->b_up),
+                                static_cast<const float*>(layer->b_down), y, z, work, err, layer->d_model, layer->d_ff,
+                                n, static_cast<cudaStream_t>(stream));
 }
 
 int hffn_forward_f16x3(const hffn_layer* layer, const hffn_dense_f16x3* dense, const float* x, float* y, float* z,

@@ -227,11 +227,13 @@ struct EpilogueArgs {
   void* peers[kMaxPeers];
   int64_t tokens_per_owner;
   int64_t rows;          // M
-  // fp16x3 (kUp, kDown): the accumulator of (row, token t) is scaled back by row_inv[row] tok_inv[t];
-  // kUp stores act 2^e_t (act_mul[t] = 2^e_t) as fp16 hi / lo parts into out_hi / out_lo
+  // fp16x3 (kUp, kDown): the accumulator of (row, token t) is scaled back by row_inv[row] times the token's inverse
+  // scale; kUp stores act 2^a_t as fp16 hi / lo parts into out_hi / out_lo. The token scales sit in the token's
+  // packet: tok_tab + t tok_stride holds {x_inv, act_mul = 2^a_t, act_inv = 2^-a_t} (kUp reads the first two, kDown
+  // the third).
   const float* row_inv;
-  const float* tok_inv;
-  const float* act_mul;
+  const float* tok_tab;
+  int64_t tok_stride;
 };
 
 // One value of the output tile: bias added, then (up) GELU and the stores of act (float32: tf32 hi and lo parts) and
@@ -383,62 +385,32 @@ __device__ __forceinline__ void emit_f16_one(const EpilogueArgs* e, int64_t at, 
   }
 }
 
-// fp16x3: four values of one output row, tokens t0 .. t0 + 3 (t0 a multiple of 4; the token tables 16-byte aligned).
+// fp16x3: the scales of token t from its packet (written by the split kernel, read-only here): kUp {x_inv, act_mul}
+// (one 8-byte load), kDown {act_inv, unused}.
 template <int EPI>
-__device__ __forceinline__ void emit4_f16(const EpilogueArgs* e, int row, int t0, int M, int N, float row_inv,
-                                          float bias, float v0, float v1, float v2, float v3) {
-  const int64_t at = (int64_t)t0 * M + row;
-  const int count = N - t0;
-  if (count >= 4) {
-    const float4 ti = *reinterpret_cast<const float4*>(e->tok_inv + t0);
-    float4 am = make_float4(0.f, 0.f, 0.f, 0.f);
-    if constexpr (EPI == kUp) am = *reinterpret_cast<const float4*>(e->act_mul + t0);
-    emit_f16_one<EPI>(e, at, v0, row_inv, ti.x, am.x, bias);
-    emit_f16_one<EPI>(e, at + M, v1, row_inv, ti.y, am.y, bias);
-    emit_f16_one<EPI>(e, at + 2 * (int64_t)M, v2, row_inv, ti.z, am.z, bias);
-    emit_f16_one<EPI>(e, at + 3 * (int64_t)M, v3, row_inv, ti.w, am.w, bias);
-    return;
-  }
-  const float v[3] = {v0, v1, v2};
-#pragma unroll
-  for (int j = 0; j < 3; ++j)
-    if (j < count)
-      emit_f16_one<EPI>(e, at + (int64_t)j * M, v[j], row_inv, e->tok_inv[t0 + j],
-                        EPI == kUp ? e->act_mul[t0 + j] : 0.f, bias);
+__device__ __forceinline__ float2 token_scales(const EpilogueArgs* e, int t) {
+  const float* p = e->tok_tab + (int64_t)t * e->tok_stride;
+  if constexpr (EPI == kUp) return __ldg(reinterpret_cast<const float2*>(p));
+  else return make_float2(__ldg(p + 2), 0.f);
 }
 
-// fp16x3: the values of one output row over the thread's HALF token columns n0 .. n0 + HALF - 1 (sum: the chunk sums).
-// With the whole column part inside [0, N), the token tables (written by the split kernel, read-only here) are read
-// as float4, each group's ahead of the previous group's stores, so that their latency overlaps the GELU of the
-// previous group instead of following its stores.
+// fp16x3: the values of one output row over the thread's HALF token columns n0 .. n0 + HALF - 1 (sum: the chunk sums),
+// in groups of four tokens, the token scales read as float4 from the warp's shared-memory table (tab: the first scale
+// of the warp's columns; the second HALF floats further).
 template <int EPI, int HALF>
-__device__ __forceinline__ void emit_row_f16(const EpilogueArgs* e, int row, int n0, int M, int N, float row_inv,
-                                             float bias, const float (&sum)[HALF]) {
-  if (n0 + HALF > N) {
-#pragma unroll
-    for (int i = 0; i < HALF; i += 4)
-      if (n0 + i < N) emit4_f16<EPI>(e, row, n0 + i, M, N, row_inv, bias, sum[i], sum[i + 1], sum[i + 2], sum[i + 3]);
-    return;
-  }
-  const float4* tok = reinterpret_cast<const float4*>(e->tok_inv + n0);
-  const float4* mul = reinterpret_cast<const float4*>(e->act_mul + n0);
-  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 ti = __ldg(tok), am = EPI == kUp ? __ldg(mul) : zero;
+__device__ __forceinline__ void emit_row_f16(const EpilogueArgs* e, const float* tab, int row, int n0, int M, int N,
+                                             float row_inv, float bias, const float (&sum)[HALF]) {
+  const int count = N - n0 < HALF ? N - n0 : HALF;
   int64_t at = (int64_t)n0 * M + row;
 #pragma unroll
   for (int g = 0; g < HALF / 4; ++g) {
-    float4 ti_next = zero, am_next = zero;
-    if (g + 1 < HALF / 4) {
-      ti_next = __ldg(tok + g + 1);
-      if constexpr (EPI == kUp) am_next = __ldg(mul + g + 1);
-    }
-    emit_f16_one<EPI>(e, at, sum[4 * g], row_inv, ti.x, am.x, bias);
-    emit_f16_one<EPI>(e, at + M, sum[4 * g + 1], row_inv, ti.y, am.y, bias);
-    emit_f16_one<EPI>(e, at + 2 * (int64_t)M, sum[4 * g + 2], row_inv, ti.z, am.z, bias);
-    emit_f16_one<EPI>(e, at + 3 * (int64_t)M, sum[4 * g + 3], row_inv, ti.w, am.w, bias);
+    const float4 a = *reinterpret_cast<const float4*>(tab + 4 * g);
+    const float4 b = EPI == kUp ? *reinterpret_cast<const float4*>(tab + HALF + 4 * g) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float sa[4] = {a.x, a.y, a.z, a.w}, sb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (4 * g + j < count) emit_f16_one<EPI>(e, at + j * (int64_t)M, sum[4 * g + j], row_inv, sa[j], sb[j], bias);
     at += 4 * (int64_t)M;
-    ti = ti_next;
-    am = am_next;
   }
 }
 
@@ -461,8 +433,10 @@ __device__ __noinline__ void sampled_entry(const EpilogueArgs* e, int q, int64_t
   e->dense_lo[dense_at] = tf32_rna(p - hi);
 }
 
-// Shared memory: [stages][A parts][128 rows x 128 B] then [stages][B parts][BN rows x 128 B], 1024-aligned.
-template <bool kBf16, int BN, int STAGES, int RB>
+// Shared memory: [stages][A parts][128 rows x RB bytes] then [stages][B parts][BN rows x RB bytes], 1024-aligned, the
+// barriers, then (fp16x3) each epilogue warp's table of token scales for its columns, [2][HALF] floats per warp (8 BN
+// floats in all).
+template <bool kBf16, int BN, int STAGES, int RB, bool kF16 = false>
 struct Layout {
   static constexpr int kParts = kBf16 ? 1 : 2;
   static constexpr int kA = BM * RB;
@@ -470,7 +444,9 @@ struct Layout {
   static constexpr int kStageBytes = kParts * (kA + kB);
   static constexpr int kOperandBytes = STAGES * kStageBytes;
   static constexpr int kBarrierBytes = 8 * (2 * STAGES + 5) + 16;
-  static constexpr int kTotal = 1024 + kOperandBytes + kBarrierBytes;
+  static constexpr int kTokOffset = kOperandBytes + (kBarrierBytes + 15) / 16 * 16;
+  static constexpr int kTokBytes = kF16 ? 8 * BN * 4 : 0;
+  static constexpr int kTotal = 1024 + kTokOffset + kTokBytes;
   static constexpr int kTmemCols = 2 * BN;
 };
 
@@ -479,7 +455,7 @@ __global__ void __launch_bounds__(threads_for(EW), 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_constant__ CUtensorMap map_a_lo,
                const __grid_constant__ CUtensorMap map_b_hi, const __grid_constant__ CUtensorMap map_b_lo, int M,
                int N, int K, const __grid_constant__ EpilogueArgs epi, int* err) {
-  using L = Layout<kBf16, BN, STAGES, RB>;
+  using L = Layout<kBf16, BN, STAGES, RB, kF16>;
   constexpr int kRowBytes = RB;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -496,6 +472,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN, num_tiles = num_m * num_n;
   static_assert(!(kBf16 && kF16), "fp16x3 operands are a float32 format");
+  static_assert(!kF16 || KCHUNK > 0, "fp16x3 accumulates in chunks");
   constexpr int kElem = kBf16 || kF16 ? 2 : 4;
   const int num_kb = (K * kElem + kRowBytes - 1) / kRowBytes;
   const int k_elems = kRowBytes / kElem;
@@ -530,6 +507,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
   __syncthreads();
   fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch (no-ops in a plain launch): the next kernel of the stream may be scheduled onto SMs
+  // this grid leaves (its prologue overlaps this grid's last tiles); this grid reads its predecessor's outputs only
+  // after the predecessor has completed.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -675,6 +657,22 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
       const int m0 = (tile % num_m) * BM, n_blk = tile / num_m, n0 = n_blk * BN + half * HALF;
       const int row = m0 + quarter * 32 + lane;
+      // fp16x3: the token scales of this warp's columns, read once per tile from the packets (one token per lane)
+      // into the warp's own shared-memory table ([first scale][HALF], [second scale][HALF]) and read back as float4 by
+      // the emit; the warp alone writes and reads it, so it needs no barrier beyond the warp's own
+      float* tok_tab = nullptr;
+      if constexpr (kF16) {
+        tok_tab = reinterpret_cast<float*>(smem + L::kTokOffset) + (warp - 2) * 2 * HALF;
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < HALF / 32; ++c) {
+          const int t = n0 + c * 32 + lane;
+          const float2 v = t < N ? token_scales<EPI>(e, t) : make_float2(0.f, 0.f);
+          tok_tab[c * 32 + lane] = v.x;
+          tok_tab[HALF + c * 32 + lane] = v.y;
+        }
+        __syncwarp();
+      }
       float bias = 0.f;
       if (row < M && e->bias != nullptr) {
         if constexpr (kBf16) bias = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(e->bias)[row]);
@@ -731,7 +729,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
           }
         } else if (row < M) {
           if constexpr (kF16) {
-            emit_row_f16<EPI, HALF>(e, row, n0, M, N, row_inv, bias, sum);
+            emit_row_f16<EPI, HALF>(e, tok_tab, row, n0, M, N, row_inv, bias, sum);
           } else {
 #pragma unroll
             for (int i = 0; i < HALF; i += 4)
@@ -757,14 +755,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
             for (int j = 0; j < 32; j += 4) {
               const int t = n0 + c * 32 + j;
               if (t < N) {
-                if constexpr (kF16) {
-                  emit4_f16<EPI>(e, row, t, M, N, row_inv, bias, v[j], v[j + 1], v[j + 2], v[j + 3]);
-                } else {
-                  const float2 r = emit4_at<kBf16, EPI, HALF>(e, row, t, M, N, bias, v[j], v[j + 1], v[j + 2],
-                                                              v[j + 3]);
-                  partial.x += r.x;
-                  partial.y += r.y;
-                }
+                const float2 r = emit4_at<kBf16, EPI, HALF>(e, row, t, M, N, bias, v[j], v[j + 1], v[j + 2],
+                                                            v[j + 3]);
+                partial.x += r.x;
+                partial.y += r.y;
               }
             }
           }
@@ -919,14 +913,22 @@ __global__ void densify_f16_kernel(const int32_t* __restrict__ off, const int16_
   }
 }
 
-// fp16x3 x operand and token scales: one warp per token row t of x [n, d] (d a multiple of 4, rows 16-byte aligned).
-// x_t 2^e_t (row_exponent of max |x_t|) split into fp16 hi / lo, x_inv[t] = 2^-e_t; act_mul[t] = 2^a_t and
-// act_inv[t] = 2^-a_t with a_t = row_exponent of the bound max(bound[0] max|x_t| + bound[1], 0.17) of |act_t|
-// (|z| <= ||W_up[r]||_1 max|x_t| + |b_up[r]|, and |gelu(z)| <= max(|z|, 0.17)): act 2^a_t stays below 2^15, half of
-// fp16's largest finite value, which leaves room for the rounding of the bound and of z.
+// fp16x3 token packets: token t's row of x as fp16 parts and its scales, one row of packet_halves(d) halves: the hi
+// part at 0, the lo part at part_halves(d), then float32 {x_inv = 2^-e_t, act_mul = 2^a_t, act_inv = 2^-a_t, 0} at
+// 2 part_halves(d); each piece starts on a 64-byte boundary (a part holds d halves rounded up to 32: the TMA rows of
+// the GEMMs then cover whole 32-byte sectors; with 16-byte offsets a 64-byte row read touched three sectors and the up
+// GEMM ran 15 % slower, measured). Packets of several ranks' tokens concatenate into one batch (the neuron-sharded
+// forward gathers them as they are); the GEMMs read the parts through tensor maps with the packet stride.
+__host__ __device__ constexpr int64_t part_halves(int64_t d) { return (d + 31) / 32 * 32; }
+__host__ __device__ constexpr int64_t packet_halves(int64_t d) { return 2 * part_halves(d) + 32; }
+
+// The split: one warp per token row t of x [n, d] (d a multiple of 8, x 16-byte aligned). e_t = row_exponent of
+// max |x_t|; a_t = row_exponent of the bound max(bound[0] max|x_t| + bound[1], 0.17) of |act_t| (|z| <=
+// ||W_up[r]||_1 max|x_t| + |b_up[r]|, and |gelu(z)| <= max(|z|, 0.17)): act 2^a_t stays below 2^15, half of fp16's
+// largest finite value, which leaves room for the rounding of the bound and of z.
 __global__ void split_f16_kernel(const float* __restrict__ x, int64_t n, int d, const float* __restrict__ bound,
-                                 __half* __restrict__ hi, __half* __restrict__ lo, float* __restrict__ x_inv,
-                                 float* __restrict__ act_mul, float* __restrict__ act_inv) {
+                                 __half* __restrict__ packets) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // the up GEMM's prologue may overlap this kernel
   const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= n) return;
@@ -940,8 +942,9 @@ __global__ void split_f16_kernel(const float* __restrict__ x, int64_t n, int d, 
   m = warp_max(m);
   const int e = row_exponent(m);
   const float scale = exp2i(e);
-  uint2* h_row = reinterpret_cast<uint2*>(hi + t * d);
-  uint2* l_row = reinterpret_cast<uint2*>(lo + t * d);
+  __half* packet = packets + t * packet_halves(d);
+  uint2* h_row = reinterpret_cast<uint2*>(packet);
+  uint2* l_row = reinterpret_cast<uint2*>(packet + part_halves(d));
   for (int i = lane; i < d4; i += 32) {
     const float4 v = row[i];
     const float s[4] = {v.x * scale, v.y * scale, v.z * scale, v.w * scale};
@@ -960,10 +963,8 @@ __global__ void split_f16_kernel(const float* __restrict__ x, int64_t n, int d, 
     l_row[i] = pl;
   }
   if (lane == 0) {
-    x_inv[t] = exp2i(-e);
     const int a = row_exponent(fmaxf(bound[0] * m + bound[1], 0.17f));
-    act_mul[t] = exp2i(a);
-    act_inv[t] = exp2i(-a);
+    *reinterpret_cast<float4*>(packet + 2 * part_halves(d)) = make_float4(exp2i(-e), exp2i(a), exp2i(-a), 0.f);
   }
 }
 
@@ -1090,11 +1091,15 @@ static int make_map_mn(CUtensorMap* map, const void* base, int64_t mn, int64_t k
 
 // D[M, N] = A[M, K] B[N, K]^T. K-major operands are [rows, K] with K contiguous; an MN-major operand A (B) is stored
 // [K, M] ([K, N]), its leading dimension lda (ldb) elements.
+// pdl: launched with programmatic stream serialization, so that its CTAs may start (and run the prologue up to
+// griddepcontrol.wait) while the previous kernel of the stream finishes; the previous kernel must be one whose
+// outputs are all this GEMM waits for (the forward's chain: split -> up GEMM -> down GEMM).
 template <bool kBf16, int BN, int STAGES, int EPI, int KCHUNK, int RB, int EW, bool A_MN = false, bool B_MN = false,
           bool kF16 = false>
 static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N, int K,
-                       const EpilogueArgs& epi, int* err, cudaStream_t s, int64_t lda = 0, int64_t ldb = 0) {
-  using L = Layout<kBf16, BN, STAGES, RB>;
+                       const EpilogueArgs& epi, int* err, cudaStream_t s, int64_t lda = 0, int64_t ldb = 0,
+                       bool pdl = false) {
+  using L = Layout<kBf16, BN, STAGES, RB, kF16>;
   static_assert(!((kBf16 || kF16) && (A_MN || B_MN)), "MN-major operands are tf32 parts only");
   constexpr int kElemType = kBf16 ? kElemBf16 : (kF16 ? kElemF16 : kElemF32);
   constexpr int k_box = RB / 4;
@@ -1119,7 +1124,21 @@ static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, con
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kernel<<<grid, threads_for(EW), L::kTotal, s>>>(ma_hi, ma_lo, mb_hi, mb_lo, M, N, K, epi, err);
+  if (!pdl) {
+    kernel<<<grid, threads_for(EW), L::kTotal, s>>>(ma_hi, ma_lo, mb_hi, mb_lo, M, N, K, epi, err);
+    return launch_status("tc_gemm");
+  }
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3((unsigned)grid);
+  config.blockDim = dim3((unsigned)threads_for(EW));
+  config.dynamicSmemBytes = L::kTotal;
+  config.stream = s;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  cudaLaunchKernelEx(&config, kernel, ma_hi, ma_lo, mb_hi, mb_lo, M, N, K, epi, err);
   return launch_status("tc_gemm");
 }
 
@@ -1167,31 +1186,31 @@ static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b
 template <int EPI>
 constexpr int f16_chunk() { return EPI == kUp ? 8 : 4; }
 
-// One fp16x3 forward GEMM: 64-byte rows of fp16 (32 K values a stage, 48 KB: A hi / lo + B hi / lo), the tile widths
+// One fp16x3 forward GEMM (ldb: the row stride of B in elements, 0: K; pdl: launched with programmatic dependent
+// launch, its predecessor in the stream being the kernel that wrote its operands): 64-byte rows of fp16 (32 K values a stage, 48 KB: A hi / lo + B hi / lo), the tile widths
 // and stage counts of the 3xTF32 GEMMs, 16 epilogue warps for up (GELU and the split), 8 for down.
 template <int EPI>
 static int launch_forward_gemm_f16(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N,
-                                   int K, const EpilogueArgs& epi, int* err, cudaStream_t s) {
+                                   int K, const EpilogueArgs& epi, int* err, cudaStream_t s, int64_t ldb, bool pdl) {
   constexpr int kWarps = EPI == kUp ? 16 : 8;
   constexpr int kChunk = f16_chunk<EPI>();
   switch (pick_tile_tokens()) {
     case 64:
       return launch_gemm<false, 64, 6, EPI, kChunk, 64, 8, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi,
-                                                                               err, s);
+                                                                               err, s, 0, ldb, pdl);
     case 128:
       return launch_gemm<false, 128, 5, EPI, kChunk, 64, kWarps, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K,
-                                                                                    epi, err, s);
+                                                                                    epi, err, s, 0, ldb, pdl);
     default:
       return launch_gemm<false, 256, 4, EPI, kChunk, 64, kWarps, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K,
-                                                                                    epi, err, s);
+                                                                                    epi, err, s, 0, ldb, pdl);
   }
 }
 
-// The fp16x3 forward's workspace: x parts [n, d] and act parts [n, H] (fp16 hi, lo), the token tables x_inv, act_mul,
-// act_inv [n] (float32), each piece 256-byte aligned.
+// The fp16x3 forward's workspace: the token packets [n, packet_halves(d)] and the act parts [n, H] (fp16 hi, lo), each
+// piece 256-byte aligned.
 struct F16Work {
-  __half *x_hi, *x_lo, *act_hi, *act_lo;
-  float *x_inv, *act_mul, *act_inv;
+  __half *packets, *act_hi, *act_lo;
 };
 
 static int64_t f16_work(int64_t d, int64_t H, int64_t n, F16Work* w, uint8_t* base) {
@@ -1203,51 +1222,79 @@ static int64_t f16_work(int64_t d, int64_t H, int64_t n, F16Work* w, uint8_t* ba
   };
   F16Work dummy;
   F16Work* t = w ? w : &dummy;
-  t->x_hi = reinterpret_cast<__half*>(take(2 * n * d));
-  t->x_lo = reinterpret_cast<__half*>(take(2 * n * d));
+  t->packets = reinterpret_cast<__half*>(take(2 * n * packet_halves(d)));
   t->act_hi = reinterpret_cast<__half*>(take(2 * n * H));
   t->act_lo = reinterpret_cast<__half*>(take(2 * n * H));
-  t->x_inv = reinterpret_cast<float*>(take(4 * n));
-  t->act_mul = reinterpret_cast<float*>(take(4 * n));
-  t->act_inv = reinterpret_cast<float*>(take(4 * n));
   return off;
+}
+
+// The up GEMM from packets (pdl: its predecessor in the stream is the split kernel that wrote them).
+static int up_from_packets(const __half* packets, const hffn_dense_f16x3* D, const float* b, float* z, __half* act_hi,
+                           __half* act_lo, int* err, int d, int H, int64_t n, bool pdl, cudaStream_t s) {
+  const int64_t stride = packet_halves(d);
+  EpilogueArgs up{};
+  up.bias = b;
+  up.out_hi = act_hi;
+  up.out_lo = act_lo;
+  up.z = z;
+  up.row_inv = D->up_scale;
+  up.tok_tab = reinterpret_cast<const float*>(packets + 2 * part_halves(d));
+  up.tok_stride = stride / 2;
+  return launch_forward_gemm_f16<kUp>(D->up_hi, D->up_lo, packets, packets + part_halves(d), H, (int)n, d, up, err, s,
+                                      stride, pdl);
+}
+
+static int down_from_packets(const __half* packets, const __half* act_hi, const __half* act_lo,
+                             const hffn_dense_f16x3* D, const float* b, float* y, int* err, int d, int H, int64_t n,
+                             cudaStream_t s) {
+  EpilogueArgs dn{};
+  dn.bias = b;
+  dn.out_hi = y;
+  dn.row_inv = D->down_scale;
+  dn.tok_tab = reinterpret_cast<const float*>(packets + 2 * part_halves(d));
+  dn.tok_stride = packet_halves(d) / 2;
+  return launch_forward_gemm_f16<kDown>(D->down_hi, D->down_lo, act_hi, act_lo, d, (int)n, H, dn, err, s, 0, true);
 }
 
 }  // namespace tc
 
 int64_t tc_f16_workspace(int d, int H, int64_t n) { return tc::f16_work(d, H, n, nullptr, nullptr); }
 
-// fp16x3 up: x [n, d] float32 -> act parts and token tables in `work` (z: float32 [n, H] token-major, or NULL).
+int64_t tc_f16_packet_bytes(int d) { return 2 * tc::packet_halves(d); }
+
+// x [n, d] float32 -> token packets [n, packet_halves(d)].
+int tc_split_f16(const float* x, const hffn_dense_f16x3* D, void* packets, int d, int64_t n, cudaStream_t s) {
+  tc::split_f16_kernel<<<(unsigned)ceil_div(n * 32, 256), 256, 0, s>>>(x, n, d, D->up_bound,
+                                                                     reinterpret_cast<__half*>(packets));
+  return launch_status("tc_split_f16");
+}
+
+// fp16x3 up: x [n, d] float32 -> packets and act parts in `work` (z: float32 [n, H] token-major, or NULL).
 int tc_up_f16(const float* x, const hffn_dense_f16x3* D, const float* b, float* z, void* work, int* err, int d, int H,
               int64_t n, cudaStream_t s) {
   tc::F16Work w;
   tc::f16_work(d, H, n, &w, reinterpret_cast<uint8_t*>(work));
-  const int64_t threads = n * 32;
-  tc::split_f16_kernel<<<(unsigned)ceil_div(threads, 256), 256, 0, s>>>(x, n, d, D->up_bound, w.x_hi, w.x_lo, w.x_inv,
-                                                                       w.act_mul, w.act_inv);
-  HFFN_TRY(launch_status("tc_split_f16"));
-  tc::EpilogueArgs up{};
-  up.bias = b;
-  up.out_hi = w.act_hi;
-  up.out_lo = w.act_lo;
-  up.z = z;
-  up.row_inv = D->up_scale;
-  up.tok_inv = w.x_inv;
-  up.act_mul = w.act_mul;
-  return tc::launch_forward_gemm_f16<tc::kUp>(D->up_hi, D->up_lo, w.x_hi, w.x_lo, H, (int)n, d, up, err, s);
+  HFFN_TRY(tc_split_f16(x, D, w.packets, d, n, s));
+  return tc::up_from_packets(w.packets, D, b, z, w.act_hi, w.act_lo, err, d, H, n, true, s);
 }
 
-// fp16x3 down: the act parts and token tables of tc_up_f16 in `work` -> y [n, d] float32.
+// fp16x3 down: the packets and act parts of tc_up_f16 in `work` -> y [n, d] float32.
 int tc_down_f16(const void* work, const hffn_dense_f16x3* D, const float* b, float* y, int* err, int d, int H,
                 int64_t n, cudaStream_t s) {
   tc::F16Work w;
   tc::f16_work(d, H, n, &w, reinterpret_cast<uint8_t*>(const_cast<void*>(work)));
-  tc::EpilogueArgs dn{};
-  dn.bias = b;
-  dn.out_hi = y;
-  dn.row_inv = D->down_scale;
-  dn.tok_inv = w.act_inv;
-  return tc::launch_forward_gemm_f16<tc::kDown>(D->down_hi, D->down_lo, w.act_hi, w.act_lo, d, (int)n, H, dn, err, s);
+  return tc::down_from_packets(w.packets, w.act_hi, w.act_lo, D, b, y, err, d, H, n, s);
+}
+
+// fp16x3 forward of n tokens from packets made by tc_split_f16 (possibly on other ranks and gathered): the up GEMM
+// (a plain launch: its predecessor in the stream need not be the split) and the down GEMM, act parts in `work`.
+int tc_forward_f16_packets(const void* packets, const hffn_dense_f16x3* D, const float* b_up, const float* b_down,
+                           float* y, float* z, void* work, int* err, int d, int H, int64_t n, cudaStream_t s) {
+  tc::F16Work w;
+  tc::f16_work(d, H, n, &w, reinterpret_cast<uint8_t*>(work));
+  const __half* p = reinterpret_cast<const __half*>(packets);
+  HFFN_TRY(tc::up_from_packets(p, D, b_up, z, w.act_hi, w.act_lo, err, d, H, n, false, s));
+  return tc::down_from_packets(p, w.act_hi, w.act_lo, D, b_down, y, err, d, H, n, s);
 }
 
 int tc_densify_f16(const int32_t* off, const int16_t* idx, const float* val, const float* bias, int rows, int cols,

@@ -70,8 +70,12 @@ class ShardedFFN:
     process group."""
 
     def __init__(self, local_forward: Callable[[torch.Tensor, torch.Tensor], None], d_model: int, group=None,
-                 segments: int | None = None, comm_sms: int = 0) -> None:
+                 segments: int | None = None, comm_sms: int = 0, packets=None) -> None:
         self.local_forward = local_forward
+        # packets: the rank-local fp16x3 runtime when its forward can start from token packets: each rank then splits
+        # its own tokens and the packets are gathered (the same bytes as float32 x), instead of every rank splitting
+        # the whole gathered batch
+        self.packets = packets
         self.d_model = d_model
         self.group = group
         self.rank = dist.get_rank(group)
@@ -113,12 +117,19 @@ class ShardedFFN:
         n, d = x_local.shape[0], self.d_model
         segments = max(1, min(segments or self.segments, n))
         bounds = [n * k // segments for k in range(segments + 1)]
-        key = (n, segments, x_local.dtype, x_local.device)
+        packed = self.packets is not None and x_local.is_cuda and all(
+            self.packets.uses_packets(self.world * (bounds[s + 1] - bounds[s])) for s in range(segments))
+        key = (n, segments, x_local.dtype, x_local.device, packed)
         if key not in self._buffers:     # exchange buffers, reused by every call of this shape
-            self._buffers[key] = [(torch.empty(self.world * (bounds[s + 1] - bounds[s]), d, dtype=x_local.dtype,
-                                               device=x_local.device),
+            device = x_local.device
+            row = (self.packets.packet_bytes(),) if packed else (d,)
+            kind = torch.uint8 if packed else x_local.dtype
+            self._buffers[key] = [(torch.empty(self.world * (bounds[s + 1] - bounds[s]), *row, dtype=kind,
+                                               device=device),
                                    torch.empty(self.world * (bounds[s + 1] - bounds[s]), d, dtype=x_local.dtype,
-                                               device=x_local.device)) for s in range(segments)]
+                                               device=device),
+                                   torch.empty(bounds[s + 1] - bounds[s], *row, dtype=kind, device=device)
+                                   if packed else None) for s in range(segments)]
         buffers = self._buffers[key]
         self._cuda = x_local.is_cuda
         if segments > 1:
@@ -126,12 +137,18 @@ class ShardedFFN:
         gathers = []
         for s in range(segments):
             part = x_local[bounds[s]:bounds[s + 1]]
+            if packed:
+                self.packets.split_packets(0, part, buffers[s][2])
+                part = buffers[s][2]
             gathers.append(dist.all_gather_into_tensor(buffers[s][0], part, group=self.group, async_op=True))
         out = torch.empty(n, d, dtype=x_local.dtype, device=x_local.device)
         scatters = []
         for s in range(segments):
             gathers[s].wait()
-            self.local_forward(buffers[s][0], buffers[s][1])
+            if packed:
+                self.packets.forward_packets(0, buffers[s][0], buffers[s][1])
+            else:
+                self.local_forward(buffers[s][0], buffers[s][1])
             scatters.append(self._reduce_scatter(out[bounds[s]:bounds[s + 1]], buffers[s][1]))
         for work in scatters:
             if work is not None:
@@ -176,8 +193,17 @@ def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, ten
     runtime = HFFNRuntime([layer], device, dtype, tensor_cores=tensor_cores, tc_format=tc_format)
     if transport == "peer":
         return runtime, PeerShardedFFN(runtime, d_model, group, push=push), (lo, hi)
+    packets = None
+    if runtime.tensor_cores and runtime.tc_format == "f16x3":
+        # every shard reads the packets every rank makes: their activation scales use the whole layer's bound
+        l1 = torch.zeros(arrays["b_up"].numel(), dtype=torch.float64).index_add_(
+            0, torch.repeat_interleave(torch.arange(arrays["b_up"].numel()), arrays["up_offsets"].cpu().diff().long()),
+            arrays["up_val"].cpu().double().abs())
+        runtime.up_bound_floor = torch.tensor([float(l1.max()), float(arrays["b_up"].cpu().double().abs().max())],
+                                              dtype=torch.float32)
+        packets = runtime
     ffn = ShardedFFN(lambda x, out: runtime.forward(0, x, out=out), d_model, group, segments=segments,
-                     comm_sms=comm_sms)
+                     comm_sms=comm_sms, packets=packets)
     return runtime, ffn, (lo, hi)
 
 

@@ -160,6 +160,9 @@ class HFFNRuntime:
         self._dense16: list[dict | None] = [None] * count
         self._dense16_structs: list = [None] * count
         self._dense16_stale: list[bool] = [True] * count
+        # A floor of the fp16x3 up bound {max row L1 norm, max |b_up|}: a neuron shard whose token packets are read
+        # by the other shards of the same layer sets the whole layer's bound (sharded_runtime)
+        self.up_bound_floor: torch.Tensor | None = None
         self._err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.forced_up: str | None = None
         self.forced_down: str | None = None
@@ -213,6 +216,8 @@ class HFFNRuntime:
                                                    t["out_val"].data_ptr(), None, d, f, dense["down_hi"].data_ptr(),
                                                    dense["down_lo"].data_ptr(), dense["down_scale"].data_ptr(), None,
                                                    stream), "hffn_densify_f16x3 down")
+        if self.up_bound_floor is not None:
+            torch.maximum(dense["up_bound"], self.up_bound_floor.to(device), out=dense["up_bound"])
         self._dense16_stale[index] = False
 
     def forward_operands(self, index: int):
@@ -225,6 +230,45 @@ class HFFNRuntime:
         if self._dense_stale[index]:
             self._densify(index)
         return self.tc_format, self._dense_structs[index]
+
+    def packet_bytes(self) -> int:
+        """Bytes per token of the fp16x3 token packets (``hffn_f16x3_packet_bytes``)."""
+        return int(native.lib.hffn_f16x3_packet_bytes(self.d_model))
+
+    def uses_packets(self, n: int) -> bool:
+        """Whether a call on ``n`` tokens runs the fp16x3 tensor-core forward, which can start from token packets."""
+        return self.tc_format == "f16x3" and self.modes(n)[0] == TC
+
+    def split_packets(self, index: int, x: torch.Tensor, packets: torch.Tensor) -> None:
+        """x [N, d_model] (float32, contiguous, on the device) -> packets (uint8 [N, packet_bytes()]): each token's
+        fp16x3 parts and scales (``hffn_split_f16x3``), the input of ``forward_packets`` here or on another rank
+        holding another shard of the same layer (the up bound of every shard must be that of the whole layer)."""
+        n = self._check_input(x)
+        if packets.dtype != torch.uint8 or packets.shape != (n, self.packet_bytes()) or not packets.is_contiguous():
+            raise ValueError("packets must be a contiguous uint8 [N, packet_bytes()] tensor")
+        _, dense = self.forward_operands(index)
+        native.check(native.lib.hffn_split_f16x3(x.data_ptr(), dense, packets.data_ptr(), self.d_model, self.d_ff, n,
+                                                 native.stream_handle(self.device)), "hffn_split_f16x3")
+
+    def forward_packets(self, index: int, packets: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """``forward`` from token packets (``split_packets``): y [N, d_model] into ``out`` (float32, contiguous)."""
+        n = packets.shape[0]
+        if packets.dtype != torch.uint8 or packets.dim() != 2 or packets.shape[1] != self.packet_bytes() \
+                or not packets.is_contiguous() or packets.device != self._y.device:
+            raise ValueError("packets must be a contiguous uint8 [N, packet_bytes()] tensor on the runtime's device")
+        if out.shape != (n, self.d_model) or out.dtype != torch.float32 or not out.is_contiguous():
+            raise ValueError("out must be a contiguous float32 [N, d_model] tensor")
+        if self.tc_format != "f16x3":
+            raise ValueError("token packets belong to the fp16x3 format")
+        if n > self._tokens:
+            self._reserve(n)
+        _, dense = self.forward_operands(index)
+        native.check(native.lib.hffn_forward_f16x3_packets(self._structs[index], dense, packets.data_ptr(),
+                                                           out.data_ptr(), None, self._tc_work.data_ptr(),
+                                                           self._err.data_ptr(), n, native.stream_handle(self.device)),
+                     "hffn_forward_f16x3_packets")
+        self.calls[TC, TC] += 1
+        return out
 
     def mark_updated(self, index: int, refreshed: str | None = None) -> None:
         """The compact values of layer ``index`` changed (an optimiser step): the dense operands are rebuilt lazily,

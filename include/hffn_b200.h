@@ -239,12 +239,28 @@ int64_t hffn_forward_f16x3_workspace(const hffn_layer* layer, int64_t n);
 int hffn_forward_f16x3(const hffn_layer* layer, const hffn_dense_f16x3* dense, const float* x, float* y, float* z,
                        void* work, int32_t* err, int64_t n, void* stream);
 
-/* The two halves of hffn_forward_f16x3, for callers that run them apart (the neuron-sharded forward, the benchmark's
- * per-kernel timing): hffn_up_f16x3 leaves act and its token scales in `work` for hffn_down_f16x3 over the same n. */
+/* The two halves of hffn_forward_f16x3, for callers that run them apart (the benchmark's per-kernel timing):
+ * hffn_up_f16x3 leaves the token packets and act in `work` for hffn_down_f16x3 over the same n. */
 int hffn_up_f16x3(const float* x, const hffn_dense_f16x3* dense, const float* b_up, float* z, void* work, int32_t* err,
                   int32_t d_model, int32_t d_ff, int64_t n, void* stream);
 int hffn_down_f16x3(const void* work, const hffn_dense_f16x3* dense, const float* b_down, float* y, int32_t* err,
                     int32_t d_model, int32_t d_ff, int64_t n, void* stream);
+
+/* Token packets of the fp16x3 forward: per token, hffn_f16x3_packet_bytes(d_model) = 4 D + 64 bytes (D = d_model
+ * rounded up to 32), the x row scaled by a power of two 2^e_t (its largest |value| into [2^14, 2^15)) as fp16 hi and
+ * lo parts of D halves each (the first d_model used), then float32 {2^-e_t, 2^a_t, 2^-a_t, 0} and 48 bytes of padding
+ * (a_t: the scale of the token's activations, from dense->up_bound; every piece 64-byte aligned). The
+ * packets of several ranks' tokens concatenate into one batch, so the neuron-sharded forward splits each rank's own
+ * tokens once and gathers the packets instead of gathering x and splitting the whole gathered batch on every rank. */
+int64_t hffn_f16x3_packet_bytes(int32_t d_model);
+
+/* x [n, d_model] float32 -> packets [n] (16-byte aligned). */
+int hffn_split_f16x3(const float* x, const hffn_dense_f16x3* dense, void* packets, int32_t d_model, int32_t d_ff,
+                     int64_t n, void* stream);
+
+/* hffn_forward_f16x3 from the packets of its n tokens (work: hffn_forward_f16x3_workspace bytes). */
+int hffn_forward_f16x3_packets(const hffn_layer* layer, const hffn_dense_f16x3* dense, const void* packets, float* y,
+                               float* z, void* work, int32_t* err, int64_t n, void* stream);
 
 /* The tensor-core down projection of a rank's neuron shard, fused with the reduction's transfer: the partial output of
  * token t is stored directly into the receive buffer of the rank that owns t (peer memory over NVLink, plain stores,

@@ -12,6 +12,9 @@
   the bits of ``hffn_forward_f16x3``.
 - After an optimiser step on the tensor cores (which refreshes the tf32 pairs in place), the next fp16x3 forward sees
   the new values.
+- Token packets (``hffn_split_f16x3``, ``hffn_forward_f16x3_packets``): packets split in parts and concatenated give
+  the forward's bits, and two neuron shards of one layer, each running on the packets the other split (the exchange
+  of the sharded forward, emulated on one GPU), sum to the whole layer within the bar.
 """
 import ctypes
 import dataclasses
@@ -170,3 +173,59 @@ def test_forward_follows_tensor_core_training_steps():
     assert not torch.equal(before, after)
     assert float((after - cuda_cores).abs().max()) <= 2e-5
     assert runtime.device_errors() == 0
+
+
+def test_packets_concatenate_and_match_the_forward():
+    """Packets split in two token halves and concatenated give the bits of the forward from x (tokens are
+    independent), through ``forward_packets`` (the entry the neuron-sharded forward calls on gathered packets)."""
+    case = synth.TEST_CASES["irreg_512_2048"]
+    layer = synth.make_layer(case)
+    runtime = runtime_of(layer)
+    n = 600
+    x = torch.from_numpy(synth.make_input(case, n)).cuda()
+    y = runtime.forward(0, x).clone()
+    packets = torch.empty(n, runtime.packet_bytes(), dtype=torch.uint8, device="cuda")
+    runtime.split_packets(0, x[:250].contiguous(), packets[:250])
+    runtime.split_packets(0, x[250:].contiguous(), packets[250:])
+    out = torch.empty(n, case.d_model, device="cuda")
+    runtime.forward_packets(0, packets, out)
+    assert torch.equal(out, y)
+    assert runtime.packet_bytes() == 4 * ((case.d_model + 31) // 32 * 32) + 64
+    assert runtime.device_errors() == 0
+
+
+def test_neuron_shards_read_each_others_packets():
+    """Two neuron shards of one layer on one GPU, each with the whole layer's up bound (as ``sharded_runtime`` sets
+    it): every shard runs on the packets the other shard split, and the sum of the partial outputs meets the float32
+    bar against the oracle of the whole layer (the exchange of the two-GPU sharded forward, emulated)."""
+    from hffn_b200.distributed import neuron_partition, shard_hidden_major
+    from hffn_b200.runtime import HFFNLayer, HFFNRuntime
+    case = synth.TEST_CASES["irreg_512_2048"]
+    layer = synth.make_layer(case)
+    arrays = {k: torch.from_numpy(getattr(layer, k)) for k in ("b_up", "up_offsets", "up_idx", "up_val", "b_down",
+                                                                 "down_offsets", "down_idx", "down_val")}
+    bounds = neuron_partition(arrays, 2)
+    l1 = np.add.reduceat(np.abs(layer.up_val.astype(np.float64)), layer.up_offsets[:-1])
+    floor = torch.tensor([l1.max(), np.abs(layer.b_up).max()], dtype=torch.float32)
+    shards = []
+    for rank in range(2):
+        s = shard_hidden_major(case.d_model, arrays, bounds[rank], bounds[rank + 1], with_bias=rank == 0)
+        kl = HFFNLayer.from_hidden_major(s["d_model"], s["d_ff"], s["b_up"], s["up_offsets"], s["up_idx"],
+                                         s["up_val"], s["b_down"], s["down_offsets"], s["down_idx"], s["down_val"])
+        rt = HFFNRuntime([kl], "cuda", torch.float32, tensor_cores=True)
+        rt.force("tc", "tc")
+        rt.up_bound_floor = floor
+        shards.append(rt)
+    n = 300
+    x_np = synth.make_input(case, n)
+    x = torch.from_numpy(x_np).cuda()
+    packets = [torch.empty(n, shards[0].packet_bytes(), dtype=torch.uint8, device="cuda") for _ in range(2)]
+    for rank in range(2):
+        shards[rank].split_packets(0, x, packets[rank])
+    partial = [torch.empty(n, case.d_model, device="cuda") for _ in range(2)]
+    for rank in range(2):
+        shards[rank].forward_packets(0, packets[1 - rank], partial[rank])
+    y = (partial[0] + partial[1]).double().cpu().numpy()
+    expected = forward64.forward(layer, x_np)
+    assert token_relative(y, expected) <= BAR, token_relative(y, expected)
+    assert all(rt.device_errors() == 0 for rt in shards)
