@@ -74,7 +74,8 @@ COMPOSITE = (("c2_fwd_fp32", "fwd"), ("c2_fwd_bf16", "fwd_bf16"), ("c1_fwd_fp32"
 # on a B200 (dram__bytes_read.sum + dram__bytes_write.sum); the command and the figures are in the named summary under
 # profiles/. Keyed by (workload, kernel, operand format); a kernel without a capture reports null.
 NCU_TRAFFIC = {
-    ("fwd", "tc_gemm_up", "tf32x3"): (142.489e6 + 96.618e6, "profiles/fwd_tensor_cores_c2_fp32.md"),
+    ("fwd", "tc_gemm_up", "f16x3"): (34.428e6 + 25.815e6, "profiles/fwd_tensor_cores_c2_fp32_f16x3.md"),
+    ("fwd", "tc_gemm_up", "tf32x3"): (142.489e6 + 96.618e6, "profiles/fwd_tensor_cores_c2_fp32_tf32x3.md"),
     ("fwd_bf16", "tc_gemm_up", "bf16"): (16.834e6 + 0.433e6, "profiles/fwd_tensor_cores_c2_bf16.md"),
 }
 CLOCK_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
