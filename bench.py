@@ -384,6 +384,7 @@ def forward_record(ctx: Context, name: str, cpu_seconds: float) -> dict | None:
         runtime, shard, (lo, hi) = sharded_runtime(case.d_model, canonical(layer, torch), device, dtype,
                                                    tensor_cores=tensor_cores, segments=args.segments,
                                                    comm_sms=args.comm_sms, transport=args.transport, push=args.push,
+                                                   schedule=args.schedule,
                                                    tc_format=args.tc_format if dtype == torch.float32 else None)
     if args.path == "tensor_cores":
         runtime.force("tc", "tc")
@@ -601,7 +602,10 @@ def forward_record(ctx: Context, name: str, cpu_seconds: float) -> dict | None:
                        f"{'the down GEMM epilogue' if args.push == 'store' else 'copy engines'})")
     else:
         parallelism = (f"neuron-sharded x{world} (all-gather / reduce-scatter pipeline over NCCL, {shard.segments} "
-                       f"segments, {shard.comm_sms} SMs left to NCCL)")
+                       f"segments, {shard.comm_sms} SMs left to NCCL)" if shard.schedule == "collective" else
+                       f"neuron-sharded x{world} (own tokens first while the inputs cross by NCCL point-to-point, "
+                       f"then the peers' tokens and their partial outputs sent to their owners, summed in rank "
+                       f"order; {shard.comm_sms} SMs left to NCCL during the first call)")
     e2e_s = statistics.median(windows[False])
     bytes_in, bytes_out = x_hosts[0].numel() * elem, y_hosts[0].numel() * elem
     tokens = n * world * args.steps
@@ -1124,6 +1128,8 @@ def main() -> int:
     parser.add_argument("--cpu-train-tokens", type=int, default=256, help="training CPU baseline: tokens per step")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--segments", type=int, default=None, help="sharded forward: pipeline segments per step")
+    parser.add_argument("--schedule", choices=("collective", "own_first"), default="collective",
+                        help="sharded forward: gather / reduce-scatter, or own tokens first with point-to-point sends")
     parser.add_argument("--comm-sms", type=int, default=0, help="sharded forward: SMs left to the collectives")
     parser.add_argument("--transport", choices=("nccl", "peer"), default="nccl",
                         help="sharded forward: NCCL collectives or NVLink peer memory (tensor cores)")

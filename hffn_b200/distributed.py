@@ -70,7 +70,10 @@ class ShardedFFN:
     process group."""
 
     def __init__(self, local_forward: Callable[[torch.Tensor, torch.Tensor], None], d_model: int, group=None,
-                 segments: int | None = None, comm_sms: int = 0, packets=None) -> None:
+                 segments: int | None = None, comm_sms: int = 0, packets=None, schedule: str = "collective") -> None:
+        if schedule not in ("collective", "own_first"):
+            raise ValueError("schedule must be 'collective' or 'own_first'")
+        self.schedule = schedule
         self.local_forward = local_forward
         # packets: the rank-local fp16x3 runtime when its forward can start from token packets: each rank then splits
         # its own tokens and the packets are gathered (the same bytes as float32 x), instead of every rank splitting
@@ -80,10 +83,11 @@ class ShardedFFN:
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
-        # Two segments: the gather of the second and the reduction of the first overlap compute, while each
-        # segment's GEMMs keep enough tiles to fill the SMs (measured on 2 x B200: 1 segment 0.515 ms, 2 segments
-        # 0.499 ms, 4 segments 0.72 ms per step).
-        self.segments = segments or (2 if self.world > 1 else 1)
+        # One segment by default: measured on B200 with the fp16x3 forward (C2, 4096 tokens per rank), 1 / 2 / 3 / 4
+        # segments took 336 / 350 / 428 / 504 us per step on 2 GPUs and 1 / 2 / 4 took 662 / 703 / 743 us on 8: the
+        # collectives of a later segment wait for SMs the persistent GEMMs hold, so cutting the batch adds launches
+        # and latency without overlap (leaving 8 to 32 SMs to NCCL did not change that).
+        self.segments = segments or 1
         self.comm_sms = comm_sms
         self._cuda = False
         self._buffers: dict = {}
@@ -114,6 +118,8 @@ class ShardedFFN:
         neuron shard runs on all of them in one call, and the partial outputs are reduce-scattered back to their
         ranks. The collectives are queued asynchronously, so the gather of segment s + 1 and the reduction of
         segment s - 1 overlap the compute of segment s."""
+        if self.schedule == "own_first" and self.world > 1:
+            return self._forward_own_first(x_local)
         n, d = x_local.shape[0], self.d_model
         segments = max(1, min(segments or self.segments, n))
         bounds = [n * k // segments for k in range(segments + 1)]
@@ -157,6 +163,57 @@ class ShardedFFN:
             self._limit_ctas(False)
         return out
 
+    def _run(self, packed: bool, inputs: torch.Tensor, out: torch.Tensor) -> None:
+        if packed:
+            self.packets.forward_packets(0, inputs, out)
+        else:
+            self.local_forward(inputs, out)
+
+    def _forward_own_first(self, x_local: torch.Tensor) -> torch.Tensor:
+        """The ``own_first`` schedule: the rank's inputs (token packets on the fp16x3 path, else x) go to every peer
+        by point-to-point sends while the shard runs on the rank's own tokens; then the shard runs on the peers'
+        tokens (one call over all of them) and each peer is sent the partial outputs of its own tokens; the rank sums
+        the partials of its tokens in rank order (fixed, whatever the arrival order). The same bytes cross NVLink as
+        with the gather / reduce-scatter pair, but the gather overlaps the first call."""
+        n, d, world, rank = x_local.shape[0], self.d_model, self.world, self.rank
+        peers = [(rank + j) % world for j in range(1, world)]
+        packed = self.packets is not None and x_local.is_cuda and self.packets.uses_packets(n) \
+            and self.packets.uses_packets((world - 1) * n)
+        key = ("own_first", n, x_local.dtype, x_local.device, packed)
+        device = x_local.device
+        if key not in self._buffers:
+            row = (self.packets.packet_bytes(),) if packed else (d,)
+            kind = torch.uint8 if packed else x_local.dtype
+            self._buffers[key] = {
+                "own": torch.empty(n, *row, dtype=kind, device=device) if packed else None,
+                "peer_in": torch.empty((world - 1) * n, *row, dtype=kind, device=device),
+                "peer_out": torch.empty((world - 1) * n, d, dtype=x_local.dtype, device=device),
+                "slots": torch.empty(world, n, d, dtype=x_local.dtype, device=device)}
+        buf = self._buffers[key]
+        self._cuda = x_local.is_cuda
+        own = x_local.contiguous()
+        if packed:
+            self.packets.split_packets(0, own, buf["own"])
+            own = buf["own"]
+        ops = []
+        for j, k in enumerate(peers):
+            ops.append(dist.P2POp(dist.isend, own, self._ranks[k], group=self.group))
+            ops.append(dist.P2POp(dist.irecv, buf["peer_in"][j * n:(j + 1) * n], self._ranks[k], group=self.group))
+        self._limit_ctas(True)
+        works = dist.batch_isend_irecv(ops)
+        self._run(packed, own, buf["slots"][rank])
+        for work in works:
+            work.wait()
+        self._limit_ctas(False)
+        self._run(packed, buf["peer_in"], buf["peer_out"])
+        ops = []
+        for j, k in enumerate(peers):
+            ops.append(dist.P2POp(dist.isend, buf["peer_out"][j * n:(j + 1) * n], self._ranks[k], group=self.group))
+            ops.append(dist.P2POp(dist.irecv, buf["slots"][k], self._ranks[k], group=self.group))
+        for work in dist.batch_isend_irecv(ops):
+            work.wait()
+        return sum_in_rank_order(buf["slots"])
+
     def _reduce_scatter(self, out: torch.Tensor, partial: torch.Tensor):
         if dist.get_backend(self.group) == "gloo":      # gloo has no reduce-scatter: all-reduce and keep the slice
             dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.scatter_group)
@@ -166,13 +223,28 @@ class ShardedFFN:
         return dist.reduce_scatter_tensor(out, partial, op=dist.ReduceOp.SUM, group=self.scatter_group, async_op=True)
 
 
+def sum_in_rank_order(slots: torch.Tensor) -> torch.Tensor:
+    """slots[0] + slots[1] + ... in that order (float32 accumulation; ``hffn_sum_slots`` on the device)."""
+    if not slots.is_cuda:
+        out = slots[0].clone()
+        for k in range(1, slots.shape[0]):
+            out += slots[k]
+        return out
+    from . import _native as native
+    out = torch.empty(slots.shape[1:], dtype=slots.dtype, device=slots.device)
+    code = native.F32 if slots.dtype == torch.float32 else native.BF16
+    native.check(native.lib.hffn_sum_slots(code, slots.data_ptr(), slots.shape[0], out.numel(), out.data_ptr(),
+                                           native.stream_handle(slots.device)), "hffn_sum_slots")
+    return out
+
+
 def x_is_cuda(ffn: "ShardedFFN") -> bool:
     return ffn._cuda
 
 
 def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, tensor_cores=None, group=None,
                     segments: int | None = None, comm_sms: int = 0, transport: str = "nccl", push: str = "copy",
-                    tc_format: str | None = None):
+                    tc_format: str | None = None, schedule: str = "collective"):
     """The rank's ``HFFNRuntime`` over its neuron shard and the sharded forward around it: ``transport="nccl"`` a
     ``ShardedFFN`` (collective kernels), ``"peer"`` a ``PeerShardedFFN`` (NVLink peer memory and copy engines,
     pipelined over batches, tensor cores only, ``push`` its delivery mode)."""
@@ -203,7 +275,7 @@ def sharded_runtime(d_model: int, arrays: dict, device, dtype=torch.float32, ten
                                               dtype=torch.float32)
         packets = runtime
     ffn = ShardedFFN(lambda x, out: runtime.forward(0, x, out=out), d_model, group, segments=segments,
-                     comm_sms=comm_sms, packets=packets)
+                     comm_sms=comm_sms, packets=packets, schedule=schedule)
     return runtime, ffn, (lo, hi)
 
 

@@ -2,7 +2,8 @@
 
 Each rank runs its neuron shard through the float64 oracle (standing in for the GPU kernels, which need a B200);
 the collectives are the product's. The sum over ranks of the shard outputs must equal the whole layer's output,
-for a replicated batch (all-reduce) and for per-rank batches (broadcast / reduce pipeline)."""
+for a replicated batch (all-reduce) and for per-rank batches (the gather / reduce-scatter pipeline, and the own-first
+schedule's point-to-point exchange at 2 and 3 ranks)."""
 import os
 import socket
 import types
@@ -68,25 +69,33 @@ def _worker(rank: int, world: int, port: int, results) -> None:
         arrays = canonical(layer)
         bounds = neuron_partition(arrays, world)
         shard = as_layer(shard_hidden_major(layer.d_model, arrays, bounds[rank], bounds[rank + 1], rank == 0))
-        ffn = ShardedFFN(lambda x, out: out.copy_(torch.from_numpy(forward64.forward(shard, x.numpy()))),
-                         layer.d_model, segments=3)
+        local = lambda x, out: out.copy_(torch.from_numpy(forward64.forward(shard, x.numpy())))  # noqa: E731
+        ffn = ShardedFFN(local, layer.d_model, segments=3)
         x_shared = torch.from_numpy(synth.make_input(case, 6)).double()
         y_rep = ffn.forward_replicated(x_shared)
         x_own = torch.from_numpy(synth.make_input(case, 7 + 100 * rank)[:7]).double()
         y_own = ffn.forward(x_own)
         ok_rep = np.allclose(y_rep.numpy(), forward64.forward(layer, x_shared.numpy()), atol=1e-12, rtol=0)
         ok_own = np.allclose(y_own.numpy(), forward64.forward(layer, x_own.numpy()), atol=1e-12, rtol=0)
-        results[rank] = (ok_rep, ok_own)
+        # the own-first schedule (point-to-point exchange, partials summed in rank order), twice: buffers reused
+        first = ShardedFFN(local, layer.d_model, schedule="own_first")
+        ok_first = True
+        for call in range(2):
+            x_k = torch.from_numpy(synth.make_input(case, 9 + 100 * rank + call)[:9]).double()
+            ok_first &= np.allclose(first.forward(x_k).numpy(), forward64.forward(layer, x_k.numpy()), atol=1e-12,
+                                    rtol=0)
+        results[rank] = (ok_rep, ok_own, bool(ok_first))
     finally:
         dist.destroy_process_group()
 
 
-def test_gloo_two_ranks():
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_ranks(world):
     ctx = mp.get_context("spawn")
     manager = ctx.Manager()
     results = manager.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(rank, 2, port, results)) for rank in range(2)]
+    procs = [ctx.Process(target=_worker, args=(rank, world, port, results)) for rank in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -94,7 +103,7 @@ def test_gloo_two_ranks():
         if p.is_alive():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    assert dict(results) == {0: (True, True), 1: (True, True)}
+    assert dict(results) == {rank: (True, True, True) for rank in range(world)}
 
 
 def test_peer_forward_requires_tensor_cores_and_checks_push():
