@@ -1142,15 +1142,21 @@ static int launch_gemm(const void* a_hi, const void* a_lo, const void* b_hi, con
   return launch_status("tc_gemm");
 }
 
-// Token width of the forward GEMMs' tiles: 256 unless g_tile_tokens forces 128 or 64. Measured on B200 over the
-// layer shapes of the single-GPU and neuron-sharded forwards (float32 and bfloat16, one call or token chunks), the
-// 256-wide tile was fastest in every case: a narrower tile reloads the whole 128 x K weight tile per token block, which
-// costs more than the rounds it saves on the persistent grid.
+// Token width of the forward GEMMs' tiles (g_tile_tokens 256, 128 or 64 forces one). Measured on B200 over the layer
+// shapes of the single-GPU and neuron-sharded forwards (float32 and bfloat16, one call or token chunks), the 256-wide
+// tile was fastest wherever it gives the persistent grid a tile for at least half of the SMs (C2's down GEMM: 128 tiles
+// of 256 took 80 us, 256 tiles of 128 took 116 us): a narrower tile reloads the whole 128 x K weight tile per token
+// block. A GEMM with fewer 256-wide tiles than that (a small batch: C1's 256 tokens make 16 up tiles and 4 down
+// tiles) takes 128, or 64 if 128 still leaves more than half of the SMs idle (C1: 78 -> 46 us per forward).
 static std::atomic<int> g_tile_tokens{0};
 
-static int pick_tile_tokens() {
+static int pick_tile_tokens(int M, int N) {
   const int forced = g_tile_tokens.load();
-  return forced == 64 || forced == 128 ? forced : 256;
+  if (forced == 64 || forced == 128 || forced == 256) return forced;
+  const int64_t m_tiles = (M + BM - 1) / BM, sms = sm_count();
+  if (2 * m_tiles * ((N + 255) / 256) >= sms) return 256;
+  if (2 * m_tiles * ((N + 127) / 128) >= sms) return 128;
+  return 64;
 }
 
 // float32 accumulation: the tensor cores' fp32 accumulation in TMEM is not round-to-nearest at every add (measured
@@ -1170,7 +1176,7 @@ static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b
   // float32 up: 16 warps (its tail epilogue, GELU and the tf32 split of 128 x 256 values, would otherwise stall the
   // MMAs; measured 0.212 ms against 0.238 ms with 8 at C2); float32 down: 8 (16 measured slower)
   constexpr int kWarps = kBf16 || EPI == kUp ? 16 : 8;
-  switch (pick_tile_tokens()) {
+  switch (pick_tile_tokens(M, N)) {
     case 64:
       return launch_gemm<kBf16, 64, 6, EPI, kChunk, kRow, 8>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi, err, s);
     case 128:
@@ -1194,7 +1200,7 @@ static int launch_forward_gemm_f16(const void* a_hi, const void* a_lo, const voi
                                    int K, const EpilogueArgs& epi, int* err, cudaStream_t s, int64_t ldb, bool pdl) {
   constexpr int kWarps = EPI == kUp ? 16 : 8;
   constexpr int kChunk = f16_chunk<EPI>();
-  switch (pick_tile_tokens()) {
+  switch (pick_tile_tokens(M, N)) {
     case 64:
       return launch_gemm<false, 64, 6, EPI, kChunk, 64, 8, false, false, true>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi,
                                                                                err, s, 0, ldb, pdl);

@@ -322,8 +322,9 @@ int hffn_peer_barrier(uint32_t* signal, const uint64_t* signal_peer, int32_t wor
  * run alongside the GEMMs. */
 int hffn_set_tc_max_ctas(int32_t max_ctas);
 
-/* Token width of the forward GEMMs' tiles, process-wide: 0 (the default) or 256, or 128 or 64. A tuning knob with no
- * reference counterpart (256 measured fastest on the forward shapes). */
+/* Token width of the forward GEMMs' tiles, process-wide: 0 (the default: 256, or 128 / 64 for a GEMM whose 256-wide
+ * tiles would leave more than half of the SMs idle) or a forced 256, 128 or 64. A tuning knob with no reference
+ * counterpart. */
 int hffn_set_tc_tile_tokens(int32_t tokens);
 
 /* The GEMM engine of the tensor-core path alone (a test entry; no reference counterpart): out [n, m] = (A B^T)^T with
