@@ -25,7 +25,11 @@ from . import _native as native
 UP_MODES = ("coop", "lane", "tile")
 DOWN_MODES = ("coop", "tiled", "blocked")
 TC = "tc"                   # the tensor-core path: up and down together, force("tc", "tc")
-TC_MIN_TOKENS = 256         # the policy's tensor-core threshold (dense operands available)
+# The policy's tensor-core threshold (dense operands available): every N above the decode kernels' range (N <= 8).
+# Measured on B200 against the CUDA-core tile / blocked kernels, N 9 .. 255: the tensor cores (narrow token tiles for
+# small N) were faster at every N on the C1, C2 / C4 and C5 layer shapes in float32 and bfloat16, from 1.6x (C1 fp32,
+# N 9-64) to 30x (C5 bf16, N 255); C2 fp32: 77-79 us against 248-903 us.
+TC_MIN_TOKENS = 9
 MAX_TOKENS = 1 << 24        # the kernels index tokens with 32-bit ints and act with 64-bit offsets
 BLOCK = 512                 # threads of the tiled kernels
 UP_TILE = 32                # largest token tile of the up kernel

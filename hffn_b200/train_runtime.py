@@ -26,7 +26,11 @@ from collections import Counter
 import torch
 
 from . import _native as native
-from .runtime import MAX_TOKENS, TC, TC_MIN_TOKENS, HFFNLayer, HFFNRuntime
+from .runtime import MAX_TOKENS, TC, HFFNLayer, HFFNRuntime
+
+# The training step's tensor-core threshold (the forward's is lower): the tensor-core MSE step contracts over the
+# tokens in its weight-gradient GEMMs and its gates run at 257 to 2100 tokens; below 256 the CUDA-core step runs.
+TC_MIN_TOKENS = 256
 
 PARAMETERS = ("up_val", "b_up", "out_val", "b_down")
 SUPPORTS = ("in_offsets", "in_pos", "in_hidden", "hid_offsets", "hid_pos", "hid_output")
