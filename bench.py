@@ -689,7 +689,8 @@ def train_record(ctx: Context, name: str, cpu_tokens: int) -> dict | None:
     case = synth.CASES[workload["case"]]
     n = workload["n"]
     layer = synth.make_layer(case)
-    runtime = HFFNRuntime([kernel_layer(layer, torch)], device, tensor_cores=False if args.path == "cuda_cores" else None)
+    runtime = HFFNRuntime([kernel_layer(layer, torch)], device, tensor_cores=False if args.path == "cuda_cores" else None,
+                          tc_format=args.tc_format)
     train = HFFNTrainRuntime(runtime, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-2, max_tokens=n,
                              store_gradients=world > 1,
                              tensor_cores={"cuda_cores": False, "tensor_cores": True}.get(args.path))
@@ -749,16 +750,25 @@ def train_record(ctx: Context, name: str, cpu_tokens: int) -> dict | None:
     simt = {"achieved_tflops": flops / seconds / 1e12, "peak_tflops": gemm["fp32_simt_tflops"],
             "frac": flops / seconds / 1e12 / gemm["fp32_simt_tflops"], "peak_source": gemm["source"]}
     if tc:
-        dense_flops = 6 * 2.0 * case.d_model * case.d_ff * n * 3      # six GEMMs, three tf32 passes each
+        dense_flops = 6 * 2.0 * case.d_model * case.d_ff * n * 3      # six GEMMs, three passes each
+        if runtime.tc_format == "f16x3":
+            # the up and down + MSE GEMMs run at the f16 rate, the other four at the tf32 rate: the pipe's peak for
+            # this mix is the harmonic blend (a third of the work at each GEMM's own peak)
+            pipe_peak = 1.0 / ((1 / 3) / pk["bf16_tflops_sustained"] + (2 / 3) / gemm["tf32_tflops"])
+            pipe = {"kind": "f16 x3 (up, down + MSE) and tf32 x3 (the four backward GEMMs)",
+                    "peak_source": "blend of MEASURED_PEAKS.json dense bf16 sustained (f16 rate) for 1/3 of the work and "
+                                   + gemm["source"] + ", TF32 on, for 2/3"}
+        else:
+            pipe_peak = gemm["tf32_tflops"]
+            pipe = {"kind": "tf32 x3 (3xTF32 split)", "peak_source": gemm["source"] + ", TF32 on"}
+        pipe.update(executed_tflops=dense_flops / seconds / 1e12, peak_tflops=pipe_peak,
+                    frac=dense_flops / seconds / 1e12 / pipe_peak)
         roofline = {"bound": "tensor", "kernel": "whole step (six tcgen05 GEMMs)", "achieved": flops / seconds / 1e12,
                     "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                     "frac": flops / seconds / 1e12 / pk["bf16_tflops_sustained"], "traffic": None,
                     "algorithmic_flops": flops, "peak_source": pk_source,
                     "note": "useful sparse FLOPs of measured dense bf16 sustained (a step of milliseconds)",
-                    "tensor_pipe": {"kind": "tf32 x3 (3xTF32 split)", "executed_tflops": dense_flops / seconds / 1e12,
-                                    "peak_tflops": gemm["tf32_tflops"], "peak_source": gemm["source"] + ", TF32 on",
-                                    "frac": dense_flops / seconds / 1e12 / gemm["tf32_tflops"]},
-                    "hbm": hbm, "fp32_cuda_cores": simt}
+                    "tensor_pipe": pipe, "hbm": hbm, "fp32_cuda_cores": simt}
     else:
         roofline = {"bound": "hbm", "kernel": "whole step", "achieved": achieved, "peak": pk["hbm_gbs"],
                     "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None,
@@ -1136,7 +1146,8 @@ def main() -> int:
     parser.add_argument("--push", choices=("copy", "store"), default="copy",
                         help="peer sharded forward: partial outputs pushed by copy engines or by the GEMM epilogue")
     parser.add_argument("--tc-format", choices=("f16x3", "tf32x3"), default=None,
-                        help="operand format of the float32 tensor-core forward (default: f16x3)")
+                        help="operand format of the float32 tensor-core forward and of the training step's up and "
+                             "down + MSE GEMMs (default: f16x3)")
     parser.add_argument("--path", choices=("auto", "cuda_cores", "tensor_cores"), default="auto",
                         help="forward kernels: the runtime policy, the CUDA-core gather kernels, or the tcgen05 path")
     args = parser.parse_args()

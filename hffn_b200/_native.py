@@ -97,7 +97,8 @@ SIGNATURES = {
     "hffn_gemm_tc_f32": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64,
                                         _P, _P]),
     "hffn_train_step_tc_workspace": (_I64, [ctypes.POINTER(Layer), _I64]),
-    "hffn_train_step_tc": (ctypes.c_int, [ctypes.POINTER(Layer), ctypes.POINTER(Dense), _P, _P, _P, _P,
+    "hffn_train_step_tc": (ctypes.c_int, [ctypes.POINTER(Layer), ctypes.POINTER(Dense), ctypes.POINTER(DenseF16x3), _P,
+                                          _P, _P, _P,
                                           ctypes.POINTER(TrainParams), ctypes.POINTER(AdamWStep), _P, _P, _P, _I64,
                                           _I64, _P]),
     "hffn_forward_noalloc_max_bytes": (_I64, []),

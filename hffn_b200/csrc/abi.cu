@@ -36,6 +36,7 @@ int tc_sum_slots(int dtype, const void* slots, int count, int64_t elems, void* o
 int tc_gemm_f32(int a_mn, int b_mn, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
                 float* d, int M, int N, int K, int64_t lda, int64_t ldb, int* err, cudaStream_t s);
 int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, const void* down_hi, const void* down_lo,
+                  const hffn_dense_f16x3* D16,
                   const float* x, const float* target, float* y, float* gx, const hffn_train_params* P,
                   const hffn_adamw_step* opt, float* loss, void* work, int* err, int64_t n, int64_t n_total,
                   cudaStream_t s);
@@ -428,15 +429,17 @@ int64_t hffn_train_step_tc_workspace(const hffn_layer* layer, int64_t n) {
   return tc_train_workspace(layer, n);
 }
 
-int hffn_train_step_tc(const hffn_layer* layer, const hffn_dense* dense, const float* x, const float* target,
-                       float* y, float* gx, const hffn_train_params* params, const hffn_adamw_step* adamw,
-                       float* loss, void* work, int32_t* err, int64_t n, int64_t n_total, void* stream) {
+int hffn_train_step_tc(const hffn_layer* layer, const hffn_dense* dense, const hffn_dense_f16x3* dense16,
+                       const float* x, const float* target, float* y, float* gx, const hffn_train_params* params,
+                       const hffn_adamw_step* adamw, float* loss, void* work, int32_t* err, int64_t n, int64_t n_total,
+                       void* stream) {
   HFFN_TRY(check_layer(layer));
   HFFN_TRY(check_tc(HFFN_F32, layer->d_model, layer->d_ff, n));
   HFFN_REQUIRE(layer->d_model % 32 == 0 && layer->d_ff % 32 == 0,
                "tensor-core training: d_model and d_ff multiples of 32");
   HFFN_REQUIRE(n_total >= n, "n_total below n");
   HFFN_REQUIRE(dense && dense->up_hi && dense->up_lo && dense->down_hi && dense->down_lo, "null dense operand");
+  if (dense16 != nullptr) HFFN_TRY(check_dense_f16(dense16, true, true));
   HFFN_REQUIRE(x && target && y && gx && params && loss && work && err, "null pointer argument");
   HFFN_REQUIRE(aligned16(x) && aligned16(work), "x and the workspace must be 16-byte aligned");
   const bool fused = adamw != nullptr;
@@ -448,8 +451,8 @@ int hffn_train_step_tc(const hffn_layer* layer, const hffn_dense* dense, const f
                    params->b_up.value == layer->b_up && params->b_down.value == layer->b_down,
                "the parameter values must be the layer's arrays");
   HFFN_TRY(bind_stream_device(stream));
-  return tc_train_step(layer, dense->up_hi, dense->up_lo, dense->down_hi, dense->down_lo, x, target, y, gx, params,
-                       adamw, loss, work, err, n, n_total, static_cast<cudaStream_t>(stream));
+  return tc_train_step(layer, dense->up_hi, dense->up_lo, dense->down_hi, dense->down_lo, dense16, x, target, y, gx,
+                       params, adamw, loss, work, err, n, n_total, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -385,13 +385,68 @@ __device__ __forceinline__ void emit_f16_one(const EpilogueArgs* e, int64_t at, 
   }
 }
 
-// fp16x3: the scales of token t from its packet (written by the split kernel, read-only here): kUp {x_inv, act_mul}
-// (one 8-byte load), kDown {act_inv, unused}.
+// fp16x3: the scales of token t from its packet (written by the split kernel, read-only here): up GEMMs {x_inv,
+// act_mul} (one 8-byte load), down GEMMs {act_inv, unused}.
 template <int EPI>
 __device__ __forceinline__ float2 token_scales(const EpilogueArgs* e, int t) {
   const float* p = e->tok_tab + (int64_t)t * e->tok_stride;
-  if constexpr (EPI == kUp) return __ldg(reinterpret_cast<const float2*>(p));
+  if constexpr (EPI == kUp || EPI == kUpT) return __ldg(reinterpret_cast<const float2*>(p));
   else return make_float2(__ldg(p + 2), 0.f);
+}
+
+// fp16x3 training epilogues: four values of one output row, tokens t0 .. t0 + 3 (t0 a multiple of 4; N - t0 of them
+// valid when fewer than four), their token scales sa (x_inv / act_inv) and sb (act_mul). kUpT: z, act 2^a_t as fp16
+// hi / lo token-major (the down GEMM's operand; the same values as the forward's up epilogue) and act as tf32 hi / lo
+// into the feature-major copies (the weight-gradient GEMM's operand); kDownMse: y, the MSE gradient gy as tf32 hi / lo
+// token-major and feature-major, and the partial sums (loss, column sum). Out of line: a thread holds 128 values.
+template <int EPI>
+__device__ __noinline__ float2 emit4t_f16(const EpilogueArgs* e, int row, int t0, int M, int N, float row_inv,
+                                          float bias, float4 v, float4 sa, float4 sb) {
+  static_assert(EPI == kUpT || EPI == kDownMse, "fp16x3 training epilogues");
+  const int count = N - t0;
+  const float vv[4] = {v.x, v.y, v.z, v.w}, a[4] = {sa.x, sa.y, sa.z, sa.w}, b[4] = {sb.x, sb.y, sb.z, sb.w};
+  float h[4] = {0.f, 0.f, 0.f, 0.f}, l[4] = {0.f, 0.f, 0.f, 0.f};
+  float2 acc = make_float2(0.f, 0.f);
+  int64_t at = (int64_t)t0 * M + row;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (count >= 4 || j < count) {
+      const float s = vv[j] * row_inv * a[j] + bias;
+      if constexpr (EPI == kUpT) {
+        if (e->z != nullptr) e->z[at] = s;
+        const float g = gelu(s);
+        const float scaled = g * b[j];
+        const __half hh = __float2half_rn(scaled);
+        reinterpret_cast<__half*>(e->out_hi)[at] = hh;
+        reinterpret_cast<__half*>(e->out_lo)[at] = __float2half_rn(scaled - __half2float(hh));
+        h[j] = tf32_rna(g);
+        l[j] = tf32_rna(g - h[j]);
+      } else {
+        reinterpret_cast<float*>(e->out_hi)[at] = s;
+        const float diff = s - e->target[at];
+        const float g = e->scale * diff;
+        h[j] = tf32_rna(g);
+        l[j] = tf32_rna(g - h[j]);
+        e->gy_hi[at] = h[j];
+        e->gy_lo[at] = l[j];
+        acc.x += diff * diff;
+        acc.y += g;
+      }
+    }
+    at += M;
+  }
+  float* th = e->t_hi + (int64_t)row * e->t_ld + t0;
+  float* tl = e->t_lo + (int64_t)row * e->t_ld + t0;
+  if (count >= 4) {
+    *reinterpret_cast<float4*>(th) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(tl) = make_float4(l[0], l[1], l[2], l[3]);
+  } else {
+    for (int j = 0; j < count; ++j) {
+      th[j] = h[j];
+      tl[j] = l[j];
+    }
+  }
+  return acc;
 }
 
 // fp16x3: the values of one output row over the thread's HALF token columns n0 .. n0 + HALF - 1 (sum: the chunk sums),
@@ -728,7 +783,19 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
             }
           }
         } else if (row < M) {
-          if constexpr (kF16) {
+          if constexpr (kF16 && (EPI == kUpT || EPI == kDownMse)) {
+#pragma unroll
+            for (int g = 0; g < HALF / 4; ++g)
+              if (n0 + 4 * g < N) {
+                const float4 sa = *reinterpret_cast<const float4*>(tok_tab + 4 * g);
+                const float4 sb = *reinterpret_cast<const float4*>(tok_tab + HALF + 4 * g);
+                const float2 r = emit4t_f16<EPI>(e, row, n0 + 4 * g, M, N, row_inv, bias,
+                                                 make_float4(sum[4 * g], sum[4 * g + 1], sum[4 * g + 2], sum[4 * g + 3]),
+                                                 sa, sb);
+                partial.x += r.x;
+                partial.y += r.y;
+              }
+          } else if constexpr (kF16) {
             emit_row_f16<EPI, HALF>(e, tok_tab, row, n0, M, N, row_inv, bias, sum);
           } else {
 #pragma unroll
@@ -1190,7 +1257,7 @@ static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b
 // on the accumulation bias; two chunks let the MMAs run a quarter of a C2 tile ahead of the GELU epilogue), down 4
 // (128 K values: its epilogue is light, and shorter chunks keep its error below the up's).
 template <int EPI>
-constexpr int f16_chunk() { return EPI == kUp ? 8 : 4; }
+constexpr int f16_chunk() { return EPI == kUp || EPI == kUpT ? 8 : 4; }
 
 // One fp16x3 forward GEMM (ldb: the row stride of B in elements, 0: K; pdl: launched with programmatic dependent
 // launch, its predecessor in the stream being the kernel that wrote its operands): 64-byte rows of fp16 (32 K values a stage, 48 KB: A hi / lo + B hi / lo), the tile widths
@@ -1489,10 +1556,13 @@ int64_t tc_train_workspace(const hffn_layer* L, int64_t n) {
   return 4 * tc::train_floats(L->d_model, L->d_ff, n, nullptr, nullptr);
 }
 
+// D16 != NULL: the up GEMM and the down + MSE GEMM run in the fp16x3 format on D16 (fp16x3 operands of the current
+// values) and the token packets of x (in the workspace of x's tf32 parts); their act operand is the fp16 hi / lo pair
+// (in the workspace of act's tf32 pairs). The other four GEMMs and the dense refresh stay on the tf32 pairs.
 int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, const void* down_hi, const void* down_lo,
-                  const float* x, const float* target, float* y, float* gx, const hffn_train_params* P,
-                  const hffn_adamw_step* opt, float* loss, void* work, int* err, int64_t n, int64_t n_total,
-                  cudaStream_t s) {
+                  const hffn_dense_f16x3* D16, const float* x, const float* target, float* y, float* gx,
+                  const hffn_train_params* P, const hffn_adamw_step* opt, float* loss, void* work, int* err, int64_t n,
+                  int64_t n_total, cudaStream_t s) {
   using namespace tc;
   const int d = L->d_model, H = L->d_ff, nn = (int)n;
   TrainWork w;
@@ -1506,12 +1576,24 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   float* dense_dn_hi = const_cast<float*>(reinterpret_cast<const float*>(down_hi));
   float* dense_dn_lo = const_cast<float*>(reinterpret_cast<const float*>(down_lo));
 
-  // x -> tf32 hi / lo
-  const int64_t count4 = n * d / 4;
-  split_kernel<<<(int)std::min<int64_t>(std::max<int64_t>(ceil_div(count4, 256), 1), 148 * 8), 256, 0, s>>>(
-      reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(w.x_hi), reinterpret_cast<float4*>(w.x_lo),
-      count4);
-  HFFN_TRY(launch_status("tc_split"));
+  // x -> tf32 hi / lo (3xTF32 up GEMM) or token packets (fp16x3), over the same workspace
+  __half* packets = reinterpret_cast<__half*>(w.x_hi);
+  __half* act16_hi = reinterpret_cast<__half*>(w.act_hi);
+  __half* act16_lo = act16_hi + n * H;
+  if (D16 != nullptr) {
+    if ((int64_t)((reinterpret_cast<uint8_t*>(w.z) - reinterpret_cast<uint8_t*>(w.x_hi))) < 2 * n * packet_halves(d)) {
+      set_error("training step: the token packets do not fit the workspace of x's parts (d_model %d)", d);
+      return HFFN_ERR_ARGUMENT;
+    }
+    split_f16_kernel<<<(unsigned)ceil_div(n * 32, 256), 256, 0, s>>>(x, n, d, D16->up_bound, packets);
+    HFFN_TRY(launch_status("tc_split_f16"));
+  } else {
+    const int64_t count4 = n * d / 4;
+    split_kernel<<<(int)std::min<int64_t>(std::max<int64_t>(ceil_div(count4, 256), 1), 148 * 8), 256, 0, s>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(w.x_hi), reinterpret_cast<float4*>(w.x_lo),
+        count4);
+    HFFN_TRY(launch_status("tc_split"));
+  }
   split_transpose_kernel<<<dim3((unsigned)ceil_div(n, 32), (unsigned)ceil_div(d, 32)), dim3(32, 8), 0, s>>>(
       x, n, d, w.xt_hi, w.xt_lo, w.t_ld);
   HFFN_TRY(launch_status("tc_split_transpose"));
@@ -1526,8 +1608,18 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   e1.t_hi = w.actt_hi;
   e1.t_lo = w.actt_lo;
   e1.t_ld = w.t_ld;
-  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kUpT, kFp32Chunk, 64, 8>(up_hi, up_lo, w.x_hi, w.x_lo, H, nn, d, e1, err,
-                                                                     s)));
+  if (D16 != nullptr) {
+    e1.out_hi = act16_hi;
+    e1.out_lo = act16_lo;
+    e1.row_inv = D16->up_scale;
+    e1.tok_tab = reinterpret_cast<const float*>(packets + 2 * part_halves(d));
+    e1.tok_stride = packet_halves(d) / 2;
+    HFFN_TRY((launch_gemm<false, kTrainBN, 4, kUpT, f16_chunk<kUpT>(), 64, 8, false, false, true>(
+        D16->up_hi, D16->up_lo, packets, packets + part_halves(d), H, nn, d, e1, err, s, 0, packet_halves(d))));
+  } else {
+    HFFN_TRY((launch_gemm<false, kTrainBN, 4, kUpT, kFp32Chunk, 64, 8>(up_hi, up_lo, w.x_hi, w.x_lo, H, nn, d, e1, err,
+                                                                       s)));
+  }
   // 2. down + MSE: y, gy = 2 (y - target) / (n_total d) (+ gy^T)  D[d, n] = W_down[d, H] act[n, H]^T
   EpilogueArgs e2{};
   e2.bias = L->b_down;
@@ -1541,8 +1633,16 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   e2.t_hi = w.gyt_hi;
   e2.t_lo = w.gyt_lo;
   e2.t_ld = w.t_ld;
-  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDownMse, kFp32Chunk, 64, 8>(down_hi, down_lo, w.act_hi, w.act_lo, d, nn,
-                                                                          H, e2, err, s)));
+  if (D16 != nullptr) {
+    e2.row_inv = D16->down_scale;
+    e2.tok_tab = reinterpret_cast<const float*>(packets + 2 * part_halves(d));
+    e2.tok_stride = packet_halves(d) / 2;
+    HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDownMse, f16_chunk<kDownMse>(), 64, 8, false, false, true>(
+        D16->down_hi, D16->down_lo, act16_hi, act16_lo, d, nn, H, e2, err, s)));
+  } else {
+    HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDownMse, kFp32Chunk, 64, 8>(down_hi, down_lo, w.act_hi, w.act_lo, d,
+                                                                            nn, H, e2, err, s)));
+  }
   // 3. gz = (W_down^T gy) * gelu'(z) (+ gz^T)                      D[H, n] = W_down^T[H, d] gy[n, d]^T
   EpilogueArgs e3{};
   e3.out_hi = w.gz_hi;

@@ -299,8 +299,12 @@ class HFFNTrainRuntime:
         self._reserve_tc(n)
         if runtime._dense_stale[index]:
             runtime._densify(index)
+        # fp16x3 runtimes: the step's up and down + MSE GEMMs run on the fp16x3 operands (rebuilt from the current
+        # values when stale, as after every applied step), the other four on the tf32 pairs
+        dense16 = runtime.forward_operands(index)[1] if runtime.tc_format == "f16x3" else None
         params = self._fused_structs[index] if apply else self._param_structs[index]
-        status = native.lib.hffn_train_step_tc(runtime._structs[index], runtime._dense_structs[index], x.data_ptr(),
+        status = native.lib.hffn_train_step_tc(runtime._structs[index], runtime._dense_structs[index], dense16,
+                                               x.data_ptr(),
                                                target.data_ptr(), runtime._y.data_ptr(), self._gx.data_ptr(), params,
                                                self._next_step(index) if apply else None, self._loss.data_ptr(),
                                                self._tc_work.data_ptr(), runtime._err.data_ptr(), n, n_total or n,

@@ -336,7 +336,7 @@ int hffn_gemm_tc_f32(int a_mn, int b_mn, const float* a_hi, const float* a_lo, c
 /* Bytes of the workspace hffn_train_step_tc needs for n tokens. */
 int64_t hffn_train_step_tc_workspace(const hffn_layer* layer, int64_t n);
 
-/* One MSE training step on the tcgen05 tensor cores (float32, 3xTF32): forward, loss, backward and AdamW, the
+/* One MSE training step on the tcgen05 tensor cores (float32): forward, loss, backward and AdamW, the
  * tensor-core form of HFFNTrainRuntime.step (runtime/gpu/nvidia/ffn/training/train_runtime.py:209-214) with the
  * training benchmark's MSE loss. Six GEMMs over the dense operands (up; down with the MSE gradient in its epilogue;
  * W_down^T gy with gelu'; W_up^T gz; gy^T act and gz^T x sampled on the supports). With adamw != NULL every gradient
@@ -345,10 +345,13 @@ int64_t hffn_train_step_tc_workspace(const hffn_layer* layer, int64_t n);
  * adamw == NULL the gradients are stored and nothing is updated (data parallelism: exchange, then hffn_adamw and
  * hffn_densify). gy = 2 (y - target) / (n_total d_model); *loss = mean((y - target)^2) over this call's n tokens.
  * Requires d_model and d_ff multiples of 32 and, for the sampled update, the up slots of each neuron in ascending
- * input order (the output-major down edges always are). x, target, y, gx token-major [n, d_model]. */
-int hffn_train_step_tc(const hffn_layer* layer, const hffn_dense* dense, const float* x, const float* target,
-                       float* y, float* gx, const hffn_train_params* params, const hffn_adamw_step* adamw,
-                       float* loss, void* work, int32_t* err, int64_t n, int64_t n_total, void* stream);
+ * input order (the output-major down edges always are). x, target, y, gx token-major [n, d_model]. The GEMMs run on
+ * the 3xTF32 pairs of `dense`, except with dense16 != NULL (fp16x3 operands of the same, current values, from
+ * hffn_densify_f16x3) the up GEMM and the down + MSE GEMM, which then run in the fp16x3 format at the f16 rate. */
+int hffn_train_step_tc(const hffn_layer* layer, const hffn_dense* dense, const hffn_dense_f16x3* dense16,
+                       const float* x, const float* target, float* y, float* gx, const hffn_train_params* params,
+                       const hffn_adamw_step* adamw, float* loss, void* work, int32_t* err, int64_t n, int64_t n_total,
+                       void* stream);
 
 /* Forward that allocates nothing and needs no workspace from the caller. No counterpart in the reference.
  * Some callers can hand this library only their input and output buffers: a plugin whose host framework owns every
