@@ -695,6 +695,7 @@ def train_record(ctx: Context, name: str, cpu_tokens: int) -> dict | None:
                              store_gradients=world > 1,
                              tensor_cores={"cuda_cores": False, "tensor_cores": True}.get(args.path))
     tc = train.uses_tensor_cores(0, n)
+    tc_format = runtime.tc_format
     train.reserve(n)
     x_host = torch.from_numpy(rank_input(case, n, rank)).pin_memory()
     target_host = torch.from_numpy(rank_target(case, n, rank)).pin_memory()
@@ -751,13 +752,14 @@ def train_record(ctx: Context, name: str, cpu_tokens: int) -> dict | None:
             "frac": flops / seconds / 1e12 / gemm["fp32_simt_tflops"], "peak_source": gemm["source"]}
     if tc:
         dense_flops = 6 * 2.0 * case.d_model * case.d_ff * n * 3      # six GEMMs, three passes each
-        if runtime.tc_format == "f16x3":
-            # the up and down + MSE GEMMs run at the f16 rate, the other four at the tf32 rate: the pipe's peak for
-            # this mix is the harmonic blend (a third of the work at each GEMM's own peak)
-            pipe_peak = 1.0 / ((1 / 3) / pk["bf16_tflops_sustained"] + (2 / 3) / gemm["tf32_tflops"])
-            pipe = {"kind": "f16 x3 (up, down + MSE) and tf32 x3 (the four backward GEMMs)",
-                    "peak_source": "blend of MEASURED_PEAKS.json dense bf16 sustained (f16 rate) for 1/3 of the work and "
-                                   + gemm["source"] + ", TF32 on, for 2/3"}
+        if tc_format == "f16x3":
+            # four GEMMs (up, down + MSE, W_down^T gy, W_up^T gz) run at the f16 rate, the two sampled weight-gradient
+            # GEMMs at the tf32 rate: the pipe's peak for this mix is the harmonic blend (each GEMM a sixth of the work)
+            pipe_peak = 1.0 / ((2 / 3) / pk["bf16_tflops_sustained"] + (1 / 3) / gemm["tf32_tflops"])
+            pipe = {"kind": "f16 x3 (up, down + MSE, W_down^T gy, W_up^T gz) and tf32 x3 (the two sampled "
+                            "weight-gradient GEMMs)",
+                    "peak_source": "blend of MEASURED_PEAKS.json dense bf16 sustained (f16 rate) for 2/3 of the work and "
+                                   + gemm["source"] + ", TF32 on, for 1/3"}
         else:
             pipe_peak = gemm["tf32_tflops"]
             pipe = {"kind": "tf32 x3 (3xTF32 split)", "peak_source": gemm["source"] + ", TF32 on"}

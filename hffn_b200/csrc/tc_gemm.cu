@@ -395,14 +395,15 @@ __device__ __forceinline__ float2 token_scales(const EpilogueArgs* e, int t) {
 }
 
 // fp16x3 training epilogues: four values of one output row, tokens t0 .. t0 + 3 (t0 a multiple of 4; N - t0 of them
-// valid when fewer than four), their token scales sa (x_inv / act_inv) and sb (act_mul). kUpT: z, act 2^a_t as fp16
-// hi / lo token-major (the down GEMM's operand; the same values as the forward's up epilogue) and act as tf32 hi / lo
-// into the feature-major copies (the weight-gradient GEMM's operand); kDownMse: y, the MSE gradient gy as tf32 hi / lo
-// token-major and feature-major, and the partial sums (loss, column sum). Out of line: a thread holds 128 values.
+// valid when fewer than four), their token scales sa (the B operand's inverse scale) and sb (act_mul). kUpT: z, act
+// 2^a_t as fp16 hi / lo token-major (the down GEMM's operand; the same values as the forward's up epilogue) and act as
+// tf32 hi / lo into the feature-major copies (the weight-gradient GEMM's operand); kDownMse: y, the MSE gradient gy as
+// tf32 hi / lo token-major and feature-major, and the partial sums (loss, column sum); kGradHidden: gz = acc gelu'(z)
+// as tf32 hi / lo token-major and feature-major, and the column sum. Out of line: a thread holds up to 128 values.
 template <int EPI>
 __device__ __noinline__ float2 emit4t_f16(const EpilogueArgs* e, int row, int t0, int M, int N, float row_inv,
                                           float bias, float4 v, float4 sa, float4 sb) {
-  static_assert(EPI == kUpT || EPI == kDownMse, "fp16x3 training epilogues");
+  static_assert(EPI == kUpT || EPI == kDownMse || EPI == kGradHidden, "fp16x3 training epilogues");
   const int count = N - t0;
   const float vv[4] = {v.x, v.y, v.z, v.w}, a[4] = {sa.x, sa.y, sa.z, sa.w}, b[4] = {sb.x, sb.y, sb.z, sb.w};
   float h[4] = {0.f, 0.f, 0.f, 0.f}, l[4] = {0.f, 0.f, 0.f, 0.f};
@@ -421,6 +422,13 @@ __device__ __noinline__ float2 emit4t_f16(const EpilogueArgs* e, int row, int t0
         reinterpret_cast<__half*>(e->out_lo)[at] = __float2half_rn(scaled - __half2float(hh));
         h[j] = tf32_rna(g);
         l[j] = tf32_rna(g - h[j]);
+      } else if constexpr (EPI == kGradHidden) {
+        const float g = s * gelu_grad(e->z_in[at]);
+        h[j] = tf32_rna(g);
+        l[j] = tf32_rna(g - h[j]);
+        reinterpret_cast<float*>(e->out_hi)[at] = h[j];
+        reinterpret_cast<float*>(e->out_lo)[at] = l[j];
+        acc.y += g;
       } else {
         reinterpret_cast<float*>(e->out_hi)[at] = s;
         const float diff = s - e->target[at];
@@ -783,7 +791,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
             }
           }
         } else if (row < M) {
-          if constexpr (kF16 && (EPI == kUpT || EPI == kDownMse)) {
+          if constexpr (kF16 && (EPI == kUpT || EPI == kDownMse || EPI == kGradHidden)) {
 #pragma unroll
             for (int g = 0; g < HALF / 4; ++g)
               if (n0 + 4 * g < N) {
@@ -1032,6 +1040,90 @@ __global__ void split_f16_kernel(const float* __restrict__ x, int64_t n, int d, 
   if (lane == 0) {
     const int a = row_exponent(fmaxf(bound[0] * m + bound[1], 0.17f));
     *reinterpret_cast<float4*>(packet + 2 * part_halves(d)) = make_float4(exp2i(-e), exp2i(a), exp2i(-a), 0.f);
+  }
+}
+
+// fp16x3 packets of a float32 operand held as tf32 hi / lo pairs [n, K] (the training step's gy and gz, the B operands of
+// its backward GEMMs): one warp per token row, v = hi + lo scaled by 2^e_t (row_exponent of its largest |v|) and split
+// into fp16 hi / lo, the table {0, 0, 2^-e_t, 0} (the down-type epilogues read the third entry).
+__global__ void split_pair_f16_kernel(const float* __restrict__ hi, const float* __restrict__ lo, int64_t n, int K,
+                                      __half* __restrict__ packets) {
+  const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= n) return;
+  const float4* rh = reinterpret_cast<const float4*>(hi + t * K);
+  const float4* rl = reinterpret_cast<const float4*>(lo + t * K);
+  const int k4 = K >> 2;
+  float m = 0.f;
+  for (int i = lane; i < k4; i += 32) {
+    const float4 a = rh[i], b = rl[i];
+    m = fmaxf(m, fmaxf(fmaxf(fabsf(a.x + b.x), fabsf(a.y + b.y)), fmaxf(fabsf(a.z + b.z), fabsf(a.w + b.w))));
+  }
+  m = warp_max(m);
+  const int e = row_exponent(m);
+  const float scale = exp2i(e);
+  __half* packet = packets + t * packet_halves(K);
+  uint2* h_row = reinterpret_cast<uint2*>(packet);
+  uint2* l_row = reinterpret_cast<uint2*>(packet + part_halves(K));
+  for (int i = lane; i < k4; i += 32) {
+    const float4 a = rh[i], b = rl[i];
+    const float sv[4] = {(a.x + b.x) * scale, (a.y + b.y) * scale, (a.z + b.z) * scale, (a.w + b.w) * scale};
+    __half h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      h[j] = __float2half_rn(sv[j]);
+      l[j] = __float2half_rn(sv[j] - __half2float(h[j]));
+    }
+    uint2 ph, pl;
+    ph.x = (uint32_t)__half_as_ushort(h[0]) | ((uint32_t)__half_as_ushort(h[1]) << 16);
+    ph.y = (uint32_t)__half_as_ushort(h[2]) | ((uint32_t)__half_as_ushort(h[3]) << 16);
+    pl.x = (uint32_t)__half_as_ushort(l[0]) | ((uint32_t)__half_as_ushort(l[1]) << 16);
+    pl.y = (uint32_t)__half_as_ushort(l[2]) | ((uint32_t)__half_as_ushort(l[3]) << 16);
+    h_row[i] = ph;
+    l_row[i] = pl;
+  }
+  if (lane == 0) *reinterpret_cast<float4*>(packet + 2 * part_halves(K)) = make_float4(0.f, 0.f, exp2i(-e), 0.f);
+}
+
+// The transposed fp16x3 operand of a dense fp16x3 matrix [R, C] (hi, lo, per-row inverse scales; R and C multiples of
+// 32), in two passes. colmax: the largest |w| of each column (atomicMax on the bits of non-negative floats; zeroed
+// before). transpose: 32 x 32 tiles through shared memory, w = (hi + lo) row_inv of the source written as the row
+// c of the result, scaled by 2^e_c (row_exponent of the column's largest) and split into fp16 hi / lo, inv[c] = 2^-e_c.
+__global__ void colmax_f16_kernel(const __half* __restrict__ hi, const __half* __restrict__ lo,
+                                  const float* __restrict__ row_inv, int R, int C, int rows_per_block,
+                                  unsigned* __restrict__ colmax) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(R, r0 + rows_per_block);
+  float m = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const int64_t at = (int64_t)r * C + c;
+    m = fmaxf(m, fabsf((__half2float(hi[at]) + __half2float(lo[at])) * row_inv[r]));
+  }
+  atomicMax(colmax + c, __float_as_uint(m));
+}
+
+__global__ void transpose_f16_kernel(const __half* __restrict__ hi, const __half* __restrict__ lo,
+                                     const float* __restrict__ row_inv, int R, int C,
+                                     const unsigned* __restrict__ colmax, __half* __restrict__ out_hi,
+                                     __half* __restrict__ out_lo, float* __restrict__ out_inv) {
+  __shared__ float tile[32][33];
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t at = (int64_t)(r0 + i) * C + c0 + threadIdx.x;
+    tile[i][threadIdx.x] = (__half2float(hi[at]) + __half2float(lo[at])) * row_inv[r0 + i];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = c0 + i;
+    const int e = row_exponent(__uint_as_float(colmax[c]));
+    const float v = tile[threadIdx.x][i] * exp2i(e);
+    const __half h = __float2half_rn(v);
+    const int64_t at = (int64_t)c * R + r0 + threadIdx.x;
+    out_hi[at] = h;
+    out_lo[at] = __float2half_rn(v - __half2float(h));
+    if (blockIdx.y == 0 && threadIdx.x == 0) out_inv[c] = exp2i(-e);
   }
 }
 
@@ -1489,6 +1581,11 @@ struct TrainWork {
   uint32_t *dn_mask, *up_mask;
   int32_t *dn_first, *up_first;
   int64_t t_ld, dn_ld, up_ld;
+  // fp16x3 backward GEMMs: W_down^T [H, d] and W_up^T [d, H] as fp16 hi / lo with their rows' inverse scales, and the
+  // column maxima of the transposes
+  __half *dnt_hi, *dnt_lo, *upt_hi, *upt_lo;
+  float *dnt_inv, *upt_inv;
+  unsigned *colmax_dn, *colmax_up;
 };
 
 static int64_t mask_words(int64_t cols) { return (cols + kTrainBN - 1) / kTrainBN * (kTrainBN / 32); }
@@ -1535,6 +1632,19 @@ static int64_t train_floats(int64_t d, int64_t H, int64_t n, TrainWork* w, float
   t->dn_first = reinterpret_cast<int32_t*>(tables[1]);
   t->up_mask = reinterpret_cast<uint32_t*>(tables[2]);
   t->up_first = reinterpret_cast<int32_t*>(tables[3]);
+  float* parts[4] = {};
+  for (int k = 0; k < 4; ++k) take(&parts[k], d * H / 2);     // d H halves each
+  t->dnt_hi = reinterpret_cast<__half*>(parts[0]);
+  t->dnt_lo = reinterpret_cast<__half*>(parts[1]);
+  t->upt_hi = reinterpret_cast<__half*>(parts[2]);
+  t->upt_lo = reinterpret_cast<__half*>(parts[3]);
+  take(&t->dnt_inv, H);
+  take(&t->upt_inv, d);
+  float* maxima[2] = {};
+  take(&maxima[0], H);
+  take(&maxima[1], d);
+  t->colmax_dn = reinterpret_cast<unsigned*>(maxima[0]);
+  t->colmax_up = reinterpret_cast<unsigned*>(maxima[1]);
   return off;
 }
 
@@ -1556,9 +1666,11 @@ int64_t tc_train_workspace(const hffn_layer* L, int64_t n) {
   return 4 * tc::train_floats(L->d_model, L->d_ff, n, nullptr, nullptr);
 }
 
-// D16 != NULL: the up GEMM and the down + MSE GEMM run in the fp16x3 format on D16 (fp16x3 operands of the current
-// values) and the token packets of x (in the workspace of x's tf32 parts); their act operand is the fp16 hi / lo pair
-// (in the workspace of act's tf32 pairs). The other four GEMMs and the dense refresh stay on the tf32 pairs.
+// D16 != NULL: four GEMMs run in the fp16x3 format: the up GEMM and the down + MSE GEMM on D16 (fp16x3 operands of
+// the current values) and the token packets of x (in the workspace of x's tf32 parts), their act operand the fp16 hi /
+// lo pair (in the workspace of act's tf32 pairs); W_down^T gy and W_up^T gz on the transposes of D16 (built here) and
+// the token packets of gy and gz (over the x and act workspaces, dead by then). The two sampled weight-gradient GEMMs
+// and the dense refresh stay on the tf32 pairs.
 int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, const void* down_hi, const void* down_lo,
                   const hffn_dense_f16x3* D16, const float* x, const float* target, float* y, float* gx,
                   const hffn_train_params* P, const hffn_adamw_step* opt, float* loss, void* work, int* err, int64_t n,
@@ -1581,8 +1693,10 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   __half* act16_hi = reinterpret_cast<__half*>(w.act_hi);
   __half* act16_lo = act16_hi + n * H;
   if (D16 != nullptr) {
-    if ((int64_t)((reinterpret_cast<uint8_t*>(w.z) - reinterpret_cast<uint8_t*>(w.x_hi))) < 2 * n * packet_halves(d)) {
-      set_error("training step: the token packets do not fit the workspace of x's parts (d_model %d)", d);
+    if ((int64_t)((reinterpret_cast<uint8_t*>(w.z) - reinterpret_cast<uint8_t*>(w.x_hi))) < 2 * n * packet_halves(d) ||
+        (int64_t)((reinterpret_cast<uint8_t*>(w.gy_hi) - reinterpret_cast<uint8_t*>(w.act_hi))) <
+            2 * n * packet_halves(H)) {
+      set_error("training step: the token packets do not fit the workspace (d_model %d, d_ff %d)", d, H);
       return HFFN_ERR_ARGUMENT;
     }
     split_f16_kernel<<<(unsigned)ceil_div(n * 32, 256), 256, 0, s>>>(x, n, d, D16->up_bound, packets);
@@ -1599,6 +1713,28 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   HFFN_TRY(launch_status("tc_split_transpose"));
   HFFN_TRY(build_support_tables(L->out_offsets, L->out_hidden, d, w.dn_ld, w.dn_mask, w.dn_first, s));
   HFFN_TRY(build_support_tables(L->up_offsets, L->up_idx, H, w.up_ld, w.up_mask, w.up_first, s));
+  if (D16 != nullptr) {
+    // W_down^T [H, d] and W_up^T [d, H] in fp16x3, from the step's fp16x3 operands: the backward GEMMs' A operands,
+    // K-major
+    if (cudaMemsetAsync(w.colmax_dn, 0, (size_t)H * 4, s) != cudaSuccess ||
+        cudaMemsetAsync(w.colmax_up, 0, (size_t)d * 4, s) != cudaSuccess)
+      return launch_status("colmax memset");
+    constexpr int kRowsPerBlock = 64;
+    colmax_f16_kernel<<<dim3((unsigned)ceil_div(H, 256), (unsigned)ceil_div(d, kRowsPerBlock)), 256, 0, s>>>(
+        reinterpret_cast<const __half*>(D16->down_hi), reinterpret_cast<const __half*>(D16->down_lo), D16->down_scale,
+        d, H, kRowsPerBlock, w.colmax_dn);
+    colmax_f16_kernel<<<dim3((unsigned)ceil_div(d, 256), (unsigned)ceil_div(H, kRowsPerBlock)), 256, 0, s>>>(
+        reinterpret_cast<const __half*>(D16->up_hi), reinterpret_cast<const __half*>(D16->up_lo), D16->up_scale, H, d,
+        kRowsPerBlock, w.colmax_up);
+    HFFN_TRY(launch_status("colmax_f16"));
+    transpose_f16_kernel<<<dim3((unsigned)(H / 32), (unsigned)(d / 32)), dim3(32, 8), 0, s>>>(
+        reinterpret_cast<const __half*>(D16->down_hi), reinterpret_cast<const __half*>(D16->down_lo), D16->down_scale,
+        d, H, w.colmax_dn, w.dnt_hi, w.dnt_lo, w.dnt_inv);
+    transpose_f16_kernel<<<dim3((unsigned)(d / 32), (unsigned)(H / 32)), dim3(32, 8), 0, s>>>(
+        reinterpret_cast<const __half*>(D16->up_hi), reinterpret_cast<const __half*>(D16->up_lo), D16->up_scale, H, d,
+        w.colmax_up, w.upt_hi, w.upt_lo, w.upt_inv);
+    HFFN_TRY(launch_status("transpose_f16"));
+  }
   // 1. up: z, act = gelu(z) (+ act^T)                             D[H, n] = W_up[H, d] x[n, d]^T
   EpilogueArgs e1{};
   e1.bias = L->b_up;
@@ -1652,13 +1788,37 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   e3.t_hi = w.gzt_hi;
   e3.t_lo = w.gzt_lo;
   e3.t_ld = w.t_ld;
-  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kGradHidden, kFp32Chunk, 64, 16, true, false>(
-      down_hi, down_lo, w.gy_hi, w.gy_lo, H, nn, d, e3, err, s, H, 0)));
+  if (D16 != nullptr) {
+    // gy into token packets over the x packets' workspace (read for the last time by the down GEMM)
+    __half* gy_pk = packets;
+    split_pair_f16_kernel<<<(unsigned)ceil_div(n * 32, 256), 256, 0, s>>>(w.gy_hi, w.gy_lo, n, d, gy_pk);
+    HFFN_TRY(launch_status("tc_split_pair gy"));
+    e3.row_inv = w.dnt_inv;
+    e3.tok_tab = reinterpret_cast<const float*>(gy_pk + 2 * part_halves(d));
+    e3.tok_stride = packet_halves(d) / 2;
+    HFFN_TRY((launch_gemm<false, kTrainBN, 4, kGradHidden, f16_chunk<kGradHidden>(), 64, 16, false, false, true>(
+        w.dnt_hi, w.dnt_lo, gy_pk, gy_pk + part_halves(d), H, nn, d, e3, err, s, 0, packet_halves(d))));
+  } else {
+    HFFN_TRY((launch_gemm<false, kTrainBN, 4, kGradHidden, kFp32Chunk, 64, 16, true, false>(
+        down_hi, down_lo, w.gy_hi, w.gy_lo, H, nn, d, e3, err, s, H, 0)));
+  }
   // 4. gx = W_up^T gz                                              D[d, n] = W_up^T[d, H] gz[n, H]^T
   EpilogueArgs e4{};
   e4.out_hi = gx;
-  HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDown, kFp32Chunk, 64, 8, true, false>(up_hi, up_lo, w.gz_hi, w.gz_lo, d,
-                                                                                    nn, H, e4, err, s, d, 0)));
+  if (D16 != nullptr) {
+    // gz into token packets over the act parts' workspace (read for the last time by the down GEMM)
+    __half* gz_pk = act16_hi;
+    split_pair_f16_kernel<<<(unsigned)ceil_div(n * 32, 256), 256, 0, s>>>(w.gz_hi, w.gz_lo, n, H, gz_pk);
+    HFFN_TRY(launch_status("tc_split_pair gz"));
+    e4.row_inv = w.upt_inv;
+    e4.tok_tab = reinterpret_cast<const float*>(gz_pk + 2 * part_halves(H));
+    e4.tok_stride = packet_halves(H) / 2;
+    HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDown, f16_chunk<kDown>(), 64, 8, false, false, true>(
+        w.upt_hi, w.upt_lo, gz_pk, gz_pk + part_halves(H), d, nn, H, e4, err, s, 0, packet_halves(H))));
+  } else {
+    HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDown, kFp32Chunk, 64, 8, true, false>(up_hi, up_lo, w.gz_hi, w.gz_lo, d,
+                                                                                      nn, H, e4, err, s, d, 0)));
+  }
   // 5. g_down sampled on the output-major support, AdamW, W_down refreshed   D[d, H] = gy^T[d, n] act^T[H, n]^T
   //    (both operands K-major: the feature-major copies)
   EpilogueArgs e5{};

@@ -347,7 +347,8 @@ int64_t hffn_train_step_tc_workspace(const hffn_layer* layer, int64_t n);
  * Requires d_model and d_ff multiples of 32 and, for the sampled update, the up slots of each neuron in ascending
  * input order (the output-major down edges always are). x, target, y, gx token-major [n, d_model]. The GEMMs run on
  * the 3xTF32 pairs of `dense`, except with dense16 != NULL (fp16x3 operands of the same, current values, from
- * hffn_densify_f16x3) the up GEMM and the down + MSE GEMM, which then run in the fp16x3 format at the f16 rate. */
+ * hffn_densify_f16x3) four of them run in the fp16x3 format at the f16 rate: up, down + MSE, W_down^T gy and W_up^T gz
+ * (on transposes of dense16 built by the step); the sampled weight-gradient GEMMs stay on the tf32 pairs. */
 int hffn_train_step_tc(const hffn_layer* layer, const hffn_dense* dense, const hffn_dense_f16x3* dense16,
                        const float* x, const float* target, float* y, float* gx, const hffn_train_params* params,
                        const hffn_adamw_step* adamw, float* loss, void* work, int32_t* err, int64_t n, int64_t n_total,
