@@ -1571,6 +1571,9 @@ __global__ void loss_reduce_kernel(const float* __restrict__ partial, int64_t co
 // epilogue warps: 2 column parts) and of the gelu' GEMM (16 warps: 4 column parts, its tail epilogue being the
 // heavier) are reduced in a fixed order afterwards.
 constexpr int kTrainBN = 256, kTrainPartsDown = 2, kTrainPartsUp = 4;
+// fp16x3: the up and down + MSE GEMMs run 16 epilogue warps (their epilogues, with the feature-major copies, took
+// longer than their MMAs at the f16 rate with 8): the down + MSE GEMM's partials come in 4 column parts
+constexpr int kTrainPartsDownF16 = 4;
 
 // The training step's workspace: token-major operands [n, features], their feature-major copies [features, t_ld]
 // (the K-major operands of the two weight-gradient GEMMs), the partial sums, and the support tables of both
@@ -1608,8 +1611,8 @@ static int64_t train_floats(int64_t d, int64_t H, int64_t n, TrainWork* w, float
   take(&t->gy_lo, n * d);
   take(&t->gz_hi, n * H);
   take(&t->gz_lo, n * H);
-  take(&t->loss_p, kTrainPartsDown * blocks * d);
-  take(&t->dn_p, kTrainPartsDown * blocks * d);
+  take(&t->loss_p, kTrainPartsDownF16 * blocks * d);
+  take(&t->dn_p, kTrainPartsDownF16 * blocks * d);
   take(&t->up_p, kTrainPartsUp * blocks * H);
   t->t_ld = (n + 3) / 4 * 4;
   take(&t->xt_hi, d * t->t_ld);
@@ -1680,7 +1683,7 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   TrainWork w;
   train_floats(d, H, n, &w, reinterpret_cast<float*>(work));
   const int blocks = (int)((n + kTrainBN - 1) / kTrainBN);
-  const int rows_dn = kTrainPartsDown * blocks, rows_up = kTrainPartsUp * blocks;
+  const int rows_dn = (D16 != nullptr ? kTrainPartsDownF16 : kTrainPartsDown) * blocks, rows_up = kTrainPartsUp * blocks;
   const int adam = opt != nullptr;
   const hffn_adamw_step st = opt ? *opt : hffn_adamw_step{};
   float* dense_up_hi = const_cast<float*>(reinterpret_cast<const float*>(up_hi));
@@ -1750,7 +1753,7 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
     e1.row_inv = D16->up_scale;
     e1.tok_tab = reinterpret_cast<const float*>(packets + 2 * part_halves(d));
     e1.tok_stride = packet_halves(d) / 2;
-    HFFN_TRY((launch_gemm<false, kTrainBN, 4, kUpT, f16_chunk<kUpT>(), 64, 8, false, false, true>(
+    HFFN_TRY((launch_gemm<false, kTrainBN, 4, kUpT, f16_chunk<kUpT>(), 64, 16, false, false, true>(
         D16->up_hi, D16->up_lo, packets, packets + part_halves(d), H, nn, d, e1, err, s, 0, packet_halves(d))));
   } else {
     HFFN_TRY((launch_gemm<false, kTrainBN, 4, kUpT, kFp32Chunk, 64, 8>(up_hi, up_lo, w.x_hi, w.x_lo, H, nn, d, e1, err,
@@ -1773,7 +1776,7 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
     e2.row_inv = D16->down_scale;
     e2.tok_tab = reinterpret_cast<const float*>(packets + 2 * part_halves(d));
     e2.tok_stride = packet_halves(d) / 2;
-    HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDownMse, f16_chunk<kDownMse>(), 64, 8, false, false, true>(
+    HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDownMse, f16_chunk<kDownMse>(), 64, 16, false, false, true>(
         D16->down_hi, D16->down_lo, act16_hi, act16_lo, d, nn, H, e2, err, s)));
   } else {
     HFFN_TRY((launch_gemm<false, kTrainBN, 4, kDownMse, kFp32Chunk, 64, 8>(down_hi, down_lo, w.act_hi, w.act_lo, d,
