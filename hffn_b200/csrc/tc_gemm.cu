@@ -491,6 +491,7 @@ __device__ __noinline__ void sampled_entry(const EpilogueArgs* e, int q, int64_t
   e->v[q] = vi;
   p -= st.step_size * mi / (sqrtf(vi) / st.bias2_sqrt + st.eps);
   e->value[q] = p;
+  if (e->dense_hi == nullptr) return;    // the fp16x3 step: the tf32 pairs are rebuilt from the values when next needed
   const float hi = tf32_rna(p);
   e->dense_hi[dense_at] = hi;
   e->dense_lo[dense_at] = tf32_rna(p - hi);
@@ -1673,7 +1674,9 @@ int64_t tc_train_workspace(const hffn_layer* L, int64_t n) {
 // the current values) and the token packets of x (in the workspace of x's tf32 parts), their act operand the fp16 hi /
 // lo pair (in the workspace of act's tf32 pairs); W_down^T gy and W_up^T gz on the transposes of D16 (built here) and
 // the token packets of gy and gz (over the x and act workspaces, dead by then). The two sampled weight-gradient GEMMs
-// and the dense refresh stay on the tf32 pairs.
+// stay on the tf32 copies (bound by their AdamW epilogue, measured: in fp16x3 the packing of their operands cost more
+// than their MMAs saved), and the dense tf32 pairs, which this step then does not read, are not refreshed (the caller
+// rebuilds them when it next needs them).
 int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, const void* down_hi, const void* down_lo,
                   const hffn_dense_f16x3* D16, const float* x, const float* target, float* y, float* gx,
                   const hffn_train_params* P, const hffn_adamw_step* opt, float* loss, void* work, int* err, int64_t n,
@@ -1832,8 +1835,8 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   e5.grad = P->out_val.grad;
   e5.m = P->out_val.m;
   e5.v = P->out_val.v;
-  e5.dense_hi = dense_dn_hi;
-  e5.dense_lo = dense_dn_lo;
+  e5.dense_hi = D16 != nullptr ? nullptr : dense_dn_hi;    // the fp16x3 step reads no tf32 pair: no refresh
+  e5.dense_lo = D16 != nullptr ? nullptr : dense_dn_lo;
   e5.adam = adam;
   e5.step = st;
   HFFN_TRY((launch_gemm<false, kTrainBN, 4, kSampled, kFp32Chunk, 64, 8, false, false>(
@@ -1847,8 +1850,8 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   e6.grad = P->up_val.grad;
   e6.m = P->up_val.m;
   e6.v = P->up_val.v;
-  e6.dense_hi = dense_up_hi;
-  e6.dense_lo = dense_up_lo;
+  e6.dense_hi = D16 != nullptr ? nullptr : dense_up_hi;
+  e6.dense_lo = D16 != nullptr ? nullptr : dense_up_lo;
   e6.adam = adam;
   e6.step = st;
   HFFN_TRY((launch_gemm<false, kTrainBN, 4, kSampled, kFp32Chunk, 64, 8, false, false>(

@@ -310,8 +310,8 @@ class HFFNTrainRuntime:
                                                self._tc_work.data_ptr(), runtime._err.data_ptr(), n, n_total or n,
                                                native.stream_handle(runtime.device))
         native.check(status, "hffn_train_step_tc")
-        if apply:                 # the step refreshed the tf32 pairs in place; the forward's fp16x3 operands are stale
-            runtime.mark_updated(index, refreshed="tf32x3")
+        if apply:                 # the 3xTF32 step refreshed the tf32 pairs in place; the fp16x3 step refreshes none
+            runtime.mark_updated(index, refreshed=None if dense16 is not None else "tf32x3")
         self._saved = None
         runtime.calls[TC, TC] += 1
         self.calls[TC, TC] += 1

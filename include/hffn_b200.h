@@ -348,7 +348,9 @@ int64_t hffn_train_step_tc_workspace(const hffn_layer* layer, int64_t n);
  * input order (the output-major down edges always are). x, target, y, gx token-major [n, d_model]. The GEMMs run on
  * the 3xTF32 pairs of `dense`, except with dense16 != NULL (fp16x3 operands of the same, current values, from
  * hffn_densify_f16x3) four of them run in the fp16x3 format at the f16 rate: up, down + MSE, W_down^T gy and W_up^T gz
- * (on transposes of dense16 built by the step); the sampled weight-gradient GEMMs stay on the tf32 pairs. */
+ * (on transposes of dense16 built by the step); the sampled weight-gradient GEMMs stay on tf32 copies of the
+ * activations and gradients, and the dense tf32 pairs are then NOT refreshed (rebuild them with hffn_densify before
+ * using them again; dense16 must be rebuilt after every applied step in any case). */
 int hffn_train_step_tc(const hffn_layer* layer, const hffn_dense* dense, const hffn_dense_f16x3* dense16,
                        const float* x, const float* target, float* y, float* gx, const hffn_train_params* params,
                        const hffn_adamw_step* adamw, float* loss, void* work, int32_t* err, int64_t n, int64_t n_total,

@@ -4,7 +4,8 @@ Against the float64 oracle on the reference's test layers: y, gx and the four co
 group's scale, the loss within 1e-5 relative, AdamW against its float64 closed form on the conditioned entries
 (relative 1e-5, the reference's gate 3), the same bits twice from the same state. At the training benchmark's layer
 shape, where the oracle is too slow, the step is checked against the CUDA-core step (itself checked against the
-oracle at that shape). The dense operands stay equal to a fresh densification of the updated compact values."""
+oracle at that shape). 3xTF32: the dense tf32 pairs stay equal to a fresh densification of the updated compact values;
+fp16x3: the step leaves the dense operands to be rebuilt, and the next forward sees the updated values."""
 import numpy as np
 import pytest
 import torch
@@ -23,10 +24,10 @@ def kernel_layer(layer):
                                        t(layer.down_val))
 
 
-def make_train(layer, n, tensor_cores):
+def make_train(layer, n, tensor_cores, tc_format=None):
     from hffn_b200.runtime import HFFNRuntime
     from hffn_b200.train_runtime import HFFNTrainRuntime
-    runtime = HFFNRuntime([kernel_layer(layer)], "cuda", tensor_cores=True)
+    runtime = HFFNRuntime([kernel_layer(layer)], "cuda", tensor_cores=True, tc_format=tc_format)
     return HFFNTrainRuntime(runtime, **train64.HYPER, max_tokens=n, tensor_cores=tensor_cores)
 
 
@@ -63,7 +64,12 @@ def test_against_oracle(name, n):
             assert np.max((np.abs(after[p_name] - p1) / np.maximum(scale, 1e-30))[mask]) <= 1e-5, p_name
 
 
-def test_repeatable_and_dense_consistent():
+@pytest.mark.parametrize("tc_format", ["tf32x3", "f16x3"])
+def test_repeatable_and_dense_consistent(tc_format):
+    """Three steps, twice from the same state: the same bits. 3xTF32: the dense tf32 pairs refreshed in place by the
+    update equal a rebuild from the compact values. fp16x3: the step refreshes no dense operand and leaves both formats
+    marked for a rebuild, and the next forward (fp16x3 operands rebuilt from the updated values) equals the CUDA-core
+    forward of the same values."""
     case = synth.TEST_CASES["irreg_512_2048"]
     layer = synth.make_layer(case)
     n = 300
@@ -71,14 +77,24 @@ def test_repeatable_and_dense_consistent():
     target = torch.from_numpy(synth.make_target(case, n)).cuda()
     states = []
     for _ in range(2):
-        train = make_train(layer, n, tensor_cores=True)
+        train = make_train(layer, n, tensor_cores=True, tc_format=tc_format)
         for _ in range(3):
             train.step_mse(0, x, target)
         states.append({k: v.clone() for k, v in train.parameters(0).items()})
-        dense = {k: v.clone() for k, v in train.runtime._dense[0].items()}
-        train.runtime._densify(0)
-        for k, v in train.runtime._dense[0].items():
-            assert torch.equal(v, dense[k]), k          # refreshed in place = rebuilt from the compact values
+        runtime = train.runtime
+        if tc_format == "tf32x3":
+            dense = {k: v.clone() for k, v in runtime._dense[0].items()}
+            runtime._densify(0)
+            for k, v in runtime._dense[0].items():
+                assert torch.equal(v, dense[k]), k      # refreshed in place = rebuilt from the compact values
+        else:
+            assert runtime._dense_stale[0] and runtime._dense16_stale[0]
+            runtime.force("tc", "tc")
+            y_tc = runtime.forward(0, x).clone()
+            runtime.force("tile", "blocked")
+            y_cc = runtime.forward(0, x).clone()
+            runtime.force(None, None)
+            assert float((y_tc - y_cc).abs().max()) <= 2e-5
     for k in states[0]:
         assert torch.equal(states[0][k], states[1][k]), k
 
