@@ -477,24 +477,48 @@ __device__ __forceinline__ void emit_row_f16(const EpilogueArgs* e, const float*
   }
 }
 
-// One support entry q of row `row`, column `col`, gradient g: stored and / or applied by AdamW (PyTorch's fused order),
-// and the dense operand [row, col] refreshed with the new value as tf32 hi / lo.
-__device__ __noinline__ void sampled_entry(const EpilogueArgs* e, int q, int64_t dense_at, float g) {
-  if (e->grad) e->grad[q] = g;
+// The support entries of one row among four consecutive columns (nib: which are on the support; q: the compact index of
+// the first of them; g0 .. g3: the gradients of the four columns): each gradient stored and / or applied by AdamW
+// (PyTorch's fused order) and, with dense_hi != NULL, the dense operand's entry refreshed with the new value as tf32
+// hi / lo. The loads of all four are issued before their arithmetic: a thread walks its own row, so its loads do not
+// coalesce with its warp's, and four independent ones in flight hide more of their latency than one (measured).
+__device__ __noinline__ void sampled_entries4(const EpilogueArgs* e, int q, uint32_t nib, int64_t dense_at, float g0,
+                                              float g1, float g2, float g3) {
+  const float g[4] = {g0, g1, g2, g3};
+  int qs[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) qs[j] = q + __popc(nib & ((1u << j) - 1u));
+  if (e->grad)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if ((nib >> j) & 1u) e->grad[qs[j]] = g[j];
   if (!e->adam) return;
   const hffn_adamw_step& st = e->step;
-  float p = e->value[q];
-  p -= st.lr_decay * p;
-  const float mi = st.beta1 * e->m[q] + st.one_minus_beta1 * g;
-  const float vi = st.beta2 * e->v[q] + st.one_minus_beta2 * g * g;
-  e->m[q] = mi;
-  e->v[q] = vi;
-  p -= st.step_size * mi / (sqrtf(vi) / st.bias2_sqrt + st.eps);
-  e->value[q] = p;
-  if (e->dense_hi == nullptr) return;    // the fp16x3 step: the tf32 pairs are rebuilt from the values when next needed
-  const float hi = tf32_rna(p);
-  e->dense_hi[dense_at] = hi;
-  e->dense_lo[dense_at] = tf32_rna(p - hi);
+  float p[4] = {0.f, 0.f, 0.f, 0.f}, m[4] = {0.f, 0.f, 0.f, 0.f}, v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if ((nib >> j) & 1u) {
+      p[j] = e->value[qs[j]];
+      m[j] = e->m[qs[j]];
+      v[j] = e->v[qs[j]];
+    }
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if ((nib >> j) & 1u) {
+      float pj = p[j];
+      pj -= st.lr_decay * pj;
+      const float mi = st.beta1 * m[j] + st.one_minus_beta1 * g[j];
+      const float vi = st.beta2 * v[j] + st.one_minus_beta2 * g[j] * g[j];
+      e->m[qs[j]] = mi;
+      e->v[qs[j]] = vi;
+      pj -= st.step_size * mi / (sqrtf(vi) / st.bias2_sqrt + st.eps);
+      e->value[qs[j]] = pj;
+      if (e->dense_hi != nullptr) {
+        const float hi = tf32_rna(pj);
+        e->dense_hi[dense_at + j] = hi;
+        e->dense_lo[dense_at + j] = tf32_rna(pj - hi);
+      }
+    }
 }
 
 // Shared memory: [stages][A parts][128 rows x RB bytes] then [stages][B parts][BN rows x RB bytes], 1024-aligned, the
@@ -784,10 +808,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a_hi, const __grid_consta
             int q = e->first[word0];
             const int64_t dense_row = (int64_t)row * N;
 #pragma unroll
-            for (int i = 0; i < HALF; ++i) {
-              if ((bits[i >> 5] >> (i & 31)) & 1u) {
-                sampled_entry(e, q, dense_row + n0 + i, sum[i]);
-                ++q;
+            for (int g4 = 0; g4 < HALF / 4; ++g4) {
+              const uint32_t nib = (bits[g4 >> 3] >> ((g4 & 7) * 4)) & 0xFu;
+              if (nib) {
+                sampled_entries4(e, q, nib, dense_row + n0 + 4 * g4, sum[4 * g4], sum[4 * g4 + 1], sum[4 * g4 + 2],
+                                 sum[4 * g4 + 3]);
+                q += __popc(nib);
               }
             }
           }
