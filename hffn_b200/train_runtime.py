@@ -297,11 +297,13 @@ class HFFNTrainRuntime:
         if self._check_tokens(target, "target") != n:
             raise ValueError("target must have the N of x")
         self._reserve_tc(n)
-        if runtime._dense_stale[index]:
+        # fp16x3 runtimes: four of the step's GEMMs run on the fp16x3 operands (rebuilt from the current values when
+        # stale, as after every applied step) and its transposes, and the step reads no tf32 pair: those are built
+        # once (the entry takes their addresses) and otherwise left stale for whoever needs them next
+        f16 = runtime.tc_format == "f16x3"
+        if runtime._dense_stale[index] and not (f16 and runtime._dense[index] is not None):
             runtime._densify(index)
-        # fp16x3 runtimes: the step's up and down + MSE GEMMs run on the fp16x3 operands (rebuilt from the current
-        # values when stale, as after every applied step), the other four on the tf32 pairs
-        dense16 = runtime.forward_operands(index)[1] if runtime.tc_format == "f16x3" else None
+        dense16 = runtime.forward_operands(index)[1] if f16 else None
         params = self._fused_structs[index] if apply else self._param_structs[index]
         status = native.lib.hffn_train_step_tc(runtime._structs[index], runtime._dense_structs[index], dense16,
                                                x.data_ptr(),
