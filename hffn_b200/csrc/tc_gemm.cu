@@ -1581,15 +1581,29 @@ __global__ void bias_reduce_kernel(const float* __restrict__ partial, int rows, 
   p.value[i] = v - st.step_size * mi / (sqrtf(vi) / st.bias2_sqrt + st.eps);
 }
 
-__global__ void loss_reduce_kernel(const float* __restrict__ partial, int64_t count, double inv, float* loss) {
+// The loss in two fixed-order levels (the same bits whatever the launch timing): block b sums its contiguous chunk of
+// the partials (each thread a strided share, then the threads' sums in thread order) into block_sums[b]; one block then
+// sums the block sums in block order. One block over all the partials took 112 us at C3 (262 k partials).
+constexpr int kLossBlocks = 148;
+__global__ void loss_blocks_kernel(const float* __restrict__ partial, int64_t count, double* __restrict__ block_sums) {
   __shared__ double red[256];
+  const int64_t chunk = (count + gridDim.x - 1) / gridDim.x;
+  const int64_t begin = (int64_t)blockIdx.x * chunk, end = begin + chunk < count ? begin + chunk : count;
   double acc = 0.0;
-  for (int64_t i = threadIdx.x; i < count; i += blockDim.x) acc += partial[i];
+  for (int64_t i = begin + threadIdx.x; i < end; i += blockDim.x) acc += partial[i];
   red[threadIdx.x] = acc;
   __syncthreads();
   if (threadIdx.x == 0) {
     double sum = 0.0;
     for (int k = 0; k < (int)blockDim.x; ++k) sum += red[k];
+    block_sums[blockIdx.x] = sum;
+  }
+}
+
+__global__ void loss_reduce_kernel(const double* __restrict__ block_sums, int blocks, double inv, float* loss) {
+  if (threadIdx.x == 0) {
+    double sum = 0.0;
+    for (int k = 0; k < blocks; ++k) sum += block_sums[k];
     *loss = (float)(sum * inv);
   }
 }
@@ -1606,7 +1620,7 @@ constexpr int kTrainPartsDownF16 = 4;
 // (the K-major operands of the two weight-gradient GEMMs), the partial sums, and the support tables of both
 // supports (bitmask words and first indices, mask_ld words per row: whole 256-column tiles).
 struct TrainWork {
-  float *x_hi, *x_lo, *z, *act_hi, *act_lo, *gy_hi, *gy_lo, *gz_hi, *gz_lo, *loss_p, *dn_p, *up_p;
+  float *x_hi, *x_lo, *z, *act_hi, *act_lo, *gy_hi, *gy_lo, *gz_hi, *gz_lo, *loss_p, *dn_p, *up_p, *loss_blocks;
   float *xt_hi, *xt_lo, *actt_hi, *actt_lo, *gyt_hi, *gyt_lo, *gzt_hi, *gzt_lo;
   uint32_t *dn_mask, *up_mask;
   int32_t *dn_first, *up_first;
@@ -1641,6 +1655,7 @@ static int64_t train_floats(int64_t d, int64_t H, int64_t n, TrainWork* w, float
   take(&t->loss_p, kTrainPartsDownF16 * blocks * d);
   take(&t->dn_p, kTrainPartsDownF16 * blocks * d);
   take(&t->up_p, kTrainPartsUp * blocks * H);
+  take(&t->loss_blocks, 2 * kLossBlocks);                      // doubles
   t->t_ld = (n + 3) / 4 * 4;
   take(&t->xt_hi, d * t->t_ld);
   take(&t->xt_lo, d * t->t_ld);
@@ -1887,7 +1902,11 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
   HFFN_TRY(launch_status("bias_reduce down"));
   bias_reduce_kernel<<<(H + 255) / 256, 256, 0, s>>>(w.up_p, rows_up, H, P->b_up, adam, st);
   HFFN_TRY(launch_status("bias_reduce up"));
-  loss_reduce_kernel<<<1, 256, 0, s>>>(w.loss_p, (int64_t)rows_dn * d, 1.0 / ((double)n * d), loss);
+  loss_blocks_kernel<<<kLossBlocks, 256, 0, s>>>(w.loss_p, (int64_t)rows_dn * d,
+                                                 reinterpret_cast<double*>(w.loss_blocks));
+  HFFN_TRY(launch_status("loss_blocks"));
+  loss_reduce_kernel<<<1, 32, 0, s>>>(reinterpret_cast<const double*>(w.loss_blocks), kLossBlocks,
+                                      1.0 / ((double)n * d), loss);
   return launch_status("loss_reduce");
 }
 
