@@ -2,10 +2,13 @@
 ``runtime/gpu/nvidia/common/kernels/hffn_cuda/runtime.py`` (``HFFNLayer``, ``HFFNRuntime``, ``up_mode``, ``down_mode``,
 ``UP_MODES``, ``DOWN_MODES``, ``MAX_TOKENS``).
 
-One call runs the whole block of N tokens of one FFN through ``hffn_forward`` of ``libhffn_b200.so``: the fused
-up + bias + GELU kernel, then the down kernel, on the caller's current CUDA stream (any ``cuda:i``, any stream; the
-reference accepts only cuda:0 and the default stream, ``runtime.py:79-82``). Model arrays are compact and stay on
-the device; the work buffers (``act`` hidden-major ``[d_ff, N]`` and ``y``) are shared by all layers, sized for the
+One call runs the whole block of N tokens of one FFN through ``libhffn_b200.so``: the fused up + bias + GELU kernel,
+then the down kernel, on the caller's current CUDA stream (any ``cuda:i``, any stream; the reference accepts only
+cuda:0 and the default stream, ``runtime.py:79-82``). The policy (``modes``): the decode kernels for N <= 8; from 9
+tokens the tcgen05 GEMMs over the densified supports (float32 in the fp16x3 operand format unless ``tc_format`` says
+otherwise), when d_model and d_ff are multiples of 8; the CUDA-core kernels otherwise or when forced. Model arrays are
+compact and stay on the device (the dense tensor-core operands are built from them on first use); the work buffers
+(``act`` hidden-major ``[d_ff, N]``, the tensor-core workspace and ``y``) are shared by all layers, sized for the
 largest N seen and reused. The output is a view of the runtime's buffer, overwritten by the next call, as in the
 reference (``runtime.py:118-121``). Storage is float32 (the reference's only type) or bfloat16 (``dtype=``); the
 kernels accumulate in float32 in both.
@@ -142,7 +145,7 @@ class HFFNRuntime:
         self._structs = [layer_struct(t, self.d_model, self.d_ff) for t in self._tensors]
         # Tensor-core operands: the supports densified (W_up [d_ff, d_model], W_down [d_model, d_ff], zeros off the
         # support), built on first use and rebuilt after the compact values change. Two formats: ``_dense`` (bfloat16;
-        # float32 as tf32 hi / lo pairs, the operands of the tensor-core training step and of the peer pipeline) and
+        # float32 as tf32 hi / lo pairs, the operands of the 3xTF32 training step and of the peer pipeline) and
         # ``_dense16`` (float32 as scaled fp16 hi / lo pairs, the fp16x3 format of the float32 forward, the default;
         # ``tc_format="tf32x3"`` runs the float32 forward on the tf32 pairs instead).
         compatible = self.d_model % 8 == 0 and self.d_ff % 8 == 0
@@ -276,7 +279,7 @@ class HFFNRuntime:
 
     def mark_updated(self, index: int, refreshed: str | None = None) -> None:
         """The compact values of layer ``index`` changed (an optimiser step): the dense operands are rebuilt lazily,
-        except those of format ``refreshed`` (``"tf32x3"``: the tensor-core training step refreshed them in place)."""
+        except those of format ``refreshed`` (``"tf32x3"``: the 3xTF32 training step refreshed them in place)."""
         if self.tensor_cores:
             if refreshed != "tf32x3":
                 self._dense_stale[index] = True
