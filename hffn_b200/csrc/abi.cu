@@ -41,7 +41,7 @@ int tc_train_step(const hffn_layer* L, const void* up_hi, const void* up_lo, con
                   const hffn_adamw_step* opt, float* loss, void* work, int* err, int64_t n, int64_t n_total,
                   cudaStream_t s);
 int tc_down(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo, const void* b,
-            void* y, int* err, int d, int H, int64_t n, cudaStream_t s);
+            void* y, int* err, int d, int H, int64_t n, cudaStream_t s, bool pdl = false);
 int tc_densify(int dtype, const int32_t* off, const int16_t* idx, const void* val, int rows, int cols, void* hi,
                void* lo, cudaStream_t s);
 int64_t tc_f16_workspace(int d, int H, int64_t n);

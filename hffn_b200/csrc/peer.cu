@@ -25,7 +25,7 @@ namespace hffn {
 int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const void* b, void* act_hi, void* act_lo,
           float* z, void* x_split, int* err, int d, int H, int64_t n, cudaStream_t s);
 int tc_down(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo, const void* b,
-            void* y, int* err, int d, int H, int64_t n, cudaStream_t s);
+            void* y, int* err, int d, int H, int64_t n, cudaStream_t s, bool pdl = false);
 int tc_down_peer(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo, const void* b,
                  void* const* peers, int world, int64_t tokens_per_owner, int* err, int d, int H, int64_t n,
                  cudaStream_t s);

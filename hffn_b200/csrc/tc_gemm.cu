@@ -1354,9 +1354,11 @@ constexpr int kFp32Chunk = 8;
 
 // One forward GEMM at the tile width pick_tile_tokens gives (float32: 64-byte rows; bfloat16: 128-byte rows; 8
 // epilogue warps at width 64, where 16 would split 64 columns too finely).
+// pdl: programmatic dependent launch, for a GEMM whose predecessor in the stream is the GEMM that wrote its operand (the
+// down GEMM after the up GEMM of the same forward).
 template <bool kBf16, int EPI>
 static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b_hi, const void* b_lo, int M, int N,
-                               int K, const EpilogueArgs& epi, int* err, cudaStream_t s) {
+                               int K, const EpilogueArgs& epi, int* err, cudaStream_t s, bool pdl = false) {
   constexpr int kChunk = kBf16 ? 0 : kFp32Chunk;
   constexpr int kRow = kBf16 ? 128 : 64;
   // float32 up: 16 warps (its tail epilogue, GELU and the tf32 split of 128 x 256 values, would otherwise stall the
@@ -1364,11 +1366,13 @@ static int launch_forward_gemm(const void* a_hi, const void* a_lo, const void* b
   constexpr int kWarps = kBf16 || EPI == kUp ? 16 : 8;
   switch (pick_tile_tokens(M, N)) {
     case 64:
-      return launch_gemm<kBf16, 64, 6, EPI, kChunk, kRow, 8>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi, err, s);
+      return launch_gemm<kBf16, 64, 6, EPI, kChunk, kRow, 8>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi, err, s, 0, 0, pdl);
     case 128:
-      return launch_gemm<kBf16, 128, 5, EPI, kChunk, kRow, kWarps>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi, err, s);
+      return launch_gemm<kBf16, 128, 5, EPI, kChunk, kRow, kWarps>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi, err, s, 0, 0,
+                                                                   pdl);
     default:
-      return launch_gemm<kBf16, 256, 4, EPI, kChunk, kRow, kWarps>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi, err, s);
+      return launch_gemm<kBf16, 256, 4, EPI, kChunk, kRow, kWarps>(a_hi, a_lo, b_hi, b_lo, M, N, K, epi, err, s, 0, 0,
+                                                                   pdl);
   }
 }
 
@@ -1530,15 +1534,16 @@ int tc_up(int dtype, const void* x, const void* w_hi, const void* w_lo, const vo
 }
 
 // down: act [n, H] token-major -> y [n, d].
+// pdl: the caller's previous launch on s is the up GEMM that wrote act (tc_forward).
 int tc_down(int dtype, const void* act_hi, const void* act_lo, const void* w_hi, const void* w_lo, const void* b,
-            void* y, int* err, int d, int H, int64_t n, cudaStream_t s) {
+            void* y, int* err, int d, int H, int64_t n, cudaStream_t s, bool pdl) {
   const int nn = (int)n;
   tc::EpilogueArgs dn{};
   dn.bias = b;
   dn.out_hi = y;
   if (dtype == HFFN_BF16)
-    return tc::launch_forward_gemm<true, tc::kDown>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s);
-  return tc::launch_forward_gemm<false, tc::kDown>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err, s);
+    return tc::launch_forward_gemm<true, tc::kDown>(w_hi, nullptr, act_hi, nullptr, d, nn, H, dn, err, s, pdl);
+  return tc::launch_forward_gemm<false, tc::kDown>(w_hi, w_lo, act_hi, act_lo, d, nn, H, dn, err, s, pdl);
 }
 
 // Workspace of the whole forward: fp32 [x_hi, x_lo (n d each), act_hi, act_lo (n H each)] floats; bf16 act [n, H].
@@ -1548,13 +1553,13 @@ int tc_forward(int dtype, const hffn_layer* L, const void* up_hi, const void* up
   const int d = L->d_model, H = L->d_ff;
   if (dtype == HFFN_BF16) {
     HFFN_TRY(tc_up(dtype, x, up_hi, nullptr, L->b_up, work, nullptr, nullptr, nullptr, err, d, H, n, s));
-    return tc_down(dtype, work, nullptr, down_hi, nullptr, L->b_down, y, err, d, H, n, s);
+    return tc_down(dtype, work, nullptr, down_hi, nullptr, L->b_down, y, err, d, H, n, s, true);
   }
   float* x_split = reinterpret_cast<float*>(work);
   float* act_hi = x_split + 2 * n * d;
   float* act_lo = act_hi + n * H;
   HFFN_TRY(tc_up(dtype, x, up_hi, up_lo, L->b_up, act_hi, act_lo, z, x_split, err, d, H, n, s));
-  return tc_down(dtype, act_hi, act_lo, down_hi, down_lo, L->b_down, y, err, d, H, n, s);
+  return tc_down(dtype, act_hi, act_lo, down_hi, down_lo, L->b_down, y, err, d, H, n, s, true);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
